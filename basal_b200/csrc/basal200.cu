@@ -1,0 +1,505 @@
+// libbasal200: host side of the C ABI declared in include/basal200.h, and the one translation unit that holds every
+// kernel of the library (the device fault word is shared by all of them).
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "block_gemm.cuh"
+#include "nvfp4_gemm.cuh"
+#include "quant.cuh"
+#include "readout.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int checked = 0;  // 1: sm_100, -1: another architecture
+  int sms = 0;
+  unsigned smem_set = 0;  // kernels whose dynamic shared memory limit was raised on this device
+};
+DeviceInfo g_dev[kMaxDevices];
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= kMaxDevices) return BASAL200_ERR_LAUNCH;
+  DeviceInfo& d = g_dev[*dev];
+  if (!d.checked) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, *dev);
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, *dev);
+    d.checked = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  return d.checked == 1 ? BASAL200_OK : BASAL200_ERR_ARCH;
+}
+
+// Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
+template <typename K>
+int set_smem(int dev, int slot, K kernel, size_t bytes) {
+  DeviceInfo& d = g_dev[dev];
+  if (d.smem_set & (1u << slot)) return BASAL200_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return BASAL200_ERR_LAUNCH;
+  d.smem_set |= 1u << slot;
+  return BASAL200_OK;
+}
+
+int launched() {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "libbasal200: launch failed: %s\n", cudaGetErrorString(e));
+    return BASAL200_ERR_LAUNCH;
+  }
+  return BASAL200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+// A 2-D byte matrix [outer, inner] with rows `row_bytes` apart, read in boxes of [box_outer, box_inner] bytes with
+// the 128-byte swizzle; out-of-range elements read as zero.
+int tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+            uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiled fn = encode_fn();
+  if (!fn) return BASAL200_ERR_TMAP;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BASAL200_OK : BASAL200_ERR_TMAP;
+}
+
+int grid_for(int dev, int64_t work_items, int per_block) {
+  const int64_t want = (work_items + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)g_dev[dev].sms * 16;
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// quantisers
+// ------------------------------------------------------------------------------------------------------------
+template <bool INT8>
+int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cudaStream_t st) {
+  if (M < 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (K % 128) return BASAL200_ERR_SHAPE;
+  if (M == 0) return BASAL200_OK;
+  if (!x || !q || !s) return BASAL200_ERR_ARG;
+  if (!aligned16(x) || !aligned16(q) || !aligned16(s)) return BASAL200_ERR_ALIGN;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t groups = M * (K / 128);
+  const int grid = grid_for(dev, groups, 16);  // 8 warps a CTA, 2 groups a warp
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  switch (xt) {
+    case BASAL200_BF16:
+      act_quant_block_kernel<__nv_bfloat16, INT8><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(x), groups, (int)(K / 128), K, qb, s);
+      break;
+    case BASAL200_F16:
+      act_quant_block_kernel<__half, INT8><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), groups,
+                                                                  (int)(K / 128), K, qb, s);
+      break;
+    case BASAL200_F32:
+      act_quant_block_kernel<float, INT8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), groups,
+                                                                 (int)(K / 128), K, qb, s);
+      break;
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+  return launched();
+}
+
+template <bool INT8>
+int weight_quant(const void* w, int wt, int64_t N, int64_t K, void* q, float* s, cudaStream_t st) {
+  if (N <= 0 || K <= 0 || !w || !q || !s) return BASAL200_ERR_ARG;
+  if (N % 128 || K % 128) return BASAL200_ERR_SHAPE;
+  if (!aligned16(w) || !aligned16(q)) return BASAL200_ERR_ALIGN;
+  if (N / 128 > 65535) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const dim3 grid((unsigned)(K / 128), (unsigned)(N / 128));
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  switch (wt) {
+    case BASAL200_BF16:
+      weight_quant_block_kernel<__nv_bfloat16, INT8><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), K,
+                                                                           qb, s);
+      break;
+    case BASAL200_F16:
+      weight_quant_block_kernel<__half, INT8><<<grid, 256, 0, st>>>(static_cast<const __half*>(w), K, qb, s);
+      break;
+    case BASAL200_F32:
+      weight_quant_block_kernel<float, INT8><<<grid, 256, 0, st>>>(static_cast<const float*>(w), K, qb, s);
+      break;
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+  return launched();
+}
+
+int nvfp4_act(const void* x, int xt, const float* inv_g, int64_t M, int64_t K, uint8_t* q, uint8_t* s,
+              cudaStream_t st) {
+  if (M < 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (K % 64) return BASAL200_ERR_SHAPE;
+  if (M == 0) return BASAL200_OK;
+  if (!x || !inv_g || !q || !s) return BASAL200_ERR_ARG;
+  if (!aligned16(x) || !aligned16(q) || !aligned16(s)) return BASAL200_ERR_ALIGN;
+  const int64_t Mp = (M + 127) / 128 * 128;
+  if (Mp / 128 > 65535 || K / 64 > 65535) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const dim3 grid((unsigned)(K / 64), (unsigned)(Mp / 128));
+  switch (xt) {
+    case BASAL200_BF16:
+      nvfp4_act_quant_kernel<__nv_bfloat16><<<grid, 512, 0, st>>>(static_cast<const __nv_bfloat16*>(x), inv_g, M,
+                                                                  K, q, s);
+      break;
+    case BASAL200_F16:
+      nvfp4_act_quant_kernel<__half><<<grid, 512, 0, st>>>(static_cast<const __half*>(x), inv_g, M, K, q, s);
+      break;
+    case BASAL200_F32:
+      nvfp4_act_quant_kernel<float><<<grid, 512, 0, st>>>(static_cast<const float*>(x), inv_g, M, K, q, s);
+      break;
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+  return launched();
+}
+
+template <typename T>
+int nvfp4_wq_typed(const T* w, int64_t N, int64_t K, uint8_t* codes, uint8_t* scales, float* g, int dev,
+                   cudaStream_t st) {
+  if (cudaMemsetAsync(g, 0, sizeof(float), st) != cudaSuccess) return BASAL200_ERR_LAUNCH;
+  const int64_t n8 = N * K / 8;
+  absmax_kernel<T><<<grid_for(dev, n8, 256), 256, 0, st>>>(w, n8, reinterpret_cast<unsigned*>(g));
+  const int64_t Np = (N + 127) / 128 * 128, c4 = (K / 16 + 3) / 4;
+  const int64_t blocks16 = Np * c4 * 4;
+  if ((blocks16 + 255) / 256 > INT32_MAX) return BASAL200_ERR_LIMIT;
+  nvfp4_weight_quant_kernel<T><<<(unsigned)((blocks16 + 255) / 256), 256, 0, st>>>(w, g, N, Np, K, c4, codes, scales);
+  nvfp4_global_scale_kernel<<<1, 1, 0, st>>>(g);
+  return launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// GEMMs
+// ------------------------------------------------------------------------------------------------------------
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8 };
+
+template <bool INT8, int OUT>
+int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::Params& p,
+                      cudaStream_t st) {
+  auto kern = blockgemm::block_gemm_kernel<INT8, OUT>;
+  int rc = set_smem(dev, kSlotBlock + (INT8 ? 3 : 0) + OUT, kern, blockgemm::SMEM_BYTES);
+  if (rc) return rc;
+  const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
+  kern<<<grid, blockgemm::NUM_THREADS, blockgemm::SMEM_BYTES, st>>>(ta, tb, p);
+  return launched();
+}
+
+template <bool INT8>
+int block_gemm(const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c, int ct,
+               int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (M < 0 || N <= 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (N % 128 || K % 128) return BASAL200_ERR_SHAPE;
+  if (M == 0) return BASAL200_OK;
+  if (!q || !s || !w || !ws || !c) return BASAL200_ERR_ARG;
+  if (!aligned16(q) || !aligned16(w) || !aligned16(c) || (bias && !aligned16(bias))) return BASAL200_ERR_ALIGN;
+  if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;
+  blockgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = bias;
+  p.c = c;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nkb = (int)(K / 128);
+  p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
+  const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  switch (ct) {
+    case BASAL200_BF16: return block_gemm_launch<INT8, BASAL200_BF16>(dev, ta, tb, p, st);
+    case BASAL200_F16: return block_gemm_launch<INT8, BASAL200_F16>(dev, ta, tb, p, st);
+    case BASAL200_F32: return block_gemm_launch<INT8, BASAL200_F32>(dev, ta, tb, p, st);
+    default: return BASAL200_ERR_DTYPE;
+  }
+}
+
+template <int OUT>
+int fp4_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const fp4gemm::Params& p,
+                    cudaStream_t st) {
+  auto kern = fp4gemm::nvfp4_gemm_kernel<OUT>;
+  int rc = set_smem(dev, kSlotFp4 + OUT, kern, fp4gemm::SMEM_BYTES);
+  if (rc) return rc;
+  const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
+  kern<<<grid, fp4gemm::NUM_THREADS, fp4gemm::SMEM_BYTES, st>>>(ta, tb, p);
+  return launched();
+}
+
+int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t* ws, const float* alpha,
+             const void* bias, void* y, int yt, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (M < 0 || N <= 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (K % 64 || N % 16) return BASAL200_ERR_SHAPE;
+  if (M == 0) return BASAL200_OK;
+  if (!q || !s || !w || !ws || !alpha || !y) return BASAL200_ERR_ARG;
+  if (!aligned16(q) || !aligned16(s) || !aligned16(w) || !aligned16(ws) || !aligned16(y) ||
+      (bias && !aligned16(bias)))
+    return BASAL200_ERR_ALIGN;
+  if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t Mp = (M + 127) / 128 * 128;
+  CUtensorMap ta, tb;
+  if ((rc = tmap_u8(&ta, q, (uint64_t)(K / 2), (uint64_t)Mp, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BM)))
+    return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BN)))
+    return rc;
+  fp4gemm::Params p;
+  p.sa = s;
+  p.sb = ws;
+  p.alpha = alpha;
+  p.bias = bias;
+  p.y = y;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nchunk = (int)(K / 64);
+  p.nkb = (p.nchunk + 3) / 4;
+  p.tiles_n = (int)((N + fp4gemm::BN - 1) / fp4gemm::BN);
+  const int64_t tiles = Mp / fp4gemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  switch (yt) {
+    case BASAL200_BF16: return fp4_gemm_launch<BASAL200_BF16>(dev, ta, tb, p, st);
+    case BASAL200_F16: return fp4_gemm_launch<BASAL200_F16>(dev, ta, tb, p, st);
+    case BASAL200_F32: return fp4_gemm_launch<BASAL200_F32>(dev, ta, tb, p, st);
+    default: return BASAL200_ERR_DTYPE;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// readout
+// ------------------------------------------------------------------------------------------------------------
+template <typename TH, typename TW>
+int logits_typed(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
+                 const int64_t* ids,
+                 int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
+  const dim3 grid((unsigned)((U + readout::TU - 1) / readout::TU), (unsigned)((R + readout::TR - 1) / readout::TR));
+  if (!bias) {
+    readout::code_logits_kernel<TH, TW, float><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U, nullptr,
+                                                                      softcap, z);
+  } else if (bt == BASAL200_F32) {
+    readout::code_logits_kernel<TH, TW, float><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
+                                                                      static_cast<const float*>(bias), softcap, z);
+  } else if (bt == BASAL200_BF16) {
+    readout::code_logits_kernel<TH, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(
+        h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z);
+  } else if (bt == BASAL200_F16) {
+    readout::code_logits_kernel<TH, TW, __half><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
+                                                                       static_cast<const __half*>(bias), softcap, z);
+  } else {
+    return BASAL200_ERR_DTYPE;
+  }
+  return launched();
+}
+
+template <typename TH>
+int logits_head(const TH* h, int64_t R, int64_t D, int64_t ldh, const void* head, int ht, int64_t V, int64_t ldw,
+                const int64_t* ids, int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
+  switch (ht) {
+    case BASAL200_BF16:
+      return logits_typed(h, R, D, ldh, static_cast<const __nv_bfloat16*>(head), V, ldw, ids, U, bias, bt, softcap,
+                          z, st);
+    case BASAL200_F16:
+      return logits_typed(h, R, D, ldh, static_cast<const __half*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
+    case BASAL200_F32:
+      return logits_typed(h, R, D, ldh, static_cast<const float*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+int basal200_fp8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, uint8_t* q, float* s, void* stream) {
+  return act_quant<false>(x, x_dtype, M, K, q, s, as_stream(stream));
+}
+
+int basal200_int8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* q, float* s, void* stream) {
+  return act_quant<true>(x, x_dtype, M, K, q, s, as_stream(stream));
+}
+
+int basal200_fp8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* q, float* s,
+                                void* stream) {
+  return weight_quant<false>(w, w_dtype, N, K, q, s, as_stream(stream));
+}
+
+int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* q, float* s,
+                                 void* stream) {
+  return weight_quant<true>(w, w_dtype, N, K, q, s, as_stream(stream));
+}
+
+int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
+                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  return block_gemm<false>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
+                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  return block_gemm<true>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,
+                              void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
+                              void* stream) {
+  if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
+  int rc = act_quant<false>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
+  if (rc) return rc;
+  return block_gemm<false>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, const float* ws, const void* bias,
+                               void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
+                               void* stream) {
+  if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
+  int rc = act_quant<true>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
+  if (rc) return rc;
+  return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_nvfp4_act_quant(const void* x, int x_dtype, const float* inv_g, int64_t M, int64_t K, uint8_t* q,
+                             uint8_t* s, void* stream) {
+  return nvfp4_act(x, x_dtype, inv_g, M, K, q, s, as_stream(stream));
+}
+
+int basal200_nvfp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t* ws, const float* alpha,
+                        const void* bias, void* y, int y_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  return fp4_gemm(q, s, w, ws, alpha, bias, y, y_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_nvfp4_linear(const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, const float* alpha,
+                          const float* inv_g, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                          uint8_t* q_scratch, uint8_t* s_scratch, void* stream) {
+  if (M > 0 && (N % 16)) return BASAL200_ERR_SHAPE;
+  int rc = nvfp4_act(x, x_dtype, inv_g, M, K, q_scratch, s_scratch, as_stream(stream));
+  if (rc) return rc;
+  return fp4_gemm(q_scratch, s_scratch, w, ws, alpha, bias, y, x_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_nvfp4_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* codes, uint8_t* scales,
+                            float* g, void* stream) {
+  if (N <= 0 || K <= 0 || !w || !codes || !scales || !g) return BASAL200_ERR_ARG;
+  if (K % 16) return BASAL200_ERR_SHAPE;
+  if (!aligned16(w) || !aligned16(codes)) return BASAL200_ERR_ALIGN;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  switch (w_dtype) {
+    case BASAL200_BF16:
+      return nvfp4_wq_typed(static_cast<const __nv_bfloat16*>(w), N, K, codes, scales, g, dev, st);
+    case BASAL200_F16: return nvfp4_wq_typed(static_cast<const __half*>(w), N, K, codes, scales, g, dev, st);
+    case BASAL200_F32: return nvfp4_wq_typed(static_cast<const float*>(w), N, K, codes, scales, g, dev, st);
+    default: return BASAL200_ERR_DTYPE;
+  }
+}
+
+int basal200_code_logits(const void* h, int h_dtype, int64_t R, int64_t D, int64_t ldh, const void* head,
+                         int head_dtype, int64_t V, int64_t ldw, const int64_t* ids, int64_t U, const void* bias,
+                         int bias_dtype, float softcap, float* z, void* stream) {
+  if (R < 0 || U < 0 || V <= 0 || D <= 0 || ldh < D || ldw < D) return BASAL200_ERR_ARG;
+  if (R == 0 || U == 0) return BASAL200_OK;
+  if (!h || !head || !ids || !z) return BASAL200_ERR_ARG;
+  if ((U + readout::TU - 1) / readout::TU > INT32_MAX || (R + readout::TR - 1) / readout::TR > 65535)
+    return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  switch (h_dtype) {
+    case BASAL200_BF16:
+      return logits_head(static_cast<const __nv_bfloat16*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+                         bias_dtype, softcap, z, st);
+    case BASAL200_F16:
+      return logits_head(static_cast<const __half*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+                         bias_dtype, softcap, z, st);
+    case BASAL200_F32:
+      return logits_head(static_cast<const float*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+                         bias_dtype, softcap, z, st);
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+}
+
+int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx, const uint8_t* pad, int64_t Kmax,
+                        float* p, void* stream) {
+  if (R < 0 || U < 0 || Kmax < 0) return BASAL200_ERR_ARG;
+  if (Kmax > 1024) return BASAL200_ERR_LIMIT;
+  if (R == 0 || Kmax == 0) return BASAL200_OK;
+  if (!z || !idx || !p) return BASAL200_ERR_ARG;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  readout::code_probs_kernel<<<(unsigned)((R + 7) / 8), 256, 0, as_stream(stream)>>>(z, R, U, idx, pad, Kmax, p);
+  return launched();
+}
+
+unsigned basal200_device_faults(int device, int clear) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  unsigned v = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(&v, g_fault, sizeof(v));
+  if (clear) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(g_fault, &zero, sizeof(zero));
+  }
+  cudaSetDevice(prev);
+  return v;
+}
+
+const char* basal200_status_string(int status) {
+  switch (status) {
+    case BASAL200_OK: return "ok";
+    case BASAL200_ERR_ARG: return "invalid argument (null pointer or negative size)";
+    case BASAL200_ERR_SHAPE: return "shape not supported by the format";
+    case BASAL200_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case BASAL200_ERR_DTYPE: return "unsupported dtype";
+    case BASAL200_ERR_ARCH: return "the current device is not sm_100 (B200)";
+    case BASAL200_ERR_LAUNCH: return "CUDA launch error";
+    case BASAL200_ERR_TMAP: return "TMA descriptor could not be encoded";
+    case BASAL200_ERR_LIMIT: return "size beyond the supported limit";
+    default: return "unknown status";
+  }
+}
+
+int basal200_version(void) { return 1; }
+
+}  // extern "C"

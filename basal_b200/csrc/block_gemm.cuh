@@ -1,0 +1,301 @@
+// The block-scaled GEMM of the FP8-block and INT8-block formats on sm_100a (replaces the Triton kernel of
+// basal/blockquant.py:63-106):
+//
+//   C[m, n] = sum_kb (A_kb[m, :] . B_kb[n, :]) * a_s[m, kb] * b_s[n / 128, kb]        (kb: 128-deep slices of K)
+//
+// A [M, K] and B [N, K] are 8-bit, K-major. One persistent CTA per SM walks 128 x 256 output tiles (static round
+// robin, the 256-wide weight tiles of one 128-row activation tile next to each other). Its warps:
+//   warp 0      TMA producer: A and B slices of 128 bytes of K into a 4-stage shared-memory ring (128-byte swizzle)
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K = 32 each) per slice into one of two TMEM accumulators of 256
+//               columns (kind::f8f6f4 e4m3 -> f32, or kind::i8 s8 -> s32, exact for a 128-deep slice)
+//   warp 2      TMEM allocation (512 columns) and release
+//   warps 4-11  promotion: per slice, tcgen05.ld of the slice's product, times a_s * b_s, added into fp32 registers
+//               (128 columns a thread); after the last slice, the cast (and bias) and the stores to C
+// The MMA of slice kb + 1 runs while the promotion reads slice kb from the other accumulator. A row's result never
+// depends on the other rows (no split of K, the same slice order for every M).
+#pragma once
+#include "quant.cuh"
+
+namespace b200 {
+namespace blockgemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes (= elements) of K per stage: one scale slice
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr uint32_t TMEM_COLS = 512;
+
+struct Shared {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mdrain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+
+struct Params {
+  const float* s;   // [M, K/128]
+  const float* ws;  // [N/128, K/128]
+  const void* bias; // [N] in the output type, or null
+  void* c;          // [M, N]
+  int M, N, nkb, tiles_n, num_tiles;
+};
+
+// Bounded drain wait (the abort flag is already set when it runs).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(&g_fault, kFaultTimeoutDrain);
+      return;
+    }
+  }
+}
+
+// All 32 lanes wait; the warp proceeds only if every lane saw the phase complete.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned fault) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, fault);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Casts and stores of fp32 results: vec8 writes 8 consecutive outputs (one 16- or 32-byte store); a bias in the
+// output type is added to the cast value and rounded again, as torch adds a bias to the cast product.
+template <int OUT>
+struct Store;
+template <>
+struct Store<BASAL200_BF16> {
+  using T = __nv_bfloat16;
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      if (bias) {
+        const float2 y = __bfloat1622float2(h);
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + 2 * i));
+        h = __floats2bfloat162_rn(__fadd_rn(y.x, b.x), __fadd_rn(y.y, b.y));
+      }
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(dst) = u;
+  }
+};
+template <>
+struct Store<BASAL200_F16> {
+  using T = __half;
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      if (bias) {
+        const float2 y = __half22float2(h);
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(bias + 2 * i));
+        h = __floats2half2_rn(__fadd_rn(y.x, b.x), __fadd_rn(y.y, b.y));
+      }
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(dst) = u;
+  }
+};
+template <>
+struct Store<BASAL200_F32> {
+  using T = float;
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+#pragma unroll
+    for (int c = 0; c < 8; c += 4) {
+      float4 f = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+      if (bias) {
+        f.x = __fadd_rn(f.x, bias[c]);
+        f.y = __fadd_rn(f.y, bias[c + 1]);
+        f.z = __fadd_rn(f.z, bias[c + 2]);
+        f.w = __fadd_rn(f.w, bias[c + 3]);
+      }
+      *reinterpret_cast<float4*>(dst + c) = f;
+    }
+  }
+};
+
+template <bool INT8, int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    block_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.tfull[b], 1);
+      mbar_init(&sh.tempty[b], NUM_EPI_WARPS);
+    }
+    mbar_init(&sh.mdrain, 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled = 0, last_phase = 0;  // per-stage bit masks, for the drain after an abort
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.full[stage], STAGE_TX);
+          tma_load_2d(sh.a[stage], &tmA, &sh.full[stage], kb * BK, tm * BM);
+          tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BK, tn * BN);
+          filled |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // let the copies already issued land before the CTA's shared memory goes away
+        for (int s = 0; s < STAGES; ++s)
+          if (filled & (1u << s)) drain_wait(&sh.full[s], (last_phase >> s) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = INT8 ? idesc_dense(2, 1, 1, BM, BN) : idesc_dense(1, 0, 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0, acc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          const uint32_t buf = acc & 1, aph = (acc >> 1) & 1;
+          if (!mbar_wait(&sh.tempty[buf], aph ^ 1, abort_flag, kFaultTimeoutMma) ||
+              !mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * BN;
+          const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
+          const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            if (INT8)
+              mma_i8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+            else
+              mma_f8f6f4(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+          }
+          mma_commit(&sh.empty[stage]);
+          mma_commit(&sh.tfull[buf]);
+          ++acc;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // every MMA issued has finished before TMEM and shared memory are released
+      mma_commit(&sh.mdrain);
+      drain_wait(&sh.mdrain, 0);
+    }
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- promotion and epilogue ----------------
+    using OutT = typename Store<OUT>::T;
+    const int ew = warp - EPI_WARP0;
+    const int half = ew >> 2;   // which 128 columns of the 256-wide tile
+    const int quad = warp & 3;  // the TMEM lane quadrant this warp may access
+    const int nkb = p.nkb;
+    uint32_t acc_cnt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+      const int row = tm * BM + quad * 32 + lane;
+      const int n0 = tn * BN + half * 128;
+      const bool nvalid = n0 < p.N;
+      const float* srow = p.s + (int64_t)min(row, p.M - 1) * nkb;
+      const float* wsr = p.ws + (int64_t)min(n0 / 128, p.N / 128 - 1) * nkb;
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      float sa = __ldg(srow), sb = __ldg(wsr);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const float sc = sa * sb;
+        if (kb + 1 < nkb) {
+          sa = __ldg(srow + kb + 1);
+          sb = __ldg(wsr + kb + 1);
+        }
+        const uint32_t buf = acc_cnt & 1, ph = (acc_cnt >> 1) & 1;
+        if (!warp_wait(&sh.tfull[buf], ph, abort_flag, kFaultTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + half * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float part = INT8 ? static_cast<float>(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+            acc[c * 16 + j] = fmaf(part, sc, acc[c * 16 + j]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.tempty[buf]);
+        ++acc_cnt;
+      }
+      if (ok && nvalid && row < p.M) {
+        OutT* dst = reinterpret_cast<OutT*>(p.c) + (int64_t)row * p.N + n0;
+        const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
+#pragma unroll
+        for (int c = 0; c < 128; c += 8) Store<OUT>::vec8(dst + c, acc + c, bias ? bias + c : nullptr);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace blockgemm
+}  // namespace b200

@@ -1,0 +1,213 @@
+// The NVFP4 GEMM on sm_100a (replaces cuBLAS's block-scaled FP4 GEMM behind F.scaled_mm, basal/nvfp4.py:167-180):
+//
+//   Y[m, n] = alpha * sum_k (e2m1 A[m, k] * sA[m, k / 16]) * (e2m1 B[n, k] * sB[n, k / 16])
+//
+// with the e4m3 block scales applied by the tensor core itself (tcgen05.mma kind::mxf4nvf4, scale_vec::4X, K = 64
+// an instruction). A [Mp, K/2] and B [N, K/2] are packed e2m1 (even feature in the low nibble), K-major. The scales
+// are consumed as the reference stores them, in the 128 x 4 tile swizzle (512 bytes for 128 rows x 64 features):
+// that tile, moved into TMEM by tcgen05.cp's 32x128b.warpx4 shape, is the layout the MMA reads (lane l, column c,
+// byte j = scale of row 32 c + l % 32, feature group j). Persistent CTAs walk 128 x 128 output tiles:
+//   warp 0      producer: TMA of A / B (256 features = 128 bytes a stage, 128-byte swizzle) and plain bulk copies of
+//               the stage's 4 + 4 scale tiles into a 5-stage ring
+//   warp 1      MMA issuer: tcgen05.cp of the stage's scale tiles to TMEM, 4 MMAs, commit
+//   warp 2      TMEM allocation: 2 accumulators of 128 columns, then 32 scale columns per stage
+//   warps 4-11  epilogue: tcgen05.ld, times alpha, (+ bias), cast, store
+#pragma once
+#include "block_gemm.cuh"
+
+namespace b200 {
+namespace fp4gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BKB = 128;  // bytes of K per stage (256 e2m1 values = 4 scale tiles)
+constexpr int STAGES = 5;
+constexpr int A_BYTES = BM * BKB;
+constexpr int B_BYTES = BN * BKB;
+constexpr int SF_BYTES = 4 * 512;
+constexpr int NUM_THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t SF_COL0 = 2 * BN;  // scale columns after the two accumulators
+constexpr uint32_t SF_COLS_PER_STAGE = 32;
+
+struct Shared {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint8_t sfa[STAGES][SF_BYTES];
+  uint8_t sfb[STAGES][SF_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mdrain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+
+struct Params {
+  const uint8_t* sa;   // swizzled scales of A: Mp/128 x (K/64) tiles
+  const uint8_t* sb;   // of B: ceil(N/128) x (K/64) tiles
+  const float* alpha;  // [1]
+  const void* bias;    // [N] output type, or null
+  void* y;             // [M, N]
+  int M, N, nchunk, nkb, tiles_n, num_tiles;
+};
+
+template <int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.tfull[b], 1);
+      mbar_init(&sh.tempty[b], NUM_EPI_WARPS);
+    }
+    mbar_init(&sh.mdrain, 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+  const int64_t c4 = p.nchunk;  // scale tiles per 128-row block (K / 64)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, filled = 0, last_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          const int nch = min(4, p.nchunk - kb * 4);
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + 2 * nch * 512);
+          tma_load_2d(sh.a[stage], &tmA, &sh.full[stage], kb * BKB, tm * BM);
+          tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BKB, tn * BN);
+          bulk_load(sh.sfa[stage], p.sa + ((int64_t)tm * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
+          bulk_load(sh.sfb[stage], p.sb + ((int64_t)tn * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
+          filled |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s)
+          if (filled & (1u << s)) blockgemm::drain_wait(&sh.full[s], (last_phase >> s) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_block_scaled(1, 1, BM, BN);  // e2m1 x e2m1, ue4m3 scales, f32 accumulate
+      int stage = 0;
+      uint32_t phase = 0, acc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const uint32_t buf = acc & 1, aph = (acc >> 1) & 1;
+        if (!mbar_wait(&sh.tempty[buf], aph ^ 1, abort_flag, kFaultTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          const int nch = min(4, p.nchunk - kb * 4);
+          if (!mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfcol = tmem + SF_COL0 + stage * SF_COLS_PER_STAGE;
+          for (int c = 0; c < nch; ++c) {
+            tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[stage] + c * 512)));
+            tmem_cp_32x128b_x4(sfcol + 16 + c * 4, desc_plain16(smem_u32(sh.sfb[stage] + c * 512)));
+          }
+          const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
+          const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
+          for (int c = 0; c < nch; ++c)
+            mma_mxf4nvf4(d, ad + 2 * c, bd + 2 * c, idesc, sfcol + c * 4, sfcol + 16 + c * 4, (kb | c) != 0);
+          mma_commit(&sh.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&sh.tfull[buf]);
+        ++acc;
+      }
+      mma_commit(&sh.mdrain);
+      blockgemm::drain_wait(&sh.mdrain, 0);
+    }
+  } else if (warp >= EPI_WARP0) {
+    using OutT = typename blockgemm::Store<OUT>::T;
+    const int ew = warp - EPI_WARP0;
+    const int half = ew >> 2;   // which 64 columns of the tile
+    const int quad = warp & 3;
+    const float alpha = __ldg(p.alpha);
+    uint32_t acc_cnt = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+      const int row = tm * BM + quad * 32 + lane;
+      const uint32_t buf = acc_cnt & 1, ph = (acc_cnt >> 1) & 1;
+      if (!blockgemm::warp_wait(&sh.tfull[buf], ph, abort_flag, kFaultTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + half * 64;
+      float v[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c * 16, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[c * 16 + j] = __fmul_rn(__uint_as_float(r[j]), alpha);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty[buf]);
+      ++acc_cnt;
+      const int n0 = tn * BN + half * 64;
+      if (row < p.M) {
+        OutT* dst = reinterpret_cast<OutT*>(p.y) + (int64_t)row * p.N + n0;
+        const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          if (n0 + c < p.N)  // N % 16 == 0: an 8-column group is whole or absent
+            blockgemm::Store<OUT>::vec8(dst + c, v + c, bias ? bias + c : nullptr);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace fp4gemm
+}  // namespace b200

@@ -1,0 +1,319 @@
+// Quantisers of the block formats and of NVFP4, bit-exact to the reference's CPU arithmetic (rkinas/basal 2.8.1):
+// every division is an IEEE round-to-nearest division (__fdiv_rn), every product that the reference rounds on its
+// own is __fmul_rn (no contraction into an FMA), casts to e4m3 round to nearest even (cvt.rn.satfinite after an
+// explicit clamp), int8 rounds half to even.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+namespace b200 {
+
+// ---- element loads: n consecutive values as fp32 (16-byte vector loads) ----
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+__device__ __forceinline__ uint8_t float_to_e4m3(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+// 8 values of one group -> 8 code bytes: v / sc, INT8: round half to even; clamp to +-qmax; cast.
+template <bool INT8>
+__device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float t = __fdiv_rn(v[i], sc);
+    uint32_t b;
+    if (INT8) {
+      t = fminf(fmaxf(rintf(t), -127.0f), 127.0f);
+      b = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(t))));
+    } else {
+      t = fminf(fmaxf(t, -448.0f), 448.0f);
+      b = float_to_e4m3(t);
+    }
+    w[i >> 2] |= b << (8 * (i & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Activations, FP8 / INT8 block formats: one half-warp per 128-feature group (8 values a lane), amax by shuffles.
+// basal/blockquant.py:118-123: s = max(amax, 1e-12) / qmax; q = cast(clamp(x / s)) (INT8: round first).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T, bool INT8>
+__global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups, int gpr,
+                                                              int64_t K, uint8_t* __restrict__ q,
+                                                              float* __restrict__ s) {
+  constexpr float kQmax = INT8 ? 127.0f : 448.0f;
+  const int lane = threadIdx.x & 31;
+  const int half = lane >> 4, l = lane & 15;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t p = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; 2 * p < groups; p += warps) {
+    const int64_t g = 2 * p + half;
+    const bool valid = g < groups;
+    float v[8];
+    int64_t off = 0;
+    if (valid) {
+      const int64_t row = g / gpr;
+      const int64_t kb = g - row * gpr;
+      off = row * K + kb * 128 + l * 8;
+      load8(x + off, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
+    const uint2 codes = block_codes8<INT8>(v, sc);
+    if (valid) {
+      *reinterpret_cast<uint2*>(q + off) = codes;
+      if (l == 0) s[g] = sc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Weights, FP8 / INT8 block formats: one CTA per 128 x 128 block (basal/blockquant.py:126-135).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T, bool INT8>
+__global__ void __launch_bounds__(256) weight_quant_block_kernel(const T* __restrict__ w, int64_t K,
+                                                                 uint8_t* __restrict__ q, float* __restrict__ s) {
+  constexpr float kQmax = INT8 ? 127.0f : 448.0f;
+  __shared__ float red[8];
+  const int kb = blockIdx.x, nb = blockIdx.y, t = threadIdx.x;
+  const int r = t >> 1, c0 = (t & 1) * 64;
+  const int64_t base = ((int64_t)nb * 128 + r) * K + (int64_t)kb * 128 + c0;
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 64; c += 8) {
+    float v[8];
+    load8(w + base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
+#pragma unroll
+  for (int c = 0; c < 64; c += 8) {
+    float v[8];
+    load8(w + base + c, v);
+    *reinterpret_cast<uint2*>(q + base + c) = block_codes8<INT8>(v, sc);
+  }
+  if (t == 0) s[(int64_t)nb * gridDim.x + kb] = sc;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// NVFP4
+// ---------------------------------------------------------------------------------------------------------------
+// e2m1 code of u (in units of the block scale): the cuts of basal/nvfp4.py:22 (ties to the even code), sign bit 3
+// for every u < 0 (nvfp4.py:36-41).
+__device__ __forceinline__ uint32_t e2m1_code(float u) {
+  const float a = fabsf(u);
+  uint32_t c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) + (a >= 3.5f) + (a > 5.0f);
+  return c | ((u < 0.0f) ? 8u : 0u);
+}
+
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const float v = mag[c & 7];
+  return (c & 8) ? -v : v;
+}
+
+// Byte offset of scale (row r, 16-group j) in the 128 x 4 tile swizzle of a matrix with `c4` tiles a row
+// (basal/nvfp4.py:49-56, :140-143).
+__device__ __forceinline__ int64_t swizzled_scale_offset(int64_t r, int64_t j, int64_t c4) {
+  return ((r >> 7) * c4 + (j >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (j & 3);
+}
+
+// One CTA per 128 rows x 64 features, one thread per (row, 16-group): codes and the tile's 512 scale bytes, staged
+// in shared memory and written as 16-byte stores. Rows past M (up to the 128-row padding) get zeros.
+template <typename T>
+__global__ void __launch_bounds__(512) nvfp4_act_quant_kernel(const T* __restrict__ x, const float* __restrict__ inv_g_p,
+                                                              int64_t M, int64_t K, uint8_t* __restrict__ q,
+                                                              uint8_t* __restrict__ s) {
+  __shared__ __align__(16) uint8_t sbuf[512];
+  const int64_t tile_r = blockIdx.y;
+  const int64_t c64 = blockIdx.x;
+  const int t = threadIdx.x;
+  const int r = t >> 2, j = t & 3;
+  const int64_t row = tile_r * 128 + r;
+  uint32_t scale_bits = 0, lo = 0, hi = 0;
+  if (row < M) {
+    const float inv_g = __ldg(inv_g_p);
+    float v[16];
+    const T* p = x + row * K + c64 * 64 + j * 16;
+    {
+      float a[8], b[8];
+      load8(p, a);
+      load8(p + 8, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = a[i];
+        v[8 + i] = b[i];
+      }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = __fmul_rn(v[i], inv_g);
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+    const uint8_t sb = float_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
+    const float sf = e4m3_to_float(sb);
+    scale_bits = sb;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float u = sf > 0.0f ? __fdiv_rn(v[i], sf) : 0.0f;
+      const uint32_t c = e2m1_code(u);
+      if (i < 8)
+        lo |= c << (4 * i);
+      else
+        hi |= c << (4 * (i - 8));
+    }
+  }
+  *reinterpret_cast<uint2*>(q + row * (K / 2) + c64 * 32 + j * 8) = make_uint2(lo, hi);
+  sbuf[(r & 31) * 16 + (r >> 5) * 4 + j] = static_cast<uint8_t>(scale_bits);
+  __syncthreads();
+  if (t < 32) {
+    const int64_t tile = tile_r * (K / 64) + c64;
+    reinterpret_cast<uint4*>(s + tile * 512)[t] = reinterpret_cast<const uint4*>(sbuf)[t];
+  }
+}
+
+// ---- NVFP4 weights (basal/nvfp4.py:75-97) ----
+// Largest |w| into g[0] (as fp32 bits; g zeroed before): the weights' global amax.
+template <typename T>
+__global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ w, int64_t n8, unsigned* __restrict__ out) {
+  float amax = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float v[8];
+    load8(w + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(amax));
+}
+
+// One thread per 16-block of the weight's scale tiles: Np = N rounded up to 128 rows, c4 tiles of 4 blocks a row
+// (K / 16 blocks rounded up to 4); blocks past N rows or past K / 16 columns get a zero scale (the padding of
+// basal/nvfp4.py:49-56).
+// g = max(amax / (6 * 448), 1e-12); b = w / g; per candidate f: s = e4m3(min(amax16 * f / 6, 448)), codes of b / s,
+// squared error summed as torch's CPU kernel sums 16 values (lanes k and k + 8, then 0 + p0 + ... + p7); the
+// smallest error wins, the earlier candidate on a tie.
+template <typename T>
+__global__ void __launch_bounds__(256) nvfp4_weight_quant_kernel(const T* __restrict__ w, const float* __restrict__ gbuf,
+                                                                 int64_t N, int64_t Np, int64_t K, int64_t c4,
+                                                                 uint8_t* __restrict__ codes,
+                                                                 uint8_t* __restrict__ scales) {
+  const int64_t kb16 = K / 16, cols = c4 * 4;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= Np * cols) return;
+  const int64_t row = idx / cols, j = idx - row * cols;
+  if (row >= N || j >= kb16) {
+    scales[swizzled_scale_offset(row, j, c4)] = 0;
+    return;
+  }
+  const float g = fmaxf(__fdiv_rn(__ldg(gbuf), 2688.0f), 1e-12f);
+  float b[16];
+  {
+    float a[8], c[8];
+    load8(w + row * K + j * 16, a);
+    load8(w + row * K + j * 16 + 8, c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      b[i] = a[i];
+      b[8 + i] = c[i];
+    }
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    b[i] = __fdiv_rn(b[i], g);
+    amax = fmaxf(amax, fabsf(b[i]));
+  }
+  // the candidates 1 - 0.04 j, computed in double by the reference and rounded to fp32 where they meet amax
+  const float cand[8] = {(float)(1.0 - 0.04 * 0), (float)(1.0 - 0.04 * 1), (float)(1.0 - 0.04 * 2),
+                         (float)(1.0 - 0.04 * 3), (float)(1.0 - 0.04 * 4), (float)(1.0 - 0.04 * 5),
+                         (float)(1.0 - 0.04 * 6), (float)(1.0 - 0.04 * 7)};
+  float best_err = 0.0f;
+  uint32_t best_lo = 0, best_hi = 0, best_s = 0;
+#pragma unroll 1
+  for (int f = 0; f < 8; ++f) {
+    const uint8_t sb = float_to_e4m3(fminf(__fdiv_rn(__fmul_rn(amax, cand[f]), 6.0f), 448.0f));
+    const float sf = e4m3_to_float(sb);
+    uint32_t lo = 0, hi = 0;
+    float d[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float u = sf > 0.0f ? __fdiv_rn(b[i], sf) : 0.0f;
+      const uint32_t c = e2m1_code(u);
+      if (i < 8)
+        lo |= c << (4 * i);
+      else
+        hi |= c << (4 * (i - 8));
+      const float e = __fsub_rn(__fmul_rn(e2m1_value(c), sf), b[i]);
+      d[i] = __fmul_rn(e, e);
+    }
+    float err = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) err = __fadd_rn(err, __fadd_rn(d[k], d[k + 8]));
+    if (f == 0 || err < best_err) {
+      best_err = err;
+      best_lo = lo;
+      best_hi = hi;
+      best_s = sb;
+    }
+  }
+  *reinterpret_cast<uint2*>(codes + row * (K / 2) + j * 8) = make_uint2(best_lo, best_hi);
+  scales[swizzled_scale_offset(row, j, c4)] = static_cast<uint8_t>(best_s);
+}
+
+__global__ void nvfp4_global_scale_kernel(float* g) {
+  g[0] = fmaxf(__fdiv_rn(g[0], 2688.0f), 1e-12f);
+}
+
+}  // namespace b200

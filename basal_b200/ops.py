@@ -1,0 +1,279 @@
+"""The torch ops of the hot path, under the reference's names where it has them, each a thin call of libbasal200.
+
+  basal::fp8_block_gemm(q, s, w, ws, dtype)      reference op, basal/blockquant.py:151-159 (FP8 format)
+  basal::int8_block_gemm(q, s, w, ws, dtype)     reference op, same, INT8 format (int8block.py:349)
+  basal::nvfp4_linear(x, w, ws, alpha, inv_g)    reference op, basal/nvfp4.py:183-194
+  basal::fp8_block_linear(x, w, ws, bias)        act_quant + GEMM (+ bias): what fp8block.linear computes
+                                                 (fp8block.py:285-296); takes the place of basal::fp8_block_linear_sm90
+  basal::int8_block_linear(x, w, ws, bias)       the same for INT8 (BlockFormat.linear, blockquant.py:175-183)
+  basal::fp8_act_quant(x), basal::int8_act_quant(x)
+                                                 BlockFormat.act_quant (blockquant.py:137-144), as ops so that a
+                                                 compiled layer keeps them whole
+  basal::nvfp4_act_quant(x, inv_g)               nvfp4.act_quant (nvfp4.py:148-158)
+  basal::nvfp4_gemm(q, s, w, ws, alpha, m, dtype)  nvfp4._mm (nvfp4.py:167-180)
+  basal::code_logits(h, head, ids, bias, softcap)  CodeReadout.logits over the option rows (readout.py:71-74)
+  basal::code_probs(z, idx, pad)                 CodeReadout.probs_of (readout.py:76-79)
+
+Every op is functional (mutates_args=()), allocates its outputs (and scratch) from the caching allocator, enqueues on
+the current stream and never synchronises: Dynamo traces them through their fake kernels and a CUDA graph captures
+their launches. They need CUDA tensors; there is no CPU implementation.
+"""
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import call, code, ptr, require_cuda
+
+E4M3 = torch.float8_e4m3fn
+Tensor = torch.Tensor
+
+
+def _c(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# block formats
+# ---------------------------------------------------------------------------------------------------------------
+def _act_quant(x, integer):
+    require_cuda(x)
+    x = _c(x)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8 if integer else E4M3, device=x.device)
+    s = torch.empty((M, K // 128 if K % 128 == 0 else 0), dtype=torch.float32, device=x.device)
+    name = "basal200_int8_act_quant" if integer else "basal200_fp8_act_quant"
+    call(name, x.device, ptr(x), code(x.dtype), M, K, ptr(q), ptr(s))
+    return q, s
+
+
+@torch.library.custom_op("basal::fp8_act_quant", mutates_args=())
+def fp8_act_quant(x: Tensor) -> tuple[Tensor, Tensor]:
+    """[M, K] -> (e4m3 [M, K], fp32 scales [M, K / 128])."""
+    return _act_quant(x, False)
+
+
+@fp8_act_quant.register_fake
+def _(x):
+    return x.new_empty(x.shape, dtype=E4M3), x.new_empty((x.shape[0], x.shape[1] // 128), dtype=torch.float32)
+
+
+@torch.library.custom_op("basal::int8_act_quant", mutates_args=())
+def int8_act_quant(x: Tensor) -> tuple[Tensor, Tensor]:
+    """[M, K] -> (int8 [M, K], fp32 scales [M, K / 128])."""
+    return _act_quant(x, True)
+
+
+@int8_act_quant.register_fake
+def _(x):
+    return x.new_empty(x.shape, dtype=torch.int8), x.new_empty((x.shape[0], x.shape[1] // 128), dtype=torch.float32)
+
+
+def _block_gemm(q, s, w, ws, dtype, integer, bias=None):
+    require_cuda(q, s, w, ws, bias)
+    q, s, w, ws = _c(q), _c(s), _c(w), _c(ws)
+    M, K = q.shape
+    N = w.shape[0]
+    c = torch.empty((M, N), dtype=dtype, device=q.device)
+    if bias is not None:
+        bias = _c(bias.to(dtype))
+    name = "basal200_int8_block_gemm" if integer else "basal200_fp8_block_gemm"
+    call(name, q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(bias), ptr(c), code(dtype), M, N, K)
+    return c
+
+
+@torch.library.custom_op("basal::fp8_block_gemm", mutates_args=())
+def fp8_block_gemm(q: Tensor, s: Tensor, w: Tensor, ws: Tensor, dtype: torch.dtype) -> Tensor:
+    """(q, s) [M, K] x (w, ws) [N, K]^T -> [M, N] in dtype (basal/blockquant.py:151-159)."""
+    return _block_gemm(q, s, w, ws, dtype, False)
+
+
+@fp8_block_gemm.register_fake
+def _(q, s, w, ws, dtype):
+    return q.new_empty((q.shape[0], w.shape[0]), dtype=dtype)
+
+
+@torch.library.custom_op("basal::int8_block_gemm", mutates_args=())
+def int8_block_gemm(q: Tensor, s: Tensor, w: Tensor, ws: Tensor, dtype: torch.dtype) -> Tensor:
+    """The INT8 format of fp8_block_gemm (int8 codes, each 128-deep slice exact in int32)."""
+    return _block_gemm(q, s, w, ws, dtype, True)
+
+
+@int8_block_gemm.register_fake
+def _(q, s, w, ws, dtype):
+    return q.new_empty((q.shape[0], w.shape[0]), dtype=dtype)
+
+
+def _block_linear(x, w, ws, bias, integer):
+    require_cuda(x, w, ws, bias)
+    x, w, ws = _c(x), _c(w), _c(ws)
+    M, K = x.shape
+    N = w.shape[0]
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    q = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((M, max(K // 128, 1)), dtype=torch.float32, device=x.device)
+    if bias is not None:
+        bias = _c(bias.to(x.dtype))
+    name = "basal200_int8_block_linear" if integer else "basal200_fp8_block_linear"
+    call(name, x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(bias), ptr(y), M, N, K, ptr(q), ptr(s))
+    return y
+
+
+@torch.library.custom_op("basal::fp8_block_linear", mutates_args=())
+def fp8_block_linear(x: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor] = None) -> Tensor:
+    """x [M, K] -> [M, N] in x's dtype through an FP8-block weight: act_quant + GEMM (+ bias)."""
+    return _block_linear(x, w, ws, bias, False)
+
+
+@fp8_block_linear.register_fake
+def _(x, w, ws, bias=None):
+    return x.new_empty((x.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("basal::int8_block_linear", mutates_args=())
+def int8_block_linear(x: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor] = None) -> Tensor:
+    """x [M, K] -> [M, N] through an INT8-block weight."""
+    return _block_linear(x, w, ws, bias, True)
+
+
+@int8_block_linear.register_fake
+def _(x, w, ws, bias=None):
+    return x.new_empty((x.shape[0], w.shape[0]))
+
+
+def block_quantize(w, integer):
+    """Weight [N, K] -> (codes [N, K], fp32 scales [N / 128, K / 128]) on w's CUDA device (load time)."""
+    require_cuda(w)
+    w = _c(w if w.dtype in _lib.DTYPE_CODE else w.float())
+    N, K = w.shape
+    if N % 128 or K % 128:
+        raise ValueError(f"block quantisation: weight {N} x {K}, both dimensions must be multiples of 128")
+    q = torch.empty((N, K), dtype=torch.int8 if integer else E4M3, device=w.device)
+    s = torch.empty((N // 128, K // 128), dtype=torch.float32, device=w.device)
+    name = "basal200_int8_block_quantize" if integer else "basal200_fp8_block_quantize"
+    call(name, w.device, ptr(w), code(w.dtype), N, K, ptr(q), ptr(s))
+    return q, s
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# NVFP4
+# ---------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op("basal::nvfp4_act_quant", mutates_args=())
+def nvfp4_act_quant(x: Tensor, inv_g: Tensor) -> tuple[Tensor, Tensor]:
+    """[M, K] -> (codes [Mp, K / 2] uint8, swizzled e4m3 scales [Mp * K / 16] uint8), Mp = M rounded up to 128."""
+    require_cuda(x, inv_g)
+    x = _c(x)
+    M, K = x.shape
+    Mp = (M + 127) // 128 * 128
+    q = torch.empty((Mp, K // 2), dtype=torch.uint8, device=x.device)
+    s = torch.empty((Mp * (K // 16),), dtype=torch.uint8, device=x.device)
+    call("basal200_nvfp4_act_quant", x.device, ptr(x), code(x.dtype), ptr(_c(inv_g.float())), M, K, ptr(q), ptr(s))
+    return q, s
+
+
+@nvfp4_act_quant.register_fake
+def _(x, inv_g):
+    M, K = x.shape
+    Mp = (M + 127) // 128 * 128
+    return x.new_empty((Mp, K // 2), dtype=torch.uint8), x.new_empty((Mp * (K // 16),), dtype=torch.uint8)
+
+
+@torch.library.custom_op("basal::nvfp4_gemm", mutates_args=())
+def nvfp4_gemm(q: Tensor, s: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, m: int, dtype: torch.dtype) -> Tensor:
+    """Codes q [Mp, K / 2] with swizzled scales s, weight codes w [N, K / 2] with ws -> [m, N] in dtype, times alpha."""
+    require_cuda(q, s, w, ws, alpha)
+    q, s, w, ws = _c(q), _c(s), _c(w), _c(ws)
+    K = q.shape[1] * 2
+    N = w.shape[0]
+    y = torch.empty((m, N), dtype=dtype, device=q.device)
+    call("basal200_nvfp4_gemm", q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(_c(alpha.float())), None, ptr(y),
+         code(dtype), m, N, K)
+    return y
+
+
+@nvfp4_gemm.register_fake
+def _(q, s, w, ws, alpha, m, dtype):
+    return q.new_empty((m, w.shape[0]), dtype=dtype)
+
+
+@torch.library.custom_op("basal::nvfp4_linear", mutates_args=())
+def nvfp4_linear(x: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, inv_g: Tensor) -> Tensor:
+    """x [M, K] -> [M, N] in x's dtype: the quantiser and the GEMM as one op (basal/nvfp4.py:183-189)."""
+    require_cuda(x, w, ws, alpha, inv_g)
+    x, w, ws = _c(x), _c(w), _c(ws)
+    M, K = x.shape
+    N = w.shape[0]
+    Mp = (M + 127) // 128 * 128
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    q = torch.empty((max(Mp, 1), K // 2), dtype=torch.uint8, device=x.device)
+    s = torch.empty((max(Mp, 1) * (K // 16),), dtype=torch.uint8, device=x.device)
+    call("basal200_nvfp4_linear", x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(_c(alpha.float())),
+         ptr(_c(inv_g.float())), None, ptr(y), M, N, K, ptr(q), ptr(s))
+    return y
+
+
+@nvfp4_linear.register_fake
+def _(x, w, ws, alpha, inv_g):
+    return x.new_empty((x.shape[0], w.shape[0]))
+
+
+def nvfp4_quantize(w):
+    """Weight [N, K] -> (codes [N, K / 2] uint8, swizzled e4m3 scales, fp32 global scale [1]) on w's CUDA device."""
+    require_cuda(w)
+    w = _c(w if w.dtype in _lib.DTYPE_CODE else w.float())
+    N, K = w.shape
+    if K % 16:
+        raise ValueError(f"NVFP4 quantisation: weight {N} x {K}, K must be a multiple of 16")
+    Np, C = (N + 127) // 128 * 128, (K // 16 + 3) // 4 * 4
+    codes = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((Np * C,), dtype=torch.uint8, device=w.device)
+    g = torch.empty((1,), dtype=torch.float32, device=w.device)
+    call("basal200_nvfp4_quantize", w.device, ptr(w), code(w.dtype), N, K, ptr(codes), ptr(scales), ptr(g))
+    return codes, scales.view(E4M3), g
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# readout
+# ---------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op("basal::code_logits", mutates_args=())
+def code_logits(h: Tensor, head: Tensor, ids: Tensor, bias: Optional[Tensor] = None,
+                softcap: float = 0.0) -> Tensor:
+    """h [R, D] . head[ids]^T (+ bias[ids]), soft-capped -> fp32 [R, U]; the rows are read from the head by id."""
+    require_cuda(h, head, ids, bias)
+    if h.stride(-1) != 1:
+        h = h.contiguous()
+    if head.stride(-1) != 1:
+        head = head.contiguous()
+    ids = _c(ids.to(torch.int64))
+    R, D = h.shape
+    U = ids.numel()
+    z = torch.empty((R, U), dtype=torch.float32, device=h.device)
+    if bias is not None:
+        bias = _c(bias)
+    call("basal200_code_logits", h.device, ptr(h), code(h.dtype), R, D, h.stride(0), ptr(head), code(head.dtype),
+         head.shape[0], head.stride(0), ptr(ids), U, ptr(bias), code(bias.dtype) if bias is not None else 0,
+         float(softcap or 0.0), ptr(z))
+    return z
+
+
+@code_logits.register_fake
+def _(h, head, ids, bias=None, softcap=0.0):
+    return h.new_empty((h.shape[0], ids.numel()), dtype=torch.float32)
+
+
+@torch.library.custom_op("basal::code_probs", mutates_args=())
+def code_probs(z: Tensor, idx: Tensor, pad: Tensor) -> Tensor:
+    """Code logits z [R, U] -> each prompt's probabilities over its codes [R, Kmax] (padding 0)."""
+    require_cuda(z, idx, pad)
+    z, idx = _c(z.float()), _c(idx.to(torch.int64))
+    pad = _c(pad.to(torch.uint8))
+    R, U = z.shape
+    Kmax = idx.shape[1]
+    p = torch.empty((R, Kmax), dtype=torch.float32, device=z.device)
+    call("basal200_code_probs", z.device, ptr(z), R, U, ptr(idx), ptr(pad), Kmax, ptr(p))
+    return p
+
+
+@code_probs.register_fake
+def _(z, idx, pad):
+    return z.new_empty((z.shape[0], idx.shape[1]), dtype=torch.float32)

@@ -1,0 +1,87 @@
+"""The readout of the option codes, B200 build (the interface of basal/readout.py, rkinas/basal 2.8.1).
+
+A question's answer is the softmax over its option codes of the logits at the answer position; only those rows of
+the output head are read. Here they are read straight from the head (bf16) by id inside the contraction kernel
+(basal::code_logits): nothing is copied or widened to fp32 first, so the row cache keeps only the ids. Products and sums are fp32; every logit is one fixed-order sum, so a prompt's probabilities are the same bits
+whatever prompts are read with it (probs and probs_each agree exactly).
+
+  rows(lids) -> (rows, idx, pad)   rows = (ids of the union of the prompts' codes on the device, None): the bias, if
+                                   any, is read by id from the head inside the kernel as well
+  logits(h, rows) -> fp32 [n, k]   basal::code_logits, soft cap applied once
+  probs_of(z, idx, pad)            basal::code_probs: gather, -inf padding, softmax
+  probs(h, lids), probs_each(h, lids)   one copy to the host
+"""
+import torch
+
+from . import ops
+
+WROWS_BYTES = 64 << 20  # what an engine's code-row cache may hold (here: the ids, 8 bytes a code)
+
+
+def _nbytes(x):
+    if x is None:
+        return 0
+    if isinstance(x, tuple):
+        return sum(_nbytes(y) for y in x)
+    return int(x.nbytes)
+
+
+def code_rows(cache, key, make):
+    """cache[key], made by make() when missing; the most recently used entries within WROWS_BYTES are kept
+    (basal/readout.py:23-36)."""
+    w = cache.pop(key, None)
+    if w is None:
+        w = make()
+    cache[key] = w
+    total = sum(_nbytes(x) for x in cache.values())
+    for old in list(cache):
+        if total <= WROWS_BYTES or old == key:
+            break
+        total -= _nbytes(cache.pop(old))
+    return w
+
+
+def capped(z, softcap):
+    """The model's final logit soft cap (Gemma: softcap x tanh(z / softcap)), applied once; none: z as it is."""
+    return torch.tanh(z / softcap) * softcap if softcap else z
+
+
+class CodeReadout:
+    """The code readout of one output head (an nn.Linear-like module: weight [vocab, D], optional bias) and soft cap."""
+
+    def __init__(self, head, softcap=None, cache=None, to_dev=None):
+        self.head, self.softcap = head, softcap
+        self.cache = {} if cache is None else cache
+        self.to_dev = to_dev or (lambda x: x.to(head.weight.device))
+
+    def rows(self, lids):
+        key = tuple(sorted({i for ids in lids for i in ids}))
+
+        def make():
+            return self.to_dev(torch.tensor(key, dtype=torch.int64)), None
+        rows = code_rows(self.cache, key, make)
+        col = {t: j for j, t in enumerate(key)}
+        K = max(map(len, lids))
+        idx = self.to_dev(torch.tensor([[col[i] for i in ids] + [0] * (K - len(ids)) for ids in lids]))
+        pad = self.to_dev(torch.tensor([[False] * len(ids) + [True] * (K - len(ids)) for ids in lids]))
+        return rows, idx, pad
+
+    def logits(self, h, rows):
+        ids, _ = rows
+        b = getattr(self.head, "bias", None)
+        return ops.code_logits(h, self.head.weight, ids, b, float(self.softcap or 0.0))
+
+    @staticmethod
+    def probs_of(z, idx, pad):
+        """Code logits [n, k] -> each prompt's probabilities over its codes [n, K] (padding 0), as a tensor."""
+        return ops.code_probs(z, idx, pad)
+
+    def probs(self, h, lids):
+        rows, idx, pad = self.rows(lids)
+        p = self.probs_of(self.logits(h, rows), idx, pad).tolist()  # one device sync
+        return [row[: len(ids)] for row, ids in zip(p, lids)]
+
+    def probs_each(self, h, lids):
+        """probs, each prompt as if read alone: the kernels' results do not depend on the other prompts, so this is
+        probs itself (basal/readout.py:86-104 reads each prompt with its own product for that guarantee)."""
+        return self.probs(h, lids)

@@ -1,0 +1,337 @@
+"""Benchmark of basal's quantised-linear hot path on B200: BASELINE config 2, one decoder layer's projection set with
+FP8-block W8A8 over 64 varlen-packed requests (lengths uniform in [128, 2048], seed 0), hidden 2048:
+qkv [2048 -> 5120], o [2048 -> 2048], gate/up [2048 -> 12288], down [6144 -> 2048].
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step = the four projections (activation quantiser + tcgen05 block GEMM each) over the packed rows. Metric:
+TFLOP/s (2 M N K summed over the projections), whole job: with N GPUs every rank serves its own 64 requests (row
+shards of independent requests, no collective; "weak" scaling) and the value is all ranks' FLOPs over the slowest
+rank's device time. One JSON line on rank 0 with, besides the contract keys:
+  roofline      the FP8 block GEMM (the dominant kernel): achieved TFLOP/s from CUDA events around its launches in
+                the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200)
+  e2e           the same metric through the public API (BlockFP8Linear modules) from pinned host memory: the H2D copy
+                of the step's activations and the D2H copy of its four outputs inside the timed region
+  cpu_baseline  the reference's CPU maths (oracle/, numpy + BLAS on all host threads) on a bounded sample of rows
+  clocks        nvidia-smi samples taken during the timed region
+--impl reference times the reference's CPU implementation of the path (the oracle port) on this box's host cores
+(the reference has no native code and no GPU path of its own for B200 besides Triton), rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "block-scaled GEMM TFLOP/s (% tcgen05 peak); decisions/s at 1/2/4/8 B200"
+PROJ = (("qkv", 5120, 2048), ("o", 2048, 2048), ("gate_up", 12288, 2048), ("down", 2048, 6144))
+HIDDEN, INTER = 2048, 6144
+WORKLOAD = ("C2: one decoder layer's projection set, FP8-block W8A8, 64 varlen-packed requests (lengths U[128,2048], "
+            "seed 0), qkv 2048->5120, o 2048->2048, gate/up 2048->12288, down 6144->2048")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+PROFILE = os.path.join(ROOT, "profiles", "fp8_block_gemm_c2.txt")
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS, bf16_tflops_sustained=FALLBACK_PEAKS["bf16_tflops"], source="fallback")
+
+
+def profiled_traffic():
+    """DRAM bytes per GEMM launch of the committed ncu summary (its 'traffic_bytes_per_launch:' line), or None."""
+    try:
+        with open(PROFILE) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def workload_rows():
+    from basal_b200.shard import varlen_lengths
+    return int(varlen_lengths(64, 128, 2048, seed=0).sum())
+
+
+def flops_per_row():
+    return sum(2 * n * k for _, n, k in PROJ)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples every 100 ms while running (started before, stopped after the timed
+    region)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc = index, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(", ") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# CPU: the reference's maths (oracle port), a bounded sample of rows
+# ------------------------------------------------------------------------------------------------------------------
+def cpu_sample(rows, seed=0):
+    """Seeded bf16-valued activations of `rows` tokens and the four quantised weights, as numpy (oracle inputs)."""
+    import numpy as np
+    from oracle import blockquant as obq
+    rng = np.random.default_rng(seed)
+    bf = lambda a: (a.astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)  # noqa: E731 (truncate)
+    xs = {HIDDEN: bf(rng.standard_normal((rows, HIDDEN))), INTER: bf(rng.standard_normal((rows, INTER)))}
+    ws = {name: obq.quantize(rng.standard_normal((n, k)).astype(np.float32) * np.float32(0.02), "fp8")
+          for name, n, k in PROJ}
+    return xs, ws
+
+
+def cpu_step(xs, ws):
+    """One step of the reference's CPU path: per projection, act_quant_ops + reference() (both operands dequantised
+    every call, an fp32 matmul), as fp8block.linear runs on CPU tensors (basal/fp8block.py:285-296)."""
+    from oracle import blockquant as obq
+    out = []
+    for name, n, k in PROJ:
+        q, s = ws[name]
+        out.append(obq.linear(xs[k], q, s, "fp8"))
+    return out
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def cpu_baseline(rows=1024, reps=3):
+    xs, ws = cpu_sample(rows)
+    cpu_step(xs, ws)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        cpu_step(xs, ws)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(rows * flops_per_row() / t / 1e12, 4), "unit": "TFLOP/s", "cores": blas_threads(),
+            "kind": "port", "sample": f"{rows} rows of the C2 workload through the 4 projections, median of {reps} "
+                                      f"steps ({t:.2f} s a step)"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    rows = 256
+    xs, ws = cpu_sample(rows)
+    for _ in range(args.warmup):
+        cpu_step(xs, ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(xs, ws)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = rows * flops_per_row() / dt / 1e12
+    cores = blas_threads()
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e4m3 (dequantised to fp32 on the CPU)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "rows_per_step": rows, "parallelism": "rank 0 only, host cores"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows} rows of the C2 workload through the 4 projections each step"},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# GPU
+# ------------------------------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import basal_b200 as b2
+    from basal_b200 import shard
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M = workload_rows()
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)  # each rank serves its own requests
+    xs = {HIDDEN: torch.randn(M, HIDDEN, device=dev, generator=g).bfloat16(),
+          INTER: torch.randn(M, INTER, device=dev, generator=g).bfloat16()}
+    mods = {}
+    for name, n, k in PROJ:
+        lin = torch.nn.Linear(k, n, bias=False, device=dev)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, 0.02, generator=g)
+        mods[name] = b2.fp8block.BlockFP8Linear.of(lin)
+        del lin
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        outs = []
+        for i, (name, n, k) in enumerate(PROJ):
+            m = mods[name]
+            q, s = b2.ops.fp8_act_quant(xs[k])
+            if ev is not None:
+                ev[i][0].record(stream)
+            outs.append(b2.ops.fp8_block_gemm(q, s, m.weight, m.weight_scale, torch.bfloat16))
+            if ev is not None:
+                ev[i][1].record(stream)
+        return outs
+
+    for _ in range(args.warmup):
+        step()
+    K = args.steps
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in PROJ]
+           for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    shard.check_peers(tag="timed")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for i in range(K):
+            step(evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / K
+    ms_max = shard.max_over_ranks(ms)
+    gemm_ms = [sum(evs[i][j][0].elapsed_time(evs[i][j][1]) for i in range(K)) / K for j in range(len(PROJ))]
+    total_rows = shard.sum_over_ranks(M)
+    value = total_rows * flops_per_row() / (ms_max * 1e-3) / 1e12
+
+    # end to end through the public API: pinned host activations in, the four outputs back to pinned host memory
+    hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    hy = {name: torch.empty(M, n, dtype=torch.bfloat16).pin_memory() for name, n, _ in PROJ}
+    h2d = sum(t.numel() * t.element_size() for t in hx.values())
+    d2h = sum(t.numel() * t.element_size() for t in hy.values())
+    dx = {k: torch.empty_like(v, device=dev) for k, v in hx.items()}
+
+    def e2e_step():
+        for k in hx:
+            dx[k].copy_(hx[k], non_blocking=True)
+        for name, n, k in PROJ:
+            hy[name].copy_(mods[name](dx[k]), non_blocking=True)
+
+    e2e_steps = max(1, min(K, 20))
+    for _ in range(2):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = shard.max_over_ranks(s2.elapsed_time(e2) / e2e_steps)
+    e2e_value = total_rows * flops_per_row() / (e2e_ms * 1e-3) / 1e12
+
+    clocks = clk.summary()
+    pk = peaks()
+    gemm_flops = sum(2 * M * n * k for _, n, k in PROJ)
+    achieved = gemm_flops / (sum(gemm_ms) * 1e-3) / 1e12
+    peak = 2.0 * pk["bf16_tflops"]
+    traffic = profiled_traffic()
+    if rank == 0:
+        cpu = cpu_baseline() if world == 1 else None
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e4m3", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": {"workload": WORKLOAD, "rows_per_rank": M, "total_rows": int(total_rows),
+                       "parallelism": f"{world} row-sharded replicas, no collective",
+                       "l2": "inputs larger than L2 (285 MB + 855 MB activations a step), no flush"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "basal200 fp8 block GEMM (tcgen05 kind::f8f6f4)",
+                         "peak_source": f"2 x bf16_tflops of {pk['source']} peaks (FP8 dense = 2 x bf16 dense)",
+                         "per_projection_tflops": {name: round(2 * M * n * k / (t * 1e-3) / 1e12, 1)
+                                                   for (name, n, k), t in zip(PROJ, gemm_ms)}},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": "BlockFP8Linear.forward on pinned host activations, outputs copied back"},
+            "gpu_launches": 2 * len(PROJ) * K,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,141 @@
+/* libbasal200: the C ABI of basal's quantised-linear hot path on B200 (sm_100a).
+ *
+ * Every entry point takes device pointers, sizes and a cudaStream_t (passed as void*; NULL = the legacy default
+ * stream), enqueues its kernels on that stream and returns a status code. None allocates memory, synchronises the
+ * stream or reads device data on the host, so a CUDA graph can capture any of them. Buffers are dense row-major
+ * ("contiguous"); the 16-byte alignment of every base pointer is checked.
+ *
+ * Citations are to the reference, rkinas/basal 2.8.1 (path:line within that project).
+ */
+#ifndef BASAL200_H
+#define BASAL200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+enum {
+  BASAL200_OK = 0,
+  BASAL200_ERR_ARG = 1,     /* a NULL pointer or a negative size */
+  BASAL200_ERR_SHAPE = 2,   /* a size the format cannot take, e.g. N % 128 != 0 (basal/blockquant.py:38-39) */
+  BASAL200_ERR_ALIGN = 3,   /* a base pointer not 16-byte aligned */
+  BASAL200_ERR_DTYPE = 4,   /* an unsupported dtype code */
+  BASAL200_ERR_ARCH = 5,    /* the current device is not compute capability 10.0 (sm_100a) */
+  BASAL200_ERR_LAUNCH = 6,  /* a CUDA error at launch */
+  BASAL200_ERR_TMAP = 7,    /* cuTensorMapEncodeTiled refused a TMA descriptor */
+  BASAL200_ERR_LIMIT = 8    /* a size beyond what the entry point was built for */
+};
+
+/* Element type codes of activations, outputs and biases. */
+enum { BASAL200_BF16 = 0, BASAL200_F16 = 1, BASAL200_F32 = 2 };
+
+/* ---- FP8-block / INT8-block (128 x 128 weight blocks, 1 x 128 activation groups, fp32 scales) ---- */
+
+/* x [M, K] (x_dtype) -> q [M, K] e4m3 codes, s [M, K/128] fp32. K % 128 == 0. Bit-exact to
+ * BlockFormat.act_quant_ops of the FP8 format (basal/blockquant.py:118-123, :137-144; fp8block.py:241-242). */
+int basal200_fp8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, uint8_t* q, float* s, void* stream);
+
+/* The INT8 format (int8block.py:349-350): q int8, round half to even, +-127. */
+int basal200_int8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* q, float* s, void* stream);
+
+/* w [N, K] (w_dtype) -> q [N, K] e4m3, s [N/128, K/128] fp32. Bit-exact to BlockFormat.quantize
+ * (basal/blockquant.py:126-135) of the FP8 format. N % 128 == 0, K % 128 == 0. */
+int basal200_fp8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* q, float* s,
+                                void* stream);
+
+/* The INT8 format of the same (int8block.py:349-350). */
+int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* q, float* s,
+                                 void* stream);
+
+/* C [M, N] (c_dtype) = sum over 128-deep K slices of (q_kb . w_kb^T) * s[m, kb] * ws[n/128, kb], fp32 accumulation,
+ * then + bias[n] (c_dtype, may be NULL) rounded as torch adds a bias to the cast output. Replaces the torch op
+ * basal::fp8_block_gemm (basal/blockquant.py:151-159, kernel :63-106). N % 128 == 0, K % 128 == 0; M may be 0. */
+int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
+                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:349): each slice's product exact in int32. */
+int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
+                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* The whole linear: act_quant of x into the caller's scratch (q_scratch [M, K] bytes, s_scratch [M, K/128] fp32),
+ * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias. Replaces fp8block.linear / BlockFormat.linear
+ * (basal/fp8block.py:285-296, basal/blockquant.py:175-183) and the op basal::fp8_block_linear_sm90
+ * (fp8block.py:272-277). */
+int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,
+                              void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
+                              void* stream);
+
+/* int8block.linear (int8block.py:350 = BlockFormat.linear, basal/blockquant.py:175-183). */
+int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, const float* ws, const void* bias,
+                               void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
+                               void* stream);
+
+/* ---- NVFP4 (e2m1 values, e4m3 scales per 16 features in the 128 x 4 swizzle, fp32 global scales) ---- */
+
+/* x [M, K] -> q [Mp, K/2] packed e2m1 (even feature in the low nibble), s [Mp * K/16] swizzled e4m3 scales,
+ * Mp = M rounded up to 128, padding rows zero; inv_g [1] fp32 on the device. K % 64 == 0. Bit-exact to the
+ * reference's quantiser (basal/nvfp4.py:115-158; its maths nvfp4.py:106-112). */
+int basal200_nvfp4_act_quant(const void* x, int x_dtype, const float* inv_g, int64_t M, int64_t K, uint8_t* q,
+                             uint8_t* s, void* stream);
+
+/* y [M, N] (y_dtype) = alpha[0] * (dequantised q [Mp, K/2] . dequantised w [N, K/2]^T), + bias. The scales s and ws
+ * in the 128 x 4 swizzle, ws covering ceil(N/128)*128 rows. Replaces nvfp4._mm (basal/nvfp4.py:167-180, cuBLAS
+ * through F.scaled_mm). K % 64 == 0, N % 16 == 0. */
+int basal200_nvfp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t* ws, const float* alpha,
+                        const void* bias, void* y, int y_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* The op basal::nvfp4_linear (basal/nvfp4.py:183-189): act_quant into the scratch (q_scratch [Mp, K/2],
+ * s_scratch [Mp * K/16]) then the GEMM into y [M, N] (y_dtype = x_dtype), + bias. */
+int basal200_nvfp4_linear(const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, const float* alpha,
+                          const float* inv_g, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                          uint8_t* q_scratch, uint8_t* s_scratch, void* stream);
+
+/* w [N, K] -> codes [N, K/2], swizzled scales [ceil(N/128)*128 * ceil(K/64)*4] (zero padded), g [1] fp32 global
+ * scale. Bit-exact to nvfp4.quantize (basal/nvfp4.py:75-97): 8 candidate scales per 16-block by least squares.
+ * Any N; K % 16 == 0 (the GEMM itself needs K % 64 == 0 and N % 16 == 0, nvfp4.fits). */
+int basal200_nvfp4_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* codes, uint8_t* scales,
+                            float* g, void* stream);
+
+/* ---- Option-code readout ---- */
+
+/* z [R, U] fp32 = h [R, D] (h_dtype, row stride ldh elements) . head[ids[u], :]^T (+ bias[ids[u]]), then
+ * softcap * tanh(z / softcap) when softcap > 0. head [V, D] bf16, fp16 or fp32 (row stride ldw), ids [U] int64
+ * into it, bias [V] (bias_dtype) or NULL. An id outside [0, V) reads nothing: its logits are NaN and the fault bit
+ * BASAL200_FAULT_BAD_ID is set. Replaces CodeReadout.rows + .logits (basal/readout.py:57-74): the option rows are
+ * read straight from the head, never copied. */
+int basal200_code_logits(const void* h, int h_dtype, int64_t R, int64_t D, int64_t ldh, const void* head,
+                         int head_dtype, int64_t V, int64_t ldw, const int64_t* ids, int64_t U, const void* bias,
+                         int bias_dtype, float softcap, float* z, void* stream);
+
+/* p [R, Kmax] fp32 = softmax over j of z[r, idx[r, j]] with -inf where pad[r, j] != 0 (the padding gets 0).
+ * Replaces CodeReadout.probs_of (basal/readout.py:76-79). Kmax <= 1024. */
+int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx, const uint8_t* pad, int64_t Kmax,
+                        float* p, void* stream);
+
+/* ---- Diagnostics ---- */
+
+/* Fault bits (basal200_device_faults): a bounded wait of a GEMM gave up (producer, MMA issuer, epilogue, drain), or a
+ * readout id was out of range. */
+enum {
+  BASAL200_FAULT_TIMEOUT_PRODUCER = 1,
+  BASAL200_FAULT_TIMEOUT_MMA = 2,
+  BASAL200_FAULT_TIMEOUT_EPILOGUE = 4,
+  BASAL200_FAULT_TIMEOUT_DRAIN = 8,
+  BASAL200_FAULT_BAD_ID = 16
+};
+
+/* The fault bits kernels on `device` recorded when a bounded wait gave up (0: none); clear != 0 resets them.
+ * Synchronises the device: for tests and error paths, not for the hot path. */
+unsigned basal200_device_faults(int device, int clear);
+
+const char* basal200_status_string(int status);
+int basal200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BASAL200_H */

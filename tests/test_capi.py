@@ -1,0 +1,76 @@
+"""The C ABI without a GPU: libbasal200.so loads, exports every entry point include/basal200.h declares, and the
+ctypes binding declares exactly those; status strings and argument checks that return before any device work."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "basal200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(basal200_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from basal_b200 import _lib
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared()
+    assert len(names) >= 17
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_binding_covers_the_header():
+    from basal_b200 import _lib
+    bound = set(_lib.SIGNATURES) | {"basal200_status_string", "basal200_version", "basal200_device_faults"}
+    assert bound == set(declared())
+
+
+def test_status_strings_and_version(lib):
+    assert lib.basal200_version() >= 1
+    assert lib.basal200_status_string(0) == b"ok"
+    assert b"shape" in lib.basal200_status_string(2)
+    assert lib.basal200_status_string(99) == b"unknown status"
+
+
+def test_argument_checks_before_device_work(lib):
+    """Sizes the format cannot take are refused before the library touches a device (status codes, no exit)."""
+    null = ctypes.c_void_p(0)
+    # K not a multiple of 128
+    assert lib.basal200_fp8_act_quant(null, 0, 4, 100, null, null, null) == 2
+    # negative M
+    assert lib.basal200_int8_act_quant(null, 0, -1, 128, null, null, null) == 1
+    # M = 0 is an empty success
+    assert lib.basal200_fp8_act_quant(null, 0, 0, 256, null, null, null) == 0
+    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 0, 256, 256, null) == 0
+    # N not a multiple of 128
+    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 4, 200, 256, null) == 2
+    # NVFP4: K % 64
+    assert lib.basal200_nvfp4_act_quant(null, 0, null, 4, 96, null, null, null) == 2
+    # readout: Kmax beyond 1024
+    assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
+
+
+def test_header_is_plain_c():
+    """The header compiles as C (no torch or C++ types in the signatures)."""
+    import shutil
+    import subprocess
+    import tempfile
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no gcc")
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "t.c")
+        with open(src, "w") as f:
+            f.write("#include \"basal200.h\"\nint (*probe)(void) = basal200_version;\n")
+        subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), "-c", src, "-o",
+                        os.path.join(d, "t.o")], check=True)

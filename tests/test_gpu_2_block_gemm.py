@@ -1,0 +1,117 @@
+"""The tcgen05 block GEMM (FP8 kind::f8f6f4, INT8 kind::i8) against the oracle's maths (basal/blockquant.py:54-60),
+the reference's own GPU tests restated (tests/test_fp8block.py:211-225, tests/test_int8block.py:308-321: the maths
+within 2e-3 (FP8) / 1e-5 (INT8), a row's output bit-identical alone and among other rows), the bf16 output within
+1e-2 relative, the edge cases (M = 0, partial tiles, N % 256 = 128, bias) and the full
+C2 projection shapes through row samples."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import blockquant as obq
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp8": 2e-3, "int8": 1e-5}
+
+
+@pytest.fixture(scope="module")
+def b2():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import basal_b200
+    return basal_b200
+
+
+def mod(b2, fmt):
+    return b2.fp8block if fmt == "fp8" else b2.int8block
+
+
+def operands(b2, fmt, M, N, K, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    w = (torch.randn(N, K, generator=g) / 32).cuda()
+    m = mod(b2, fmt)
+    q, s = m.quantize(w)
+    qa, sa = m.act_quant(x)
+    return x, q, s, qa, sa
+
+
+def oracle_y(fmt, qa, sa, q, s):
+    c = lambda t: t.view(torch.uint8).cpu().numpy() if fmt == "fp8" else t.cpu().numpy()  # noqa: E731
+    return obq.gemm(c(qa), sa.cpu().numpy(), c(q), s.cpu().numpy(), fmt)
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M, N, K", [(128, 256, 128), (1, 256, 128), (37, 768, 1024), (128, 768, 1024),
+                                     (1000, 768, 1024), (300, 384, 256), (129, 128, 512)])
+def test_gemm_equals_the_maths(b2, fmt, M, N, K):
+    x, q, s, qa, sa = operands(b2, fmt, M, N, K, seed=M + N + K)
+    y = mod(b2, fmt).gemm(qa, sa, q, s, torch.float32)
+    ref = oracle_y(fmt, qa, sa, q, s)
+    got = y.cpu().numpy()
+    assert np.allclose(got, ref, rtol=TOL[fmt], atol=TOL[fmt]), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M", [1, 37, 128, 1000])
+def test_kernel_ignores_the_other_rows(b2, fmt, M):
+    """tests/test_fp8block.py:211-225: a row's output alone and among other rows, bit for bit."""
+    x, q, s, qa, sa = operands(b2, fmt, M, 768, 1024)
+    m = mod(b2, fmt)
+    alone = m.gemm(qa[-1:], sa[-1:], q, s, torch.bfloat16)
+    many = m.gemm(torch.cat([qa, qa]), torch.cat([sa, sa]), q, s, torch.bfloat16)
+    assert torch.equal(alone[0], many[M - 1]) and torch.equal(many[M - 1], many[2 * M - 1])
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+def test_bf16_linear_within_north_star_tolerance(b2, fmt):
+    """linear (act_quant + GEMM, bf16 out) against the oracle's linear: 1e-2 relative."""
+    M, N, K = 517, 1280, 2048
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = torch.randn(N, generator=g).bfloat16()
+    m = mod(b2, fmt)
+    q, s = m.quantize(w.cuda())
+    y = m.linear(x.cuda(), q, s, bias.cuda())
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    qc = q.view(torch.uint8).cpu().numpy() if fmt == "fp8" else q.cpu().numpy()
+    ref = obq.linear(x.float().numpy(), qc, s.cpu().numpy(), fmt)
+    ref = torch.from_numpy(ref).bfloat16().float() + bias.float()  # the bias added to the cast output
+    err = (y.float().cpu() - ref).abs().max() / ref.abs().max()
+    assert err < 1e-2, err
+
+
+def test_empty_rows_and_refusals(b2):
+    x, q, s, qa, sa = operands(b2, "fp8", 4, 256, 256)
+    y = b2.fp8block.gemm(qa[:0], sa[:0], q, s, torch.bfloat16)
+    assert y.shape == (0, 256)
+    assert b2.fp8block.linear(x[:0], q, s).shape == (0, 256)
+    with pytest.raises(ValueError, match="not a multiple of 128"):
+        b2.blockquant.grid(4, 200)
+    with pytest.raises(ValueError):
+        b2.fp8block.gemm(qa, sa, q[:200], s[:2], torch.bfloat16)
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("name, N, K", [("qkv", 5120, 2048), ("o", 2048, 2048), ("gate_up", 12288, 2048),
+                                        ("down", 2048, 6144)])
+def test_c2_projection_shapes_by_row_samples(b2, fmt, name, N, K):
+    """The config-2 projections at a packed M of 8,320 rows: 64 sampled rows against the oracle (within the
+    north-star 1e-2 of each row's largest output) and the sampled rows recomputed alone, bit for bit."""
+    M = 8320
+    g = torch.Generator().manual_seed(N + K)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    w = (torch.randn(N, K, generator=g) * 0.02).cuda()
+    m = mod(b2, fmt)
+    q, s = m.quantize(w)
+    y = m.linear(x, q, s)
+    rows = torch.randperm(M, generator=g)[:64].sort().values
+    qa, sa = m.act_quant(x[rows.cuda()])
+    qc = q.view(torch.uint8).cpu().numpy() if fmt == "fp8" else q.cpu().numpy()
+    qac = qa.view(torch.uint8).cpu().numpy() if fmt == "fp8" else qa.cpu().numpy()
+    ref = obq.gemm(qac, sa.cpu().numpy(), qc, s.cpu().numpy(), fmt)
+    got = y[rows.cuda()].float().cpu().numpy()
+    err = np.abs(got - ref).max(1) / np.abs(ref).max(1)
+    assert err.max() < 1e-2, err.max()
+    assert torch.equal(m.linear(x[rows.cuda()], q, s), y[rows.cuda()])

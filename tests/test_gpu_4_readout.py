@@ -1,0 +1,78 @@
+"""The readout kernels (basal::code_logits, basal::code_probs) against the reference's golden probabilities and the
+oracle (basal/readout.py:57-104): golden to 1e-5, the C4 shapes (R = 256 answer positions, D = 2048, a 151,936-row
+bf16 head, 2 / 8 / 64 / 255 options) with identical argmax and max |diff| <= 1e-3 (checked here
+at 1e-5), and a prompt's probabilities the same bits alone and in any batch."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import readout as oro
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def b2():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import basal_b200
+    return basal_b200
+
+
+class Head(torch.nn.Module):
+    def __init__(self, w, b=None):
+        super().__init__()
+        self.weight = torch.nn.Parameter(w, requires_grad=False)
+        self.bias = None if b is None else torch.nn.Parameter(b, requires_grad=False)
+
+
+@pytest.mark.parametrize("tag, cap, bias", [("cap", 30.0, True), ("plain", None, False)])
+def test_golden(b2, tag, cap, bias):
+    g = golden("readout")
+    lids = [[int(i) for i in row if i >= 0] for row in g["lids"]]
+    w = torch.from_numpy(g["head_w"]).bfloat16().cuda()
+    b = torch.from_numpy(g["head_b"]).bfloat16().cuda() if bias else None
+    r = b2.readout.CodeReadout(Head(w, b), softcap=cap)
+    h = torch.from_numpy(g["h"]).cuda()
+    for fn, key in ((r.probs, "probs"), (r.probs_each, "probs_each")):
+        got = fn(h, lids)
+        for row, ids, want in zip(got, lids, g[f"{key}_{tag}"]):
+            assert np.allclose(row, want[: len(ids)], atol=1e-5)
+
+
+@pytest.fixture(scope="module")
+def c4_head():
+    g = torch.Generator().manual_seed(0)
+    w = (torch.randn(151936, 2048, generator=g) * 0.02).bfloat16()
+    h = torch.randn(256, 2048, generator=g).bfloat16()
+    return w, h
+
+
+@pytest.mark.parametrize("k", [2, 8, 64, 255])
+@pytest.mark.parametrize("cap", [None, 30.0])
+def test_c4_shapes(b2, c4_head, k, cap):
+    w, h = c4_head
+    g = torch.Generator().manual_seed(k)
+    ids = torch.randperm(151936, generator=g)[:k].tolist()
+    lids = [ids] * 256
+    r = b2.readout.CodeReadout(Head(w.cuda()), softcap=cap)
+    got = np.asarray(r.probs(h.cuda(), lids))
+    rows = w[ids].float().numpy()
+    ref = oro.softmax(oro.logits(h.float().numpy(), (rows, None), cap))
+    assert np.array_equal(got.argmax(1), ref.argmax(1))
+    assert np.abs(got - ref).max() <= 1e-5
+
+
+def test_batch_invariance(b2, c4_head):
+    """Per-row code sets whose union is <= 255: each prompt's probabilities read alone are the same bits."""
+    w, h = c4_head
+    g = torch.Generator().manual_seed(9)
+    pool = torch.randperm(151936, generator=g)[:255].tolist()
+    lids = [pool[i % 200: i % 200 + 2 + i % 9] for i in range(64)]
+    r = b2.readout.CodeReadout(Head(w.cuda()), softcap=30.0)
+    hh = h[:64].cuda()
+    batch = r.probs(hh, lids)
+    assert batch == r.probs_each(hh, lids)
+    for i in (0, 5, 63):
+        assert r.probs(hh[i:i + 1], [lids[i]])[0] == batch[i]
