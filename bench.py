@@ -303,13 +303,54 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+CASES = {
+    # name: (format, M, N, K) -- the small cases the committed ncu summaries were captured on (inputs > L2, a few
+    # GB on the device): 2 untimed launches, then 3 launches of the kernel under study
+    "fp8_gemm": ("fp8", 65536, 5120, 2048),
+    "int8_gemm": ("int8", 65536, 5120, 2048),
+    "fp8_act_quant": ("fp8", 65536, 0, 2048),
+    "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
+}
+
+
+def run_case(name):
+    import torch
+
+    import basal_b200 as b2
+    fmt, M, N, K = CASES[name]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+    if N == 0:
+        for _ in range(5):
+            b2.fp8block.act_quant(x)
+    elif fmt == "nvfp4":
+        lin = torch.nn.Linear(K, N, bias=False, device=dev)
+        f = b2.nvfp4.NVFP4Linear.of(lin, float(x.abs().max()))
+        q, s = b2.nvfp4.act_quant(x, f.inv_g)
+        for _ in range(5):
+            torch.ops.basal.nvfp4_gemm(q, s, f.weight, f.weight_scale.view(torch.uint8), f.alpha, M, torch.bfloat16)
+    else:
+        mod = b2.fp8block if fmt == "fp8" else b2.int8block
+        q, s = mod.quantize(torch.randn(N, K, device=dev, generator=g) * 0.02)
+        qa, sa = mod.act_quant(x)
+        for _ in range(5):
+            mod.gemm(qa, sa, q, s, torch.bfloat16)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "M": M, "N": N, "K": K, "faults": b2._lib.device_faults(0)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
