@@ -31,6 +31,7 @@ SIGNATURES = {
     "basal200_int8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
     "basal200_fp8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
     "basal200_int8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
+    "basal200_fp8_block_linear_noalloc": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "basal200_nvfp4_act_quant": [_P, _I, _P, _I64, _I64, _P, _P, _P],
     "basal200_nvfp4_gemm": [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
     "basal200_nvfp4_linear": [_P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],

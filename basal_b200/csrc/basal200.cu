@@ -2,6 +2,7 @@
 // kernel of the library (the device fault word is shared by all of them).
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "block_gemm.cuh"
@@ -342,6 +343,38 @@ int logits_head(const TH* h, int64_t R, int64_t D, int64_t ldh, const void* head
 }
 
 }  // namespace
+
+// ------------------------------------------------------------------------------------------------------------
+// Allocation-free FP8-block linear: the activation codes and scales live in one file-scope device array instead of
+// caller scratch. The array is part of the loaded module, so every GPU that loads the library holds its
+// 16.5 MiB until the process exits; all calls on a device share it.
+// ------------------------------------------------------------------------------------------------------------
+constexpr int64_t kNoAllocMaxElems = BASAL200_NOALLOC_MAX_ELEMS;              // M * K activation values at most
+constexpr size_t kNoAllocCodeBytes = (size_t)kNoAllocMaxElems;                // e4m3 codes, one byte each
+constexpr size_t kNoAllocScaleBytes = (size_t)(kNoAllocMaxElems / 128) * 4;  // one fp32 scale per 128 values
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocCodeBytes + kNoAllocScaleBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[kMaxDevices];  // the array's device address, per device ordinal (null: not set up yet)
+
+// Host code may not take the array's address itself (on the host the symbol is only a stand-in): the runtime
+// translates it, once per device, with that device current.
+int noalloc_scratch(int dev, uint8_t** q, float** s) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return BASAL200_ERR_LAUNCH;
+    }
+    g_noalloc_base[dev] = p;
+  }
+  *q = static_cast<uint8_t*>(g_noalloc_base[dev]);
+  *s = reinterpret_cast<float*>(static_cast<uint8_t*>(g_noalloc_base[dev]) + kNoAllocCodeBytes);
+  return BASAL200_OK;
+}
+}  // namespace
 }  // namespace b200
 
 using namespace b200;
@@ -394,6 +427,25 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
   int rc = act_quant<true>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
   if (rc) return rc;
   return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+}
+
+// The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing
+// there needs clearing between calls: the quantiser writes every code and scale the GEMM then reads, and rows past M
+// are zero-filled by the GEMM's TMA loads, never read from the array.
+int basal200_fp8_block_linear_noalloc(const void* x, int x_dtype, const uint8_t* w, const float* ws,
+                                      const void* bias, void* y, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M < 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
+  if (M > kNoAllocMaxElems / K) return BASAL200_ERR_LIMIT;
+  if (M == 0) return BASAL200_OK;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  uint8_t* q = nullptr;
+  float* s = nullptr;
+  if ((rc = noalloc_scratch(dev, &q, &s))) return rc;
+  rc = act_quant<false>(x, x_dtype, M, K, q, s, as_stream(stream));
+  if (rc) return rc;
+  return block_gemm<false>(q, s, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
 }
 
 int basal200_nvfp4_act_quant(const void* x, int x_dtype, const float* inv_g, int64_t M, int64_t K, uint8_t* q,

@@ -73,6 +73,20 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                void* stream);
 
+/* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
+#define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)
+
+/* basal200_fp8_block_linear without caller scratch, for callers that cannot allocate device memory: a runtime whose
+ * device memory is planned up front in a fixed arena, a host language that holds no device allocator of its own, a
+ * caller that must not let cudaMalloc synchronise the device mid-request. The activation codes and scales go to an
+ * array inside the library (16 MiB + 512 KiB, BASAL200_NOALLOC_MAX_ELEMS values), which every GPU that loads the
+ * library holds until the process exits. M * K above that limit returns BASAL200_ERR_LIMIT before any work. The
+ * call allocates nothing. Its first call on a device looks up the array's address on that device (with the device
+ * current): make that first call before any stream capture. All calls on a device share the array, so calls that
+ * overlap on the GPU (other streams, other threads) race on it; serialise them. No counterpart in the reference. */
+int basal200_fp8_block_linear_noalloc(const void* x, int x_dtype, const uint8_t* w, const float* ws,
+                                      const void* bias, void* y, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* ---- NVFP4 (e2m1 values, e4m3 scales per 16 features in the 128 x 4 swizzle, fp32 global scales) ---- */
 
 /* x [M, K] -> q [Mp, K/2] packed e2m1 (even feature in the low nibble), s [Mp * K/16] swizzled e4m3 scales,
