@@ -9,10 +9,12 @@
 //   warp 1      MMA issuer: 4 x tcgen05.mma (K = 32 each) per slice into one of two TMEM accumulators of 256
 //               columns (kind::f8f6f4 e4m3 -> f32, or kind::i8 s8 -> s32, exact for a 128-deep slice)
 //   warp 2      TMEM allocation (512 columns) and release
-//   warps 4-11  promotion: per slice, tcgen05.ld of the slice's product, times a_s * b_s, added into fp32 registers
-//               (128 columns a thread); after the last slice, the cast (and bias) and the stores to C
-// The MMA of slice kb + 1 runs while the promotion reads slice kb from the other accumulator. A row's result never
-// depends on the other rows (no split of K, the same slice order for every M).
+//   warps 4-11  promotion: per slice, tcgen05.ld of the slice's product (64 columns in flight per wait), times
+//               a_s * b_s, added into fp32 registers with packed f32x2 FMAs (128 columns a thread); after the last
+//               slice, the cast (and bias) and the stores to C
+// The MMA of slice kb + 1 runs while the promotion reads slice kb from the other accumulator. The producer warpgroup
+// gives registers to the promotion warpgroups (setmaxnreg: 40 / 232 of the 168 a thread at launch). A row's result
+// never depends on the other rows (no split of K, the same slice order for every M).
 #pragma once
 #include "quant.cuh"
 
@@ -30,6 +32,12 @@ constexpr int NUM_THREADS = 384;
 constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 512;
+// setmaxnreg split: 128 producer-warpgroup threads at REGS_LOW, 256 promotion threads at REGS_HIGH; the launch must
+// hold LAUNCH_REGS a thread (checked on the host before every first launch: a split beyond the launch's registers
+// would wait forever)
+constexpr uint32_t REGS_LOW = 40, REGS_HIGH = 232;
+constexpr uint32_t LAUNCH_REGS = (REGS_LOW * 128 + REGS_HIGH * 256) / NUM_THREADS;
+static_assert(REGS_LOW * 128 + REGS_HIGH * 256 <= LAUNCH_REGS * NUM_THREADS, "register split");
 
 struct Shared {
   uint8_t a[STAGES][A_BYTES];
@@ -162,6 +170,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = sh.tmem_base;
   volatile int* abort_flag = &sh.abort;
 
+  if (warp < EPI_WARP0) regs_release<REGS_LOW>();
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -233,6 +242,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp >= EPI_WARP0) {
     // ---------------- promotion and epilogue ----------------
+    regs_claim<REGS_HIGH>();
     using OutT = typename Store<OUT>::T;
     const int ew = warp - EPI_WARP0;
     const int half = ew >> 2;   // which 128 columns of the 256-wide tile
@@ -247,12 +257,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool nvalid = n0 < p.N;
       const float* srow = p.s + (int64_t)min(row, p.M - 1) * nkb;
       const float* wsr = p.ws + (int64_t)min(n0 / 128, p.N / 128 - 1) * nkb;
-      float acc[128];
+      uint64_t acc[64];  // 128 fp32 accumulators as packed pairs
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < 64; ++i) acc[i] = 0ull;
       float sa = __ldg(srow), sb = __ldg(wsr);
       for (int kb = 0; kb < nkb; ++kb) {
         const float sc = sa * sb;
+        const uint64_t sc2 = pack_f2(sc, sc);
         if (kb + 1 < nkb) {
           sa = __ldg(srow + kb + 1);
           sb = __ldg(wsr + kb + 1);
@@ -265,26 +276,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + half * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c * 16, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float part = INT8 ? static_cast<float>(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
-            acc[c * 16 + j] = fmaf(part, sc, acc[c * 16 + j]);
+        for (int h = 0; h < 2; ++h) {  // 64 columns in flight per wait
+          uint64_t x[32];
+          tmem_ld64_pairs<INT8>(taddr + h * 64, x);
+          if (h == 1) {  // every read of this accumulator is done: hand it back to the MMA before the FMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.tempty[buf]);
           }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ffma2p(acc[h * 32 + j], x[j], sc2);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.tempty[buf]);
         ++acc_cnt;
       }
       if (ok && nvalid && row < p.M) {
         OutT* dst = reinterpret_cast<OutT*>(p.c) + (int64_t)row * p.N + n0;
         const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
 #pragma unroll
-        for (int c = 0; c < 128; c += 8) Store<OUT>::vec8(dst + c, acc + c, bias ? bias + c : nullptr);
+        for (int c = 0; c < 128; c += 8) {
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack_f2(acc[c / 2 + i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+          }
+          Store<OUT>::vec8(dst + c, v, bias ? bias + c : nullptr);
+        }
       }
     }
   }

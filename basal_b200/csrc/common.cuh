@@ -88,7 +88,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor, no multicast) and the plain bulk copy
+// clusters of two CTAs (the CTA pair of tcgen05 cta_group::2); every load targets one CTA only
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of `local` (an address of this CTA's shared memory) in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster. The pair exchanges no data through generic memory: copies
+// complete through the async proxy, TMEM reads are ordered by tcgen05.wait::ld and the tcgen05 fences, so the default
+// (CTA-scope) semantics suffice and the cheaper arrive is used.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Waits on a local barrier that the pair's other CTA (or its tcgen05 commits) arrives on: the plain bounded wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned fault) {
+  return mbar_wait(bar, parity, abort_flag, fault);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor, one destination CTA per copy) and the plain bulk copy
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -99,6 +132,48 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// The CTA-pair form: the copy lands in this CTA's shared memory and completes its bytes on `cluster_bar`, an mbarrier
+// of either CTA of the pair (here always the pair's leader). The data goes to this CTA only.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+
+// Tiled shared -> global store of one box (bulk-group completion), and its group bookkeeping.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the smem sources of every committed store group have been read (the buffer may be rewritten).
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until every committed store group has completed (its writes are visible).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// A named barrier that also ANDs a flag over its threads: every thread leaves with the same answer (so a group whose
+// members saw different outcomes of a bounded wait still takes the same branch afterwards).
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %3, 0;\n\tbarrier.red.and.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(threads), "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
 }
 
 // Contiguous global -> shared copy; both addresses 16-byte aligned, bytes a multiple of 16.
@@ -192,6 +267,43 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// CTA-pair forms. The MMA of a pair (M = 256: 128 rows in each CTA's TMEM, A rows from each CTA's shared memory,
+// B split along N between them) is issued by the pair's leader.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on the mbarrier at `cluster_bar` (a shared::cluster address: this CTA's or its pair's) once every tcgen05
+// operation this thread issued before has completed. One call per CTA to signal.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 // 32 lanes x 16 columns of 32 bits: thread i of the warp gets lane (quadrant base + i), columns taddr .. taddr+15.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -201,7 +313,74 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+// 32 lanes x 32 columns of 32 bits.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// packed fp32 pairs (sm_100 f32x2 arithmetic) and register reallocation between warpgroups
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ float2 unpack_f2(uint64_t v) {
+  float2 f;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(v));
+  return f;
+}
+
+// acc = {lo, hi} * s2 + acc, both lanes rounded once (fma.rn.f32x2).
+__device__ __forceinline__ void ffma2(uint64_t& acc, uint32_t lo, uint32_t hi, uint64_t s2) {
+  asm("{\n\t.reg .b64 t;\n\tmov.b64 t, {%1, %2};\n\tfma.rn.f32x2 %0, t, %3, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(lo), "r"(hi), "l"(s2));
+}
+
+// 64 consecutive TMEM columns of this warp's 32 lanes (two 32x32b.x32 loads, then the wait), returned as 32 packed
+// fp32 pairs (columns 2j, 2j+1) ready for f32x2 arithmetic; INT8: the s32 values are converted to fp32 first (exact
+// below 2^24). The loads, the wait and the packing are one asm block so that the pairs need no register moves.
+template <bool INT8>
+__device__ __forceinline__ void tmem_ld64_pairs(uint32_t taddr, uint64_t (&d)[32]) {
+  if (INT8) {
+    asm volatile("{\n\t.reg .b32 a0,a1,a2,a3,a4,a5,a6,a7,a8,a9,a10,a11,a12,a13,a14,a15,a16,a17,a18,a19,a20,a21,a22,a23,a24,a25,a26,a27,a28,a29,a30,a31,a32,a33,a34,a35,a36,a37,a38,a39,a40,a41,a42,a43,a44,a45,a46,a47,a48,a49,a50,a51,a52,a53,a54,a55,a56,a57,a58,a59,a60,a61,a62,a63;\n\ttcgen05.ld.sync.aligned.32x32b.x32.b32 {a0,a1,a2,a3,a4,a5,a6,a7,a8,a9,a10,a11,a12,a13,a14,a15,a16,a17,a18,a19,a20,a21,a22,a23,a24,a25,a26,a27,a28,a29,a30,a31}, [%32];\n\ttcgen05.ld.sync.aligned.32x32b.x32.b32 {a32,a33,a34,a35,a36,a37,a38,a39,a40,a41,a42,a43,a44,a45,a46,a47,a48,a49,a50,a51,a52,a53,a54,a55,a56,a57,a58,a59,a60,a61,a62,a63}, [%33];\n\ttcgen05.wait::ld.sync.aligned;\n\tcvt.rn.f32.s32 a0, a0;\n\tcvt.rn.f32.s32 a1, a1;\n\tcvt.rn.f32.s32 a2, a2;\n\tcvt.rn.f32.s32 a3, a3;\n\tcvt.rn.f32.s32 a4, a4;\n\tcvt.rn.f32.s32 a5, a5;\n\tcvt.rn.f32.s32 a6, a6;\n\tcvt.rn.f32.s32 a7, a7;\n\tcvt.rn.f32.s32 a8, a8;\n\tcvt.rn.f32.s32 a9, a9;\n\tcvt.rn.f32.s32 a10, a10;\n\tcvt.rn.f32.s32 a11, a11;\n\tcvt.rn.f32.s32 a12, a12;\n\tcvt.rn.f32.s32 a13, a13;\n\tcvt.rn.f32.s32 a14, a14;\n\tcvt.rn.f32.s32 a15, a15;\n\tcvt.rn.f32.s32 a16, a16;\n\tcvt.rn.f32.s32 a17, a17;\n\tcvt.rn.f32.s32 a18, a18;\n\tcvt.rn.f32.s32 a19, a19;\n\tcvt.rn.f32.s32 a20, a20;\n\tcvt.rn.f32.s32 a21, a21;\n\tcvt.rn.f32.s32 a22, a22;\n\tcvt.rn.f32.s32 a23, a23;\n\tcvt.rn.f32.s32 a24, a24;\n\tcvt.rn.f32.s32 a25, a25;\n\tcvt.rn.f32.s32 a26, a26;\n\tcvt.rn.f32.s32 a27, a27;\n\tcvt.rn.f32.s32 a28, a28;\n\tcvt.rn.f32.s32 a29, a29;\n\tcvt.rn.f32.s32 a30, a30;\n\tcvt.rn.f32.s32 a31, a31;\n\tcvt.rn.f32.s32 a32, a32;\n\tcvt.rn.f32.s32 a33, a33;\n\tcvt.rn.f32.s32 a34, a34;\n\tcvt.rn.f32.s32 a35, a35;\n\tcvt.rn.f32.s32 a36, a36;\n\tcvt.rn.f32.s32 a37, a37;\n\tcvt.rn.f32.s32 a38, a38;\n\tcvt.rn.f32.s32 a39, a39;\n\tcvt.rn.f32.s32 a40, a40;\n\tcvt.rn.f32.s32 a41, a41;\n\tcvt.rn.f32.s32 a42, a42;\n\tcvt.rn.f32.s32 a43, a43;\n\tcvt.rn.f32.s32 a44, a44;\n\tcvt.rn.f32.s32 a45, a45;\n\tcvt.rn.f32.s32 a46, a46;\n\tcvt.rn.f32.s32 a47, a47;\n\tcvt.rn.f32.s32 a48, a48;\n\tcvt.rn.f32.s32 a49, a49;\n\tcvt.rn.f32.s32 a50, a50;\n\tcvt.rn.f32.s32 a51, a51;\n\tcvt.rn.f32.s32 a52, a52;\n\tcvt.rn.f32.s32 a53, a53;\n\tcvt.rn.f32.s32 a54, a54;\n\tcvt.rn.f32.s32 a55, a55;\n\tcvt.rn.f32.s32 a56, a56;\n\tcvt.rn.f32.s32 a57, a57;\n\tcvt.rn.f32.s32 a58, a58;\n\tcvt.rn.f32.s32 a59, a59;\n\tcvt.rn.f32.s32 a60, a60;\n\tcvt.rn.f32.s32 a61, a61;\n\tcvt.rn.f32.s32 a62, a62;\n\tcvt.rn.f32.s32 a63, a63;\n\tmov.b64 %0, {a0, a1};\n\tmov.b64 %1, {a2, a3};\n\tmov.b64 %2, {a4, a5};\n\tmov.b64 %3, {a6, a7};\n\tmov.b64 %4, {a8, a9};\n\tmov.b64 %5, {a10, a11};\n\tmov.b64 %6, {a12, a13};\n\tmov.b64 %7, {a14, a15};\n\tmov.b64 %8, {a16, a17};\n\tmov.b64 %9, {a18, a19};\n\tmov.b64 %10, {a20, a21};\n\tmov.b64 %11, {a22, a23};\n\tmov.b64 %12, {a24, a25};\n\tmov.b64 %13, {a26, a27};\n\tmov.b64 %14, {a28, a29};\n\tmov.b64 %15, {a30, a31};\n\tmov.b64 %16, {a32, a33};\n\tmov.b64 %17, {a34, a35};\n\tmov.b64 %18, {a36, a37};\n\tmov.b64 %19, {a38, a39};\n\tmov.b64 %20, {a40, a41};\n\tmov.b64 %21, {a42, a43};\n\tmov.b64 %22, {a44, a45};\n\tmov.b64 %23, {a46, a47};\n\tmov.b64 %24, {a48, a49};\n\tmov.b64 %25, {a50, a51};\n\tmov.b64 %26, {a52, a53};\n\tmov.b64 %27, {a54, a55};\n\tmov.b64 %28, {a56, a57};\n\tmov.b64 %29, {a58, a59};\n\tmov.b64 %30, {a60, a61};\n\tmov.b64 %31, {a62, a63};\n\t}"
+                 : "=l"(d[0]), "=l"(d[1]), "=l"(d[2]), "=l"(d[3]), "=l"(d[4]), "=l"(d[5]), "=l"(d[6]), "=l"(d[7]), "=l"(d[8]), "=l"(d[9]), "=l"(d[10]), "=l"(d[11]), "=l"(d[12]), "=l"(d[13]), "=l"(d[14]), "=l"(d[15]), "=l"(d[16]), "=l"(d[17]), "=l"(d[18]), "=l"(d[19]), "=l"(d[20]), "=l"(d[21]), "=l"(d[22]), "=l"(d[23]), "=l"(d[24]), "=l"(d[25]), "=l"(d[26]), "=l"(d[27]), "=l"(d[28]), "=l"(d[29]), "=l"(d[30]), "=l"(d[31])
+                 : "r"(taddr), "r"(taddr + 32)
+                 : "memory");
+  } else {
+    asm volatile("{\n\t.reg .b32 a0,a1,a2,a3,a4,a5,a6,a7,a8,a9,a10,a11,a12,a13,a14,a15,a16,a17,a18,a19,a20,a21,a22,a23,a24,a25,a26,a27,a28,a29,a30,a31,a32,a33,a34,a35,a36,a37,a38,a39,a40,a41,a42,a43,a44,a45,a46,a47,a48,a49,a50,a51,a52,a53,a54,a55,a56,a57,a58,a59,a60,a61,a62,a63;\n\ttcgen05.ld.sync.aligned.32x32b.x32.b32 {a0,a1,a2,a3,a4,a5,a6,a7,a8,a9,a10,a11,a12,a13,a14,a15,a16,a17,a18,a19,a20,a21,a22,a23,a24,a25,a26,a27,a28,a29,a30,a31}, [%32];\n\ttcgen05.ld.sync.aligned.32x32b.x32.b32 {a32,a33,a34,a35,a36,a37,a38,a39,a40,a41,a42,a43,a44,a45,a46,a47,a48,a49,a50,a51,a52,a53,a54,a55,a56,a57,a58,a59,a60,a61,a62,a63}, [%33];\n\ttcgen05.wait::ld.sync.aligned;\n\tmov.b64 %0, {a0, a1};\n\tmov.b64 %1, {a2, a3};\n\tmov.b64 %2, {a4, a5};\n\tmov.b64 %3, {a6, a7};\n\tmov.b64 %4, {a8, a9};\n\tmov.b64 %5, {a10, a11};\n\tmov.b64 %6, {a12, a13};\n\tmov.b64 %7, {a14, a15};\n\tmov.b64 %8, {a16, a17};\n\tmov.b64 %9, {a18, a19};\n\tmov.b64 %10, {a20, a21};\n\tmov.b64 %11, {a22, a23};\n\tmov.b64 %12, {a24, a25};\n\tmov.b64 %13, {a26, a27};\n\tmov.b64 %14, {a28, a29};\n\tmov.b64 %15, {a30, a31};\n\tmov.b64 %16, {a32, a33};\n\tmov.b64 %17, {a34, a35};\n\tmov.b64 %18, {a36, a37};\n\tmov.b64 %19, {a38, a39};\n\tmov.b64 %20, {a40, a41};\n\tmov.b64 %21, {a42, a43};\n\tmov.b64 %22, {a44, a45};\n\tmov.b64 %23, {a46, a47};\n\tmov.b64 %24, {a48, a49};\n\tmov.b64 %25, {a50, a51};\n\tmov.b64 %26, {a52, a53};\n\tmov.b64 %27, {a54, a55};\n\tmov.b64 %28, {a56, a57};\n\tmov.b64 %29, {a58, a59};\n\tmov.b64 %30, {a60, a61};\n\tmov.b64 %31, {a62, a63};\n\t}"
+                 : "=l"(d[0]), "=l"(d[1]), "=l"(d[2]), "=l"(d[3]), "=l"(d[4]), "=l"(d[5]), "=l"(d[6]), "=l"(d[7]), "=l"(d[8]), "=l"(d[9]), "=l"(d[10]), "=l"(d[11]), "=l"(d[12]), "=l"(d[13]), "=l"(d[14]), "=l"(d[15]), "=l"(d[16]), "=l"(d[17]), "=l"(d[18]), "=l"(d[19]), "=l"(d[20]), "=l"(d[21]), "=l"(d[22]), "=l"(d[23]), "=l"(d[24]), "=l"(d[25]), "=l"(d[26]), "=l"(d[27]), "=l"(d[28]), "=l"(d[29]), "=l"(d[30]), "=l"(d[31])
+                 : "r"(taddr), "r"(taddr + 32)
+                 : "memory");
+  }
+}
+
+// acc = x * s2 + acc on packed fp32 pairs (fma.rn.f32x2, each lane rounded once).
+__device__ __forceinline__ void ffma2p(uint64_t& acc, uint64_t x, uint64_t s2) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(x), "l"(s2));
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void regs_claim() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // misc
