@@ -7,7 +7,6 @@
 #include "common.cuh"
 #include "block_gemm.cuh"
 #include "nvfp4_gemm.cuh"
-#include "pair_gemm.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
 
@@ -219,7 +218,7 @@ int nvfp4_wq_typed(const T* w, int64_t N, int64_t K, uint8_t* codes, uint8_t* sc
 // ------------------------------------------------------------------------------------------------------------
 // GEMMs
 // ------------------------------------------------------------------------------------------------------------
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotPair = 12 };
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8 };
 
 // The block GEMM moves registers between warpgroups (setmaxnreg); a launch with fewer registers a thread than the
 // split needs would wait forever, so the compiled kernel's count is checked before its first launch on a device.
@@ -236,83 +235,18 @@ int check_launch_regs(K kernel, int need) {
 }
 
 template <bool INT8, int OUT>
-int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::Params& p,
-                      cudaStream_t st) {
+int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                      const blockgemm::Params& p, cudaStream_t st) {
   auto kern = blockgemm::block_gemm_kernel<INT8, OUT>;
   const int slot = kSlotBlock + (INT8 ? 3 : 0) + OUT;
   if (!(g_dev[dev].smem_set & (1u << slot))) {
     const int rc = check_launch_regs(kern, (int)blockgemm::LAUNCH_REGS);
     if (rc) return rc;
   }
-  int rc = set_smem(dev, slot, kern, blockgemm::SMEM_BYTES);
+  int rc = set_smem(dev, slot, kern, blockgemm::smem_bytes<OUT>());
   if (rc) return rc;
   const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
-  kern<<<grid, blockgemm::NUM_THREADS, blockgemm::SMEM_BYTES, st>>>(ta, tb, p);
-  return launched();
-}
-
-// CTA-pair kernel for 16-bit outputs: launched as clusters of 2, as many pairs as fit at once (persistent).
-template <bool INT8, int OUT>
-int pair_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c,
-                     int64_t M, int64_t N, int64_t K, cudaStream_t st) {
-  auto kern = pairgemm::pair_gemm_kernel<INT8, OUT>;
-  const int slot = kSlotPair + (INT8 ? 2 : 0) + OUT;
-  static int max_pairs[kMaxDevices][4];
-  if (!(g_dev[dev].smem_set & (1u << slot))) {
-    int rc = check_launch_regs(kern, (int)pairgemm::LAUNCH_REGS);
-    if (rc) return rc;
-    if ((rc = set_smem(dev, slot, kern, pairgemm::SMEM_BYTES))) return rc;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(g_dev[dev].sms & ~1);
-    cfg.blockDim = dim3(pairgemm::NUM_THREADS);
-    cfg.dynamicSmemBytes = pairgemm::SMEM_BYTES;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
-      cudaGetLastError();
-      return BASAL200_ERR_LAUNCH;
-    }
-    max_pairs[dev][(INT8 ? 2 : 0) + OUT] = n;
-  } else {
-    int rc = set_smem(dev, slot, kern, pairgemm::SMEM_BYTES);
-    if (rc) return rc;
-  }
-  CUtensorMap ta, tb, tc;
-  int rc;
-  if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, pairgemm::BK, pairgemm::BM))) return rc;
-  if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, pairgemm::BK, pairgemm::BN / 2))) return rc;
-  if ((rc = tmap_u16(&tc, c, (uint64_t)N, (uint64_t)M, 64, pairgemm::BM))) return rc;
-  pairgemm::Params p;
-  p.s = s;
-  p.ws = ws;
-  p.bias = bias;
-  p.M = (int)M;
-  p.N = (int)N;
-  p.nkb = (int)(K / 128);
-  p.tiles_n = (int)((N + pairgemm::BN - 1) / pairgemm::BN);
-  const int64_t tiles = (M + 2 * pairgemm::BM - 1) / (2 * pairgemm::BM) * p.tiles_n;
-  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
-  p.num_tiles = (int)tiles;
-  const int pairs = (int)(tiles < max_pairs[dev][(INT8 ? 2 : 0) + OUT] ? tiles : max_pairs[dev][(INT8 ? 2 : 0) + OUT]);
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(pairgemm::NUM_THREADS);
-  cfg.dynamicSmemBytes = pairgemm::SMEM_BYTES;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p) != cudaSuccess) return launched();
+  kern<<<grid, blockgemm::NUM_THREADS, blockgemm::smem_bytes<OUT>(), st>>>(ta, tb, tc, p);
   return launched();
 }
 
@@ -327,11 +261,13 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
-  if (ct == BASAL200_BF16) return pair_gemm_launch<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, c, M, N, K, st);
-  if (ct == BASAL200_F16) return pair_gemm_launch<INT8, BASAL200_F16>(dev, q, s, w, ws, bias, c, M, N, K, st);
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
   if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;
+  if (ct == BASAL200_F32)
+    memset(&tc, 0, sizeof(tc));  // fp32 outputs are stored directly, without TMA
+  else if ((rc = tmap_u16(&tc, c, (uint64_t)N, (uint64_t)M, 64, blockgemm::BM)))
+    return rc;
   blockgemm::Params p;
   p.s = s;
   p.ws = ws;
@@ -345,9 +281,9 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;
   switch (ct) {
-    case BASAL200_BF16: return block_gemm_launch<INT8, BASAL200_BF16>(dev, ta, tb, p, st);
-    case BASAL200_F16: return block_gemm_launch<INT8, BASAL200_F16>(dev, ta, tb, p, st);
-    case BASAL200_F32: return block_gemm_launch<INT8, BASAL200_F32>(dev, ta, tb, p, st);
+    case BASAL200_BF16: return block_gemm_launch<INT8, BASAL200_BF16>(dev, ta, tb, tc, p, st);
+    case BASAL200_F16: return block_gemm_launch<INT8, BASAL200_F16>(dev, ta, tb, tc, p, st);
+    case BASAL200_F32: return block_gemm_launch<INT8, BASAL200_F32>(dev, ta, tb, tc, p, st);
     default: return BASAL200_ERR_DTYPE;
   }
 }

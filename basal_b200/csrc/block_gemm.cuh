@@ -5,13 +5,16 @@
 //
 // A [M, K] and B [N, K] are 8-bit, K-major. One persistent CTA per SM walks 128 x 256 output tiles (static round
 // robin, the 256-wide weight tiles of one 128-row activation tile next to each other). Its warps:
-//   warp 0      TMA producer: A and B slices of 128 bytes of K into a 4-stage shared-memory ring (128-byte swizzle)
+//   warp 0      TMA producer: A and B slices of 128 bytes of K into a shared-memory ring (128-byte swizzle), 3
+//               stages for 16-bit outputs, 4 for fp32
 //   warp 1      MMA issuer: 4 x tcgen05.mma (K = 32 each) per slice into one of two TMEM accumulators of 256
 //               columns (kind::f8f6f4 e4m3 -> f32, or kind::i8 s8 -> s32, exact for a 128-deep slice)
 //   warp 2      TMEM allocation (512 columns) and release
 //   warps 4-11  promotion: per slice, tcgen05.ld of the slice's product (64 columns in flight per wait), times
 //               a_s * b_s, added into fp32 registers with packed f32x2 FMAs (128 columns a thread); after the last
-//               slice, the cast (and bias) and the stores to C
+//               slice, the cast (and bias); 16-bit outputs go through a 64 KB staging buffer (128-byte swizzle) and
+//               asynchronous TMA stores (rows past M clipped by the tensor map), so the promotion of the next tile
+//               starts at once; fp32 outputs are stored directly
 // The MMA of slice kb + 1 runs while the promotion reads slice kb from the other accumulator. The producer warpgroup
 // gives registers to the promotion warpgroups (setmaxnreg: 40 / 232 of the 168 a thread at launch). A row's result
 // never depends on the other rows (no split of K, the same slice order for every M).
@@ -24,7 +27,6 @@ namespace blockgemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 128;  // bytes (= elements) of K per stage: one scale slice
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
@@ -39,9 +41,16 @@ constexpr uint32_t REGS_LOW = 40, REGS_HIGH = 232;
 constexpr uint32_t LAUNCH_REGS = (REGS_LOW * 128 + REGS_HIGH * 256) / NUM_THREADS;
 static_assert(REGS_LOW * 128 + REGS_HIGH * 256 <= LAUNCH_REGS * NUM_THREADS, "register split");
 
-struct Shared {
+constexpr int SUB_BYTES = BM * 128;  // one 64-column x 128-row sub-tile of 16-bit outputs (128-byte swizzle)
+
+// Shared memory of one CTA: the stage ring, the output staging (16-bit outputs), the barriers.
+template <int STAGES_, bool STAGING_>
+struct Smem {
+  static constexpr int STAGES = STAGES_;
+  static constexpr bool STAGING = STAGING_;
   uint8_t a[STAGES][A_BYTES];
   uint8_t b[STAGES][B_BYTES];
+  uint8_t out[STAGING ? 4 : 1][STAGING ? SUB_BYTES : 1024];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[2];
@@ -50,7 +59,12 @@ struct Shared {
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+template <int OUT>
+using SmemOf = Smem<OUT == BASAL200_F32 ? 4 : 3, OUT != BASAL200_F32>;
+template <int OUT>
+constexpr size_t smem_bytes() {
+  return sizeof(SmemOf<OUT>) + 1024;
+}
 
 struct Params {
   const float* s;   // [M, K/128]
@@ -70,6 +84,10 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
   }
 }
+
+// Offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled sub-tile (the layout TMA reads with
+// CU_TENSOR_MAP_SWIZZLE_128B).
+__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 // All 32 lanes wait; the warp proceeds only if every lane saw the phase complete.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned fault) {
@@ -140,9 +158,11 @@ struct Store<BASAL200_F32> {
 template <bool INT8, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     block_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const Params p) {
+                      const __grid_constant__ CUtensorMap tmC, const Params p) {
+  using S = SmemOf<OUT>;
+  constexpr int STAGES = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  S& sh = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = warp_id();
   const int lane = lane_id();
 
@@ -162,6 +182,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (S::STAGING) tma_prefetch_desc(&tmC);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
   tc_fence_before();
@@ -245,14 +266,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     regs_claim<REGS_HIGH>();
     using OutT = typename Store<OUT>::T;
     const int ew = warp - EPI_WARP0;
-    const int half = ew >> 2;   // which 128 columns of the 256-wide tile
-    const int quad = warp & 3;  // the TMEM lane quadrant this warp may access
+    const int half = ew >> 2;        // which 128 columns of the 256-wide tile
+    const int quad = warp & 3;       // the TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;  // row within the tile
+    const bool issuer = (ew & 3) == 0 && lane == 0;
     const int nkb = p.nkb;
     uint32_t acc_cnt = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-      const int row = tm * BM + quad * 32 + lane;
+      const int row = tm * BM + r;
       const int n0 = tn * BN + half * 128;
       const bool nvalid = n0 < p.N;
       const float* srow = p.s + (int64_t)min(row, p.M - 1) * nkb;
@@ -261,7 +284,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0ull;
       float sa = __ldg(srow), sb = __ldg(wsr);
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; ok && kb < nkb; ++kb) {
         const float sc = sa * sb;
         const uint64_t sc2 = pack_f2(sc, sc);
         if (kb + 1 < nkb) {
@@ -289,22 +312,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         ++acc_cnt;
       }
-      if (ok && nvalid && row < p.M) {
-        OutT* dst = reinterpret_cast<OutT*>(p.c) + (int64_t)row * p.N + n0;
-        const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
+      const OutT* bias = (p.bias && nvalid) ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
+      if constexpr (S::STAGING) {
+        // cast (+ bias) into this half's two staging sub-tiles, then two TMA stores of 128 rows x 64 columns
+        if (issuer) tma_store_wait_read();          // the previous tile's stores have read the staging
+        ok = named_barrier_and(1 + half, 128, ok);  // the warpgroup agrees whether to go on
+        if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < 128; c += 8) {
+        for (int j = 0; j < 16; ++j) {
           float v[8];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_f2(acc[c / 2 + i]);
+            const float2 f = unpack_f2(acc[j * 4 + i]);
             v[2 * i] = f.x;
             v[2 * i + 1] = f.y;
           }
-          Store<OUT>::vec8(dst + c, v, bias ? bias + c : nullptr);
+          OutT* dst = reinterpret_cast<OutT*>(sh.out[half * 2 + (j >> 3)] + sw128(r, j & 7));
+          Store<OUT>::vec8(dst, v, bias ? bias + j * 8 : nullptr);
+        }
+        fence_proxy_async();
+        named_barrier(1 + half, 128);
+        if (issuer) {
+          if (nvalid) {
+            tma_store_2d(&tmC, sh.out[half * 2], n0, tm * BM);
+            tma_store_2d(&tmC, sh.out[half * 2 + 1], n0 + 64, tm * BM);
+          }
+          tma_store_commit();
+        }
+      } else {
+        if (!ok) break;
+        if (nvalid && row < p.M) {
+          OutT* dst = reinterpret_cast<OutT*>(p.c) + (int64_t)row * p.N + n0;
+#pragma unroll
+          for (int c = 0; c < 128; c += 8) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = unpack_f2(acc[c / 2 + i]);
+              v[2 * i] = f.x;
+              v[2 * i + 1] = f.y;
+            }
+            Store<OUT>::vec8(dst + c, v, bias ? bias + c : nullptr);
+          }
         }
       }
     }
+    if (S::STAGING && issuer) tma_store_wait_all();
   }
 
   tc_fence_before();

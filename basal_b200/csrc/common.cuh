@@ -88,40 +88,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// clusters of two CTAs (the CTA pair of tcgen05 cta_group::2); every load targets one CTA only
-// ---------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// The shared::cluster address of `local` (an address of this CTA's shared memory) in the CTA of rank `rank`.
-__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Arrive on an mbarrier of another CTA of the cluster. The pair exchanges no data through generic memory: copies
-// complete through the async proxy, TMEM reads are ordered by tcgen05.wait::ld and the tcgen05 fences, so the default
-// (CTA-scope) semantics suffice and the cheaper arrive is used.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-// Waits on a local barrier that the pair's other CTA (or its tcgen05 commits) arrives on: the plain bounded wait.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                  unsigned fault) {
-  return mbar_wait(bar, parity, abort_flag, fault);
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor, one destination CTA per copy) and the plain bulk copy
+// TMA (cp.async.bulk.tensor) loads and stores, and the plain bulk copy
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -131,16 +98,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// The CTA-pair form: the copy lands in this CTA's shared memory and completes its bytes on `cluster_bar`, an mbarrier
-// of either CTA of the pair (here always the pair's leader). The data goes to this CTA only.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-      "[%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
       : "memory");
 }
 
@@ -267,43 +224,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// CTA-pair forms. The MMA of a pair (M = 256: 128 rows in each CTA's TMEM, A rows from each CTA's shared memory,
-// B split along N between them) is issued by the pair's leader.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-__device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrives on the mbarrier at `cluster_bar` (a shared::cluster address: this CTA's or its pair's) once every tcgen05
-// operation this thread issued before has completed. One call per CTA to signal.
-__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
-               : "memory");
-}
-
 // 32 lanes x 16 columns of 32 bits: thread i of the warp gets lane (quadrant base + i), columns taddr .. taddr+15.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -350,8 +270,9 @@ __device__ __forceinline__ void ffma2(uint64_t& acc, uint32_t lo, uint32_t hi, u
 }
 
 // 64 consecutive TMEM columns of this warp's 32 lanes (two 32x32b.x32 loads, then the wait), returned as 32 packed
-// fp32 pairs (columns 2j, 2j+1) ready for f32x2 arithmetic; INT8: the s32 values are converted to fp32 first (exact
-// below 2^24). The loads, the wait and the packing are one asm block so that the pairs need no register moves.
+// fp32 pairs (columns 2j, 2j+1) ready for f32x2 arithmetic. The loads, the wait and the packing are one asm block so
+// that the pairs need no register moves. INT8: the s32 partials (below 2^21 in magnitude for a 128-deep slice) are
+// converted to fp32 exactly first. (Measured on B200: cvt beats the integer-add / packed-subtract conversion.)
 template <bool INT8>
 __device__ __forceinline__ void tmem_ld64_pairs(uint32_t taddr, uint64_t (&d)[32]) {
   if (INT8) {
