@@ -35,6 +35,9 @@ int current_device(int* dev) {
   return d.checked == 1 ? BASAL200_OK : BASAL200_ERR_ARCH;
 }
 
+// Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8 };
+
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
 int set_smem(int dev, int slot, K kernel, size_t bytes) {
@@ -128,16 +131,14 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   uint8_t* qb = static_cast<uint8_t*>(q);
   switch (xt) {
     case BASAL200_BF16:
-      act_quant_block_kernel<__nv_bfloat16, INT8><<<grid, 256, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(x), groups, (int)(K / 128), K, qb, s);
+      act_quant_block_kernel<__nv_bfloat16, INT8><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), groups,
+                                                                         qb, s);
       break;
     case BASAL200_F16:
-      act_quant_block_kernel<__half, INT8><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), groups,
-                                                                  (int)(K / 128), K, qb, s);
+      act_quant_block_kernel<__half, INT8><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), groups, qb, s);
       break;
     case BASAL200_F32:
-      act_quant_block_kernel<float, INT8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), groups,
-                                                                 (int)(K / 128), K, qb, s);
+      act_quant_block_kernel<float, INT8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), groups, qb, s);
       break;
     default:
       return BASAL200_ERR_DTYPE;
@@ -218,7 +219,6 @@ int nvfp4_wq_typed(const T* w, int64_t N, int64_t K, uint8_t* codes, uint8_t* sc
 // ------------------------------------------------------------------------------------------------------------
 // GEMMs
 // ------------------------------------------------------------------------------------------------------------
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8 };
 
 // The block GEMM moves registers between warpgroups (setmaxnreg); a launch with fewer registers a thread than the
 // split needs would wait forever, so the compiled kernel's count is checked before its first launch on a device.

@@ -1,7 +1,7 @@
 // Quantisers of the block formats and of NVFP4, bit-exact to the reference's CPU arithmetic (rkinas/basal 2.8.1):
-// every division is an IEEE round-to-nearest division (__fdiv_rn), every product that the reference rounds on its
-// own is __fmul_rn (no contraction into an FMA), casts to e4m3 round to nearest even (cvt.rn.satfinite after an
-// explicit clamp), int8 rounds half to even.
+// every division gives the code of an IEEE round-to-nearest division (__fdiv_rn, or a checked reciprocal product,
+// quotient_for_code), every product that the reference rounds on its own is __fmul_rn (no contraction into an FMA),
+// casts to e4m3 round to nearest even with saturation at +-448 (cvt.rn.satfinite), int8 rounds half to even.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -48,34 +48,58 @@ __device__ __forceinline__ uint8_t float_to_e4m3(float v) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
 }
 
-// 8 values of one group -> 8 code bytes: v / sc, INT8: round half to even; clamp to +-qmax; cast.
+// v / sc rounded as an IEEE division, where that rounding can change the code; elsewhere the cheaper v * RN(1 / sc).
+// The product y is within 1.5 ulp of the correctly rounded quotient, so the two give the same code unless the
+// quotient lies within a few ulps of a rounding boundary of the code: an e4m3 midpoint (low 20 mantissa bits near
+// 0x80000) or the e4m3 subnormal range (FP8), a half-integer (INT8). Those few values (about 1e-4 of random data)
+// take the exact division; every code equals the one of the reference's x / s (checked against the oracle).
+template <bool INT8>
+__device__ __forceinline__ float quotient_for_code(float v, float sc, float rcp) {
+  const float y = __fmul_rn(v, rcp);
+  bool near;
+  if (INT8) {
+    near = fabsf(__fsub_rn(y, __fadd_rn(floorf(y), 0.5f))) < 0x1p-14f;
+  } else {
+    const uint32_t low = __float_as_uint(y) & 0xFFFFFu;
+    near = (low - 0x7FFFCu) <= 8u || (fabsf(y) < 0x1p-6f && y != 0.0f);
+  }
+  return near ? __fdiv_rn(v, sc) : y;
+}
+
+// 8 values of one group -> 8 code bytes: v / sc; INT8: round half to even, clamp to +-127, cast; FP8: cast two at a
+// time with cvt.rn.satfinite.e4m3x2, whose saturation at +-448 is the reference's clamp (the quotient never exceeds 448
+// by more than rounding).
 template <bool INT8>
 __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
+  const float rcp = __frcp_rn(sc);
   uint32_t w[2] = {0u, 0u};
+  if (INT8) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float t = __fdiv_rn(v[i], sc);
-    uint32_t b;
-    if (INT8) {
-      t = fminf(fmaxf(rintf(t), -127.0f), 127.0f);
-      b = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(t))));
-    } else {
-      t = fminf(fmaxf(t, -448.0f), 448.0f);
-      b = float_to_e4m3(t);
+    for (int i = 0; i < 8; ++i) {
+      const float t = fminf(fmaxf(rintf(quotient_for_code<true>(v[i], sc, rcp)), -127.0f), 127.0f);
+      const uint32_t b = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(t))));
+      w[i >> 2] |= b << (8 * (i & 3));
     }
-    w[i >> 2] |= b << (8 * (i & 3));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const float2 t = make_float2(quotient_for_code<false>(v[i], sc, rcp), quotient_for_code<false>(v[i + 1], sc, rcp));
+      const uint32_t b = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(t, __NV_SATFINITE, __NV_E4M3));
+      w[i >> 2] |= b << (8 * (i & 3));
+    }
   }
   return make_uint2(w[0], w[1]);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
 // Activations, FP8 / INT8 block formats: one half-warp per 128-feature group (8 values a lane), amax by shuffles.
-// basal/blockquant.py:118-123: s = max(amax, 1e-12) / qmax; q = cast(clamp(x / s)) (INT8: round first).
+// basal/blockquant.py:118-123: s = max(amax, 1e-12) / qmax; q = cast(clamp(x / s)) (INT8: round first). The
+// activations are contiguous, so group g is the 128 values from element 128 g. (Measured on B200: this kernel is
+// bound by its per-value arithmetic, not by bytes in flight; staging chunks through shared memory did not speed it.)
 // ---------------------------------------------------------------------------------------------------------------
 template <typename T, bool INT8>
-__global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups, int gpr,
-                                                              int64_t K, uint8_t* __restrict__ q,
-                                                              float* __restrict__ s) {
+__global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups,
+                                                              uint8_t* __restrict__ q, float* __restrict__ s) {
   constexpr float kQmax = INT8 ? 127.0f : 448.0f;
   const int lane = threadIdx.x & 31;
   const int half = lane >> 4, l = lane & 15;
@@ -84,11 +108,8 @@ __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restric
     const int64_t g = 2 * p + half;
     const bool valid = g < groups;
     float v[8];
-    int64_t off = 0;
+    const int64_t off = g * 128 + l * 8;
     if (valid) {
-      const int64_t row = g / gpr;
-      const int64_t kb = g - row * gpr;
-      off = row * K + kb * 128 + l * 8;
       load8(x + off, v);
     } else {
 #pragma unroll
