@@ -9,7 +9,8 @@ TFLOP/s (2 M N K summed over the projections), whole job: with N GPUs every rank
 shards of independent requests, no collective; "weak" scaling) and the value is all ranks' FLOPs over the slowest
 rank's device time. One JSON line on rank 0 with, besides the contract keys:
   roofline      the FP8 block GEMM (the dominant kernel): achieved TFLOP/s from CUDA events around its launches in
-                the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200)
+                the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200), the sustained
+                figure since the GEMM runs inside a long power-capped step (the burst fraction is reported beside it)
   e2e           the same metric through the public API (BlockFP8Linear modules) from pinned host memory: the H2D copy
                 of the step's activations and the D2H copy of its four outputs inside the timed region
   cpu_baseline  the reference's CPU maths (oracle/, numpy + BLAS on all host threads) on a bounded sample of rows
@@ -33,7 +34,7 @@ PROJ = (("qkv", 5120, 2048), ("o", 2048, 2048), ("gate_up", 12288, 2048), ("down
 HIDDEN, INTER = 2048, 6144
 WORKLOAD = ("C2: one decoder layer's projection set, FP8-block W8A8, 64 varlen-packed requests (lengths U[128,2048], "
             "seed 0), qkv 2048->5120, o 2048->2048, gate/up 2048->12288, down 6144->2048")
-FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 PROFILE = os.path.join(ROOT, "profiles", "fp8_block_gemm_c2.txt")
 
 
@@ -44,7 +45,7 @@ def peaks():
         return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
                 "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "source": "measured"}
     except (OSError, KeyError, ValueError):
-        return dict(FALLBACK_PEAKS, bf16_tflops_sustained=FALLBACK_PEAKS["bf16_tflops"], source="fallback")
+        return dict(FALLBACK_PEAKS, source="fallback")
 
 
 def profiled_traffic():
@@ -275,7 +276,8 @@ def run_ours(args, rank, world, local_rank):
     pk = peaks()
     gemm_flops = sum(2 * M * n * k for _, n, k in PROJ)
     achieved = gemm_flops / (sum(gemm_ms) * 1e-3) / 1e12
-    peak = 2.0 * pk["bf16_tflops"]
+    peak = 2.0 * pk["bf16_tflops_sustained"]
+    peak_burst = 2.0 * pk["bf16_tflops"]
     traffic = profiled_traffic()
     if rank == 0:
         cpu = cpu_baseline() if world == 1 else None
@@ -289,7 +291,9 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "basal200 fp8 block GEMM (tcgen05 kind::f8f6f4)",
-                         "peak_source": f"2 x bf16_tflops of {pk['source']} peaks (FP8 dense = 2 x bf16 dense)",
+                         "peak_source": f"2 x bf16_tflops_sustained of {pk['source']} peaks (FP8 dense = 2 x bf16 "
+                                        "dense; the GEMM is timed inside a long power-capped step)",
+                         "frac_of_burst_peak": round(achieved / peak_burst, 4),
                          "per_projection_tflops": {name: round(2 * M * n * k / (t * 1e-3) / 1e12, 1)
                                                    for (name, n, k), t in zip(PROJ, gemm_ms)}},
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
