@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "block_gemm.cuh"
+#include "small_gemm.cuh"
 #include "nvfp4_gemm.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
@@ -36,7 +37,7 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8 };
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 11 };  // kSlotSmall .. kSlotSmall + 11
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -250,6 +251,37 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
   return launched();
 }
 
+// Few rows (M <= 64): the weight-streaming kernel, NT token rows a tile (32 or 64), one CTA per 128-row weight tile.
+template <bool INT8, int OUT, int NT>
+int small_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
+                      void* c, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  auto kern = smallgemm::small_gemm_kernel<INT8, OUT, NT>;
+  constexpr size_t smem = smallgemm::smem_bytes<NT>();
+  const int slot = kSlotSmall + (INT8 ? 6 : 0) + OUT * 2 + (NT == 32 ? 0 : 1);
+  int rc = set_smem(dev, slot, kern, smem);
+  if (rc) return rc;
+  CUtensorMap tw, tt;
+  if ((rc = tmap_u8(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, smallgemm::BK, smallgemm::BW))) return rc;
+  if ((rc = tmap_u8(&tt, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, smallgemm::BK, NT))) return rc;
+  smallgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = bias;
+  p.c = c;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nkb = (int)(K / 128);
+  kern<<<(unsigned)(N / smallgemm::BW), smallgemm::Cfg<NT>::THREADS, smem, st>>>(tw, tt, p);
+  return launched();
+}
+
+template <bool INT8, int OUT>
+int small_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c,
+               int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (M <= 32) return small_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, c, M, N, K, st);
+  return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, c, M, N, K, st);
+}
+
 template <bool INT8>
 int block_gemm(const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c, int ct,
                int64_t M, int64_t N, int64_t K, cudaStream_t st) {
@@ -261,6 +293,14 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
+  if (M <= smallgemm::MAX_ROWS && K / 128 <= smallgemm::MAX_KB && N / smallgemm::BW <= 65535) {
+    switch (ct) {
+      case BASAL200_BF16: return small_gemm<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, c, M, N, K, st);
+      case BASAL200_F16: return small_gemm<INT8, BASAL200_F16>(dev, q, s, w, ws, bias, c, M, N, K, st);
+      case BASAL200_F32: return small_gemm<INT8, BASAL200_F32>(dev, q, s, w, ws, bias, c, M, N, K, st);
+      default: return BASAL200_ERR_DTYPE;
+    }
+  }
   CUtensorMap ta, tb, tc;
   if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
   if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;

@@ -1,0 +1,274 @@
+// The block-scaled GEMM of the FP8-block and INT8-block formats for few rows (M <= 64: decode steps, short chunks),
+// where the weights are nearly all of the bytes and the GEMM is bound by how fast the weights stream from HBM.
+//
+// The same arithmetic as block_gemm.cuh, element for element: per 128-deep slice kb the exact product of the codes
+// (tcgen05.mma, kind::f8f6f4 -> f32 or kind::i8 -> s32), then acc = fma(product, a_s * b_s, acc) in slice order from
+// zero, a_s * b_s rounded once. So a row's output is bit-identical whichever kernel computes it and whatever the other
+// rows are, as the reference requires (basal/blockquant.py:14-16, tests/test_fp8block.py:134-148): the reduction is
+// never split.
+//
+// Operands swapped: a tile is 128 weight rows (the MMA's M) x NT token rows (the MMA's N: 32 or 64, the rows past M
+// read as zeros). The products of two codes are exact and the MMA reduces along K either way, so the swap changes no
+// bit of a slice's product.
+//
+// What bounds it, measured on B200: one SM fetches a 16 KB slice from HBM about every 0.3-0.4 us (the requests one SM
+// keeps in flight cover about 50 KB, whatever the ring depth), and one thread issuing a slice's 4 MMAs and their
+// commits, or one warp testing a barrier and loading a slice's product, spends hundreds of cycles in issue latency,
+// which few tokens cannot hide. (Spreading a tile's loads over a cluster, with loader CTAs pushing slices into the
+// leader's ring through distributed shared memory, was measured slower: the go-ahead/push round trip per stage costs
+// about as much as the DRAM latency it hides.) So one CTA streams one 128-row weight tile through its whole K, and:
+//   * three MMA issuers (warps 1-3; slice kb by warp 1 + kb % 3) overlap their issue latency; each owns every third
+//     stage of the ring (9 stages for NT = 32, 6 for NT = 64) and its column block of the two TMEM product groups, so
+//     every barrier's phases are produced and awaited in one thread's program order (a parity wait only tells the
+//     current phase from the one before);
+//   * the promotion takes the products three slices at a time (one barrier, three TMEM loads, one wait, one release),
+//     with every a_s * b_s of the tile computed into shared memory before the first slice; 32 tokens a warp (4 warps
+//     for NT = 32, 8 for NT = 64), thread = weight row; at the end the cast (and bias) and the stores, each token's 128
+//     outputs consecutive.
+#pragma once
+#include "block_gemm.cuh"
+
+namespace b200 {
+namespace smallgemm {
+
+constexpr int BW = 128;            // weight rows a tile (the MMA's M)
+constexpr int BK = 128;            // K bytes a slice
+constexpr int W_BYTES = BW * BK;   // 16 KB
+constexpr int MMA_WARPS = 3;       // warps 1-3 issue the MMAs
+constexpr int GROUP = MMA_WARPS;   // slices a product group (one per issuer)
+constexpr int GSLOTS = 2;          // product groups in TMEM
+
+constexpr int EPI_WARP0 = 4;
+constexpr int MAX_ROWS = 64;       // rows served by this kernel
+constexpr int MAX_KB = 64;         // K <= 8192 (all scales of a tile in shared memory)
+
+template <int NT>
+struct Cfg {
+  static constexpr int T_BYTES = NT * BK;
+  static constexpr int STAGE_BYTES = W_BYTES + T_BYTES;  // weights then tokens
+  static constexpr int STAGES = NT == 32 ? 9 : 6;        // a multiple of MMA_WARPS (stage ownership)
+  static_assert(STAGES % MMA_WARPS == 0, "stage ownership");
+  static constexpr int EPI_WARPS = NT / 32 * 4;          // 32 tokens a warp
+  static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+  static constexpr uint32_t TMEM_COLS = GSLOTS * GROUP * NT <= 256 ? 256 : 512;  // a power of two
+};
+
+template <int NT>
+struct Smem {
+  static constexpr int STAGES = Cfg<NT>::STAGES;
+  uint8_t stage[STAGES][Cfg<NT>::STAGE_BYTES];  // [weights 128 x 128][tokens NT x 128], 128-byte swizzle each
+  float sc[MAX_KB][NT];                          // a_s[token, kb] * b_s[tile, kb]
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t gfull[GSLOTS];
+  uint64_t gempty[GSLOTS];
+  uint64_t mdrain;
+  uint32_t tmem_base;
+  int abort;
+};
+template <int NT>
+constexpr size_t smem_bytes() {
+  return sizeof(Smem<NT>) + 1024;
+}
+
+struct Params {
+  const float* s;    // [M, K/128] activation scales
+  const float* ws;   // [N/128, K/128] weight scales
+  const void* bias;  // [N] in the output type, or null
+  void* c;           // [M, N]
+  int M, N, nkb;
+};
+
+// One bf16 / f16 / f32 output, with the bias added to the cast value and rounded again (as blockgemm::Store).
+template <int OUT>
+__device__ __forceinline__ void store1(void* c, int64_t idx, float v, const void* bias, int n) {
+  if (OUT == BASAL200_BF16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    if (bias)
+      h = __float2bfloat16_rn(
+          __fadd_rn(__bfloat162float(h), __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n])));
+    static_cast<__nv_bfloat16*>(c)[idx] = h;
+  } else if (OUT == BASAL200_F16) {
+    __half h = __float2half_rn(v);
+    if (bias) h = __float2half_rn(__fadd_rn(__half2float(h), __half2float(static_cast<const __half*>(bias)[n])));
+    static_cast<__half*>(c)[idx] = h;
+  } else {
+    if (bias) v = __fadd_rn(v, static_cast<const float*>(bias)[n]);
+    static_cast<float*>(c)[idx] = v;
+  }
+}
+
+// acc (16 packed pairs: this warp's 32 tokens) += product x scale, scale = a_s * b_s of the token (the large-M kernel's
+// rounding: one product, then one fma per element).
+template <bool INT8>
+__device__ __forceinline__ void promote32(uint64_t (&acc)[16], const uint32_t (&x)[32], const float* sc) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    uint32_t lo = x[j], hi = x[j + 1];
+    if (INT8) {
+      lo = __float_as_uint(__int2float_rn((int)lo));
+      hi = __float_as_uint(__int2float_rn((int)hi));
+    }
+    ffma2p(acc[j / 2], pack_u2(lo, hi), *reinterpret_cast<const uint64_t*>(sc + j));
+  }
+}
+
+template <bool INT8, int OUT, int NT>
+__global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
+    small_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
+                      const Params p) {
+  using S = Smem<NT>;
+  using C = Cfg<NT>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  S& sh = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int nkb = p.nkb;
+  const int ngroups = (nkb + GROUP - 1) / GROUP;
+  const int tile = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int g = 0; g < GSLOTS; ++g) {
+      mbar_init(&sh.gfull[g], MMA_WARPS);
+      mbar_init(&sh.gempty[g], C::EPI_WARPS);
+    }
+    mbar_init(&sh.mdrain, MMA_WARPS);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmT);
+  }
+  if (warp == 2) tmem_alloc(&sh.tmem_base, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+
+  {
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        uint32_t filled = 0, last_phase = 0;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int stage = kb % STAGES;
+          const uint32_t phase = (uint32_t)(kb / STAGES) & 1;
+          if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) break;
+          mbar_arrive_expect_tx(&sh.full[stage], C::STAGE_BYTES);
+          tma_load_2d(sh.stage[stage], &tmW, &sh.full[stage], kb * BK, tile * BW);
+          tma_load_2d(sh.stage[stage] + W_BYTES, &tmT, &sh.full[stage], kb * BK, 0);
+          filled |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+        }
+        if (*abort_flag) {  // let the copies already issued land
+          for (int s = 0; s < STAGES; ++s)
+            if (filled & (1u << s)) blockgemm::drain_wait(&sh.full[s], (last_phase >> s) & 1);
+        }
+      }
+    } else if (warp < EPI_WARP0) {
+      // ---------------- MMA issuers: warp 1 + i issues slice 3g + i of every group g ----------------
+      if (lane == 0) {
+        constexpr uint32_t idesc = INT8 ? idesc_dense(2, 1, 1, BW, NT) : idesc_dense(1, 0, 0, BW, NT);
+        const int i = warp - 1;
+        for (int g = 0; g < ngroups; ++g) {
+          const int slot = g % GSLOTS;
+          // the group's TMEM block is free (its previous group was read); an issuer without a slice in the last
+          // group still waits and commits, so every group's barrier phase gets its three arrivals in order
+          if (!mbar_wait(&sh.gempty[slot], ((uint32_t)(g / GSLOTS) & 1) ^ 1, abort_flag, kFaultTimeoutMma)) break;
+          const int kb = g * GROUP + i;
+          if (kb < nkb) {
+            const int stage = kb % STAGES;
+            if (!mbar_wait(&sh.full[stage], (uint32_t)(kb / STAGES) & 1, abort_flag, kFaultTimeoutMma)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)((slot * GROUP + i) * NT);
+            const uint64_t ad = desc_sw128(smem_u32(sh.stage[stage]));
+            const uint64_t bd = desc_sw128(smem_u32(sh.stage[stage] + W_BYTES));
+#pragma unroll
+            for (int k = 0; k < BK / 32; ++k) {
+              if (INT8)
+                mma_i8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+              else
+                mma_f8f6f4(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+            }
+            mma_commit(&sh.empty[stage]);
+          }
+          mma_commit(&sh.gfull[slot]);
+        }
+        // every MMA this thread issued has finished before TMEM and shared memory are released
+        mma_commit(&sh.mdrain);
+        blockgemm::drain_wait(&sh.mdrain, 0);
+      }
+    } else {
+      // ---------------- promotion and epilogue ----------------
+      const int ew = warp - EPI_WARP0;
+      const int quad = warp & 3;       // TMEM lane quadrant: weight rows quad * 32 ..
+      const int half = ew >> 2;        // which 32 of the NT tokens
+      const int t = quad * 32 + lane;  // weight row of the tile
+      const int et = ew * 32 + lane;   // index among the promotion threads
+      constexpr int ETHREADS = C::EPI_WARPS * 32;
+      const uint32_t tcol = tmem + ((uint32_t)(quad * 32) << 16) + half * 32;
+      // every a_s * b_s of the tile, while the first slices load (token j's scales are contiguous)
+      for (int idx = et; idx < NT * nkb; idx += ETHREADS) {
+        const int j = idx / nkb, kb = idx - j * nkb;
+        sh.sc[kb][j] = j < p.M ? __ldg(p.s + (int64_t)j * nkb + kb) * __ldg(p.ws + (int64_t)tile * nkb + kb) : 0.f;
+      }
+      named_barrier(1, ETHREADS);
+      uint64_t acc[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = 0ull;
+      bool ok = true;
+      for (int g = 0; ok && g < ngroups; ++g) {
+        const int slot = g % GSLOTS;
+        if (!blockgemm::warp_wait(&sh.gfull[slot], (uint32_t)(g / GSLOTS) & 1, abort_flag, kFaultTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int n = nkb - g * GROUP < GROUP ? nkb - g * GROUP : GROUP;  // slices in this group
+        uint32_t x0[32], x1[32], x2[32];
+        const uint32_t base = tcol + (uint32_t)(slot * GROUP * NT);
+        tmem_ld32_issue(base, x0);
+        if (n > 1) tmem_ld32_issue(base + NT, x1);
+        if (n > 2) tmem_ld32_issue(base + 2 * NT, x2);
+        tmem_ld_wait32(x0);  // one wait covers every load in flight; the other two name their registers
+        tmem_ld_wait32(x1);
+        tmem_ld_wait32(x2);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.gempty[slot]);
+        const int kb = g * GROUP;
+        promote32<INT8>(acc, x0, &sh.sc[kb][half * 32]);
+        if (n > 1) promote32<INT8>(acc, x1, &sh.sc[kb + 1][half * 32]);
+        if (n > 2) promote32<INT8>(acc, x2, &sh.sc[kb + 2][half * 32]);
+      }
+      if (ok) {
+        // cast (+ bias) and store: token j's outputs of this tile are 128 consecutive values
+        const int n = tile * BW + t;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float2 v = unpack_f2(acc[j / 2]);
+          const int tok = half * 32 + j;
+          if (tok < p.M) store1<OUT>(p.c, (int64_t)tok * p.N + n, v.x, p.bias, n);
+          if (tok + 1 < p.M) store1<OUT>(p.c, (int64_t)(tok + 1) * p.N + n, v.y, p.bias, n);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace smallgemm
+}  // namespace b200

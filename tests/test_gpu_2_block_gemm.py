@@ -64,9 +64,28 @@ def test_kernel_ignores_the_other_rows(b2, fmt, M):
 
 
 @pytest.mark.parametrize("fmt", ["fp8", "int8"])
-def test_bf16_linear_within_north_star_tolerance(b2, fmt):
-    """linear (act_quant + GEMM, bf16 out) against the oracle's linear: 1e-2 relative."""
-    M, N, K = 517, 1280, 2048
+@pytest.mark.parametrize("M", [1, 16, 32, 33, 64, 65, 100, 128])
+def test_few_rows_kernel_equals_the_maths_and_the_large_kernel(b2, fmt, M):
+    """M <= 128 runs the weight-streaming kernel (weights as the MMA's M side): within the maths' tolerance, and
+    every row bit-identical to the same row computed by the large-M kernel among 300 rows, for fp32 and bf16."""
+    N, K = 640, 1152
+    x, q, s, qa, sa = operands(b2, fmt, 300, N, K, seed=M)
+    m = mod(b2, fmt)
+    for dt in (torch.float32, torch.bfloat16, torch.float16):
+        small = m.gemm(qa[:M].contiguous(), sa[:M].contiguous(), q, s, dt)
+        large = m.gemm(qa, sa, q, s, dt)
+        assert torch.equal(small, large[:M]), (dt, (small.float() - large[:M].float()).abs().max())
+    ref = oracle_y(fmt, qa[:M], sa[:M], q, s)
+    got = m.gemm(qa[:M].contiguous(), sa[:M].contiguous(), q, s, torch.float32).cpu().numpy()
+    assert np.allclose(got, ref, rtol=TOL[fmt], atol=TOL[fmt]), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M", [517, 7])
+def test_bf16_linear_within_north_star_tolerance(b2, fmt, M):
+    """linear (act_quant + GEMM, bf16 out, bias) against the oracle's linear: 1e-2 relative, for the large-M and
+    the few-rows kernel."""
+    N, K = 1280, 2048
     g = torch.Generator().manual_seed(5)
     x = torch.randn(M, K, generator=g).bfloat16()
     w = torch.randn(N, K, generator=g) * 0.02
