@@ -387,18 +387,19 @@ int logits_typed(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head,
                  const int64_t* ids,
                  int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
   const dim3 grid((unsigned)((U + readout::TU - 1) / readout::TU), (unsigned)((R + readout::TR - 1) / readout::TR));
+  constexpr int threads = readout::WARPS * 32;
   if (!bias) {
-    readout::code_logits_kernel<TH, TW, float><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U, nullptr,
-                                                                      softcap, z);
+    readout::code_logits_kernel<TH, TW, float><<<grid, threads, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U, nullptr,
+                                                                          softcap, z);
   } else if (bt == BASAL200_F32) {
-    readout::code_logits_kernel<TH, TW, float><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
-                                                                      static_cast<const float*>(bias), softcap, z);
+    readout::code_logits_kernel<TH, TW, float><<<grid, threads, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
+                                                                          static_cast<const float*>(bias), softcap, z);
   } else if (bt == BASAL200_BF16) {
-    readout::code_logits_kernel<TH, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(
+    readout::code_logits_kernel<TH, TW, __nv_bfloat16><<<grid, threads, 0, st>>>(
         h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z);
   } else if (bt == BASAL200_F16) {
-    readout::code_logits_kernel<TH, TW, __half><<<grid, 256, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
-                                                                       static_cast<const __half*>(bias), softcap, z);
+    readout::code_logits_kernel<TH, TW, __half><<<grid, threads, 0, st>>>(
+        h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z);
   } else {
     return BASAL200_ERR_DTYPE;
   }

@@ -344,6 +344,113 @@ def run_case(name):
     print(json.dumps({"case": name, "M": M, "N": N, "K": K, "faults": b2._lib.device_faults(0)}))
 
 
+def run_sweep(fmts):
+    """The C3 / C4 linear sweeps (BASELINE configs 3 and 4): M in {16, 128, 1024, 8192} x (N, K) in {(2048, 2048),
+    (12288, 2048), (2048, 6144)}, per format. One JSON line per point: the GEMM alone (codes and scales already
+    quantised) and the linear (activation quantiser + GEMM), each timed as 4 launches on 4 different weights inside
+    one CUDA graph that first reads a 256 MB buffer (L2 holds no operand, and stays clean), minus that read alone;
+    bytes = weight codes + scales + activation codes + scales + bf16 output (the algorithmic bytes), against the
+    measured HBM copy bandwidth. Synthetic inputs: X ~ N(0, 1) (NVFP4: 1% of values x 20), W ~ N(0, 0.02), seed 0."""
+    import torch
+
+    import basal_b200 as b2
+    dev = torch.device("cuda", 0)
+    pk = peaks()
+    flush = torch.ones(64 << 20, device=dev)
+    reps = 4
+
+    def graph_us(fn, n=15):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        del g
+        return statistics.median(ts)
+
+    base = graph_us(lambda: flush.sum())
+    gen = torch.Generator(device=dev).manual_seed(0)
+    if "readout" in fmts:
+        # C4's readout: h [256, 2048] bf16 ~ N(0, 1) at the answer positions, a 151,936-row bf16 head ~ N(0, 0.02),
+        # one code set of k ids shared by all rows; the device part (code_logits + code_probs) per call
+        R, D, V = 256, 2048, 151936
+        head = torch.nn.Linear(D, V, bias=False, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            head.weight.normal_(0.0, 0.02, generator=gen)
+        h = torch.randn(R, D, device=dev, generator=gen).bfloat16()
+        for softcap in (None, 30.0):
+            ro = b2.readout.CodeReadout(head, softcap=softcap)
+            for k in (2, 8, 64, 255):
+                ids = torch.randperm(V, device=dev, generator=gen)[:k].tolist()
+                rows, idx, pad = ro.rows([ids] * R)
+                t = (graph_us(lambda: (flush.sum(), ro.probs_of(ro.logits(h, rows), idx, pad))) - base)
+                byts = 2 * R * D + 2 * k * D + 4 * R * k * 2 + 8 * k
+                print(json.dumps({"sweep": "C4 readout", "R": R, "D": D, "k": k, "softcap": softcap,
+                                  "us": round(t, 2), "gbs": round(byts / t / 1e3, 1),
+                                  "gflops": round(2 * R * k * D / t / 1e3, 1)}), flush=True)
+        del head
+        fmts = [f for f in fmts if f != "readout"]
+    for fmt in fmts:
+        for N, K in ((2048, 2048), (12288, 2048), (2048, 6144)):
+            ws = [torch.randn(N, K, device=dev, generator=gen) * 0.02 for _ in range(reps)]
+            if fmt == "nvfp4":
+                lins = []
+                for w in ws:
+                    lin = torch.nn.Linear(K, N, bias=False, device=dev)
+                    with torch.no_grad():
+                        lin.weight.copy_(w)
+                    lins.append(lin)
+            else:
+                mod = b2.fp8block if fmt == "fp8" else b2.int8block
+                qw = [mod.quantize(w) for w in ws]
+            del ws
+            for M in (16, 128, 1024, 8192):
+                x = torch.randn(M, K, device=dev, generator=gen)
+                if fmt == "nvfp4":
+                    x = torch.where(torch.rand(M, K, device=dev, generator=gen) < 0.01, x * 20, x).bfloat16()
+                    fs = [b2.nvfp4.NVFP4Linear.of(lin, float(x.abs().max())) for lin in lins]
+                    qa, sa = b2.nvfp4.act_quant(x, fs[0].inv_g)
+                    gemm = [lambda f=f: torch.ops.basal.nvfp4_gemm(qa, sa, f.weight, f.weight_scale.view(torch.uint8),
+                                                                  f.alpha, M, torch.bfloat16) for f in fs]
+                    linear = [lambda f=f: f(x) for f in fs]
+                    wbytes, abytes = N * K // 2 + N * K // 16, M * K // 2 + M * K // 16
+                else:
+                    x = x.bfloat16()
+                    qa, sa = mod.act_quant(x)
+                    gemm = [lambda q=q, s=s: mod.gemm(qa, sa, q, s, torch.bfloat16) for q, s in qw]
+                    linear = [lambda q=q, s=s: mod.linear(x, q, s) for q, s in qw]
+                    wbytes, abytes = N * K + 4 * (N // 128) * (K // 128), M * K + 4 * M * (K // 128)
+
+                def body(fns):
+                    flush.sum()
+                    for fn in fns:
+                        fn()
+                tg = (graph_us(lambda: body(gemm)) - base) / reps
+                tl = (graph_us(lambda: body(linear)) - base) / reps
+                byts = wbytes + abytes + 2 * M * N
+                print(json.dumps({
+                    "sweep": "C3" if fmt == "nvfp4" else ("C4" if fmt == "int8" else "C3/C4 shapes, FP8"),
+                    "format": fmt, "M": M, "N": N, "K": K, "gemm_us": round(tg, 2),
+                    "gemm_tflops": round(2 * M * N * K / tg / 1e6, 1), "gemm_gbs": round(byts / tg / 1e3, 1),
+                    "gemm_hbm_frac": round(byts / tg / 1e3 / pk["hbm_gbs"], 3), "linear_us": round(tl, 2),
+                    "kernel": ("nvfp4" if fmt == "nvfp4" else ("few-rows" if M <= 64 else "block"))}), flush=True)
+    print(json.dumps({"faults": b2._lib.device_faults(0), "hbm_peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -351,7 +458,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
+    ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout) "
+                    "instead of the benchmark")
     args = ap.parse_args()
+    if args.sweep:
+        run_sweep(args.sweep.split(","))
+        return
     if args.case:
         run_case(args.case)
         return
