@@ -311,6 +311,7 @@ CASES = {
     # name: (format, M, N, K) -- the small cases the committed ncu summaries were captured on (inputs > L2, a few
     # GB on the device): 2 untimed launches, then 3 launches of the kernel under study
     "fp8_gemm": ("fp8", 65536, 5120, 2048),
+    "fp8_gemm_few": ("fp8", 16, 12288, 2048),  # the few-rows (weight-streaming) kernel; ncu flushes L2 per pass
     "int8_gemm": ("int8", 65536, 5120, 2048),
     "fp8_act_quant": ("fp8", 65536, 0, 2048),
     "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
