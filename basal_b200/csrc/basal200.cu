@@ -115,6 +115,25 @@ int grid_for(int dev, int64_t work_items, int per_block) {
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
+// Launches a kernel that may start while the kernel before it in the stream finishes, once that one allows it
+// (programmatic stream serialization). The kernel calls pdl_wait() before reading any earlier kernel's output and
+// before its first store. The weight quantisers are launched plainly and never allow an early start.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) != cudaSuccess) return launched();
+  return launched();
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // quantisers
 // ------------------------------------------------------------------------------------------------------------
@@ -132,15 +151,14 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   uint8_t* qb = static_cast<uint8_t*>(q);
   switch (xt) {
     case BASAL200_BF16:
-      act_quant_block_kernel<__nv_bfloat16, INT8><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), groups,
-                                                                         qb, s);
-      break;
+      return launch_pdl(act_quant_block_kernel<__nv_bfloat16, INT8>, grid, 256, 0, st,
+                        static_cast<const __nv_bfloat16*>(x), groups, qb, s);
     case BASAL200_F16:
-      act_quant_block_kernel<__half, INT8><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), groups, qb, s);
-      break;
+      return launch_pdl(act_quant_block_kernel<__half, INT8>, grid, 256, 0, st, static_cast<const __half*>(x), groups,
+                        qb, s);
     case BASAL200_F32:
-      act_quant_block_kernel<float, INT8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), groups, qb, s);
-      break;
+      return launch_pdl(act_quant_block_kernel<float, INT8>, grid, 256, 0, st, static_cast<const float*>(x), groups,
+                        qb, s);
     default:
       return BASAL200_ERR_DTYPE;
   }
@@ -188,15 +206,14 @@ int nvfp4_act(const void* x, int xt, const float* inv_g, int64_t M, int64_t K, u
   const dim3 grid((unsigned)(K / 64), (unsigned)(Mp / 128));
   switch (xt) {
     case BASAL200_BF16:
-      nvfp4_act_quant_kernel<__nv_bfloat16><<<grid, 512, 0, st>>>(static_cast<const __nv_bfloat16*>(x), inv_g, M,
-                                                                  K, q, s);
-      break;
+      return launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16>, grid, 512, 0, st,
+                        static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s);
     case BASAL200_F16:
-      nvfp4_act_quant_kernel<__half><<<grid, 512, 0, st>>>(static_cast<const __half*>(x), inv_g, M, K, q, s);
-      break;
+      return launch_pdl(nvfp4_act_quant_kernel<__half>, grid, 512, 0, st, static_cast<const __half*>(x), inv_g, M, K,
+                        q, s);
     case BASAL200_F32:
-      nvfp4_act_quant_kernel<float><<<grid, 512, 0, st>>>(static_cast<const float*>(x), inv_g, M, K, q, s);
-      break;
+      return launch_pdl(nvfp4_act_quant_kernel<float>, grid, 512, 0, st, static_cast<const float*>(x), inv_g, M, K,
+                        q, s);
     default:
       return BASAL200_ERR_DTYPE;
   }
@@ -247,8 +264,7 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
   int rc = set_smem(dev, slot, kern, blockgemm::smem_bytes<OUT>());
   if (rc) return rc;
   const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
-  kern<<<grid, blockgemm::NUM_THREADS, blockgemm::smem_bytes<OUT>(), st>>>(ta, tb, tc, p);
-  return launched();
+  return launch_pdl(kern, grid, blockgemm::NUM_THREADS, blockgemm::smem_bytes<OUT>(), st, ta, tb, tc, p);
 }
 
 // Few rows (M <= 64): the weight-streaming kernel, NT token rows a tile (32 or 64), one CTA per 128-row weight tile.
@@ -271,8 +287,7 @@ int small_gemm_launch(int dev, const void* q, const float* s, const void* w, con
   p.M = (int)M;
   p.N = (int)N;
   p.nkb = (int)(K / 128);
-  kern<<<(unsigned)(N / smallgemm::BW), smallgemm::Cfg<NT>::THREADS, smem, st>>>(tw, tt, p);
-  return launched();
+  return launch_pdl(kern, (unsigned)(N / smallgemm::BW), smallgemm::Cfg<NT>::THREADS, smem, st, tw, tt, p);
 }
 
 template <bool INT8, int OUT>
@@ -335,8 +350,7 @@ int fp4_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const
   int rc = set_smem(dev, kSlotFp4 + OUT, kern, fp4gemm::SMEM_BYTES);
   if (rc) return rc;
   const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
-  kern<<<grid, fp4gemm::NUM_THREADS, fp4gemm::SMEM_BYTES, st>>>(ta, tb, p);
-  return launched();
+  return launch_pdl(kern, grid, fp4gemm::NUM_THREADS, fp4gemm::SMEM_BYTES, st, ta, tb, p);
 }
 
 int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t* ws, const float* alpha,
@@ -388,22 +402,19 @@ int logits_typed(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head,
                  int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
   const dim3 grid((unsigned)((U + readout::TU - 1) / readout::TU), (unsigned)((R + readout::TR - 1) / readout::TR));
   constexpr int threads = readout::WARPS * 32;
-  if (!bias) {
-    readout::code_logits_kernel<TH, TW, float><<<grid, threads, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U, nullptr,
-                                                                          softcap, z);
-  } else if (bt == BASAL200_F32) {
-    readout::code_logits_kernel<TH, TW, float><<<grid, threads, 0, st>>>(h, R, D, ldh, head, V, ldw, ids, U,
-                                                                          static_cast<const float*>(bias), softcap, z);
-  } else if (bt == BASAL200_BF16) {
-    readout::code_logits_kernel<TH, TW, __nv_bfloat16><<<grid, threads, 0, st>>>(
-        h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z);
-  } else if (bt == BASAL200_F16) {
-    readout::code_logits_kernel<TH, TW, __half><<<grid, threads, 0, st>>>(
-        h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z);
-  } else {
-    return BASAL200_ERR_DTYPE;
-  }
-  return launched();
+  if (!bias)
+    return launch_pdl(readout::code_logits_kernel<TH, TW, float>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
+                      ids, U, static_cast<const float*>(nullptr), softcap, z);
+  if (bt == BASAL200_F32)
+    return launch_pdl(readout::code_logits_kernel<TH, TW, float>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
+                      ids, U, static_cast<const float*>(bias), softcap, z);
+  if (bt == BASAL200_BF16)
+    return launch_pdl(readout::code_logits_kernel<TH, TW, __nv_bfloat16>, grid, threads, 0, st, h, R, D, ldh, head, V,
+                      ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z);
+  if (bt == BASAL200_F16)
+    return launch_pdl(readout::code_logits_kernel<TH, TW, __half>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
+                      ids, U, static_cast<const __half*>(bias), softcap, z);
+  return BASAL200_ERR_DTYPE;
 }
 
 template <typename TH>
@@ -598,8 +609,8 @@ int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx
   if (!z || !idx || !p) return BASAL200_ERR_ARG;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
-  readout::code_probs_kernel<<<(unsigned)((R + 7) / 8), 256, 0, as_stream(stream)>>>(z, R, U, idx, pad, Kmax, p);
-  return launched();
+  return launch_pdl(readout::code_probs_kernel, (unsigned)((R + 7) / 8), 256, 0, as_stream(stream), z, R, U, idx, pad,
+                    Kmax, p);
 }
 
 unsigned basal200_device_faults(int device, int clear) {

@@ -185,6 +185,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (S::STAGING) tma_prefetch_desc(&tmC);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
+  pdl_launch();
+  pdl_wait();  // the set-up above ran while the kernel before this one finished
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

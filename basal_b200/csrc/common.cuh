@@ -37,6 +37,20 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// programmatic dependent launch: the library's kernels (but the weight quantisers) are launched so that they may
+// start while the kernel before them in the stream finishes, once that kernel allows it
+// ---------------------------------------------------------------------------------------------------------------
+// Waits until the kernels this one may have started ahead of have completed and their writes are visible. Every
+// kernel launched that way calls it before reading what an earlier kernel may have written and before its first
+// store; without a kernel ahead it returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel of the stream start launching (it still waits for this one in its pdl_wait). The weight
+// quantisers never call it, so what follows them (a GEMM that loads weights before its pdl_wait) starts only after
+// the weights are written.
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
+  pdl_launch();
+  pdl_wait();  // the set-up above ran while the kernel before this one finished
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

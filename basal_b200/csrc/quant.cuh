@@ -100,6 +100,8 @@ __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
 template <typename T, bool INT8>
 __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups,
                                                               uint8_t* __restrict__ q, float* __restrict__ s) {
+  pdl_launch();
+  pdl_wait();
   constexpr float kQmax = INT8 ? 127.0f : 448.0f;
   const int lane = threadIdx.x & 31;
   const int half = lane >> 4, l = lane & 15;
@@ -194,6 +196,8 @@ template <typename T>
 __global__ void __launch_bounds__(512) nvfp4_act_quant_kernel(const T* __restrict__ x, const float* __restrict__ inv_g_p,
                                                               int64_t M, int64_t K, uint8_t* __restrict__ q,
                                                               uint8_t* __restrict__ s) {
+  pdl_launch();
+  pdl_wait();
   __shared__ __align__(16) uint8_t sbuf[512];
   const int64_t tile_r = blockIdx.y;
   const int64_t c64 = blockIdx.x;

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(WARPS * 32) code_logits_kernel(const TH* __res
                                                                  float softcap, float* __restrict__ z) {
   __shared__ float part[WARPS][WR * WU];
   __shared__ int64_t sid[WU];
+  pdl_launch();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = (int64_t)blockIdx.y * TR;
   const int64_t u0 = (int64_t)blockIdx.x * TU;
@@ -117,6 +119,8 @@ __global__ void __launch_bounds__(256) code_probs_kernel(const float* __restrict
                                                          const int64_t* __restrict__ idx,
                                                          const uint8_t* __restrict__ pad, int64_t Kmax,
                                                          float* __restrict__ p) {
+  pdl_launch();
+  pdl_wait();
   const int64_t r = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (r >= R) return;

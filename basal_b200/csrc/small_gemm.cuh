@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
     tma_prefetch_desc(&tmT);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, C::TMEM_COLS);
+  pdl_launch();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -157,7 +158,17 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
       // ---------------- TMA producer ----------------
       if (lane == 0) {
         uint32_t filled = 0, last_phase = 0;
-        for (int kb = 0; kb < nkb; ++kb) {
+        // the weights of the first ring of slices load while the kernel before this one finishes (no kernel that
+        // lets its successor start early writes weights); the tokens, an earlier kernel's output, after pdl_wait
+        const int pre = nkb < STAGES ? nkb : STAGES;
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&sh.full[kb], C::STAGE_BYTES);
+          tma_load_2d(sh.stage[kb], &tmW, &sh.full[kb], kb * BK, tile * BW);
+          filled |= 1u << kb;
+        }
+        pdl_wait();
+        for (int kb = 0; kb < pre; ++kb) tma_load_2d(sh.stage[kb] + W_BYTES, &tmT, &sh.full[kb], kb * BK, 0);
+        for (int kb = pre; kb < nkb; ++kb) {
           const int stage = kb % STAGES;
           const uint32_t phase = (uint32_t)(kb / STAGES) & 1;
           if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) break;
@@ -214,7 +225,9 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
       const int et = ew * 32 + lane;   // index among the promotion threads
       constexpr int ETHREADS = C::EPI_WARPS * 32;
       const uint32_t tcol = tmem + ((uint32_t)(quad * 32) << 16) + half * 32;
-      // every a_s * b_s of the tile, while the first slices load (token j's scales are contiguous)
+      // every a_s * b_s of the tile, while the first slices load (token j's scales are contiguous); the scales and
+      // this thread's stores come after the kernels before this one
+      pdl_wait();
       for (int idx = et; idx < NT * nkb; idx += ETHREADS) {
         const int j = idx / nkb, kb = idx - j * nkb;
         sh.sc[kb][j] = j < p.M ? __ldg(p.s + (int64_t)j * nkb + kb) * __ldg(p.ws + (int64_t)tile * nkb + kb) : 0.f;
