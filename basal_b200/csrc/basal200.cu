@@ -382,6 +382,7 @@ int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t
   p.nchunk = (int)(K / 64);
   p.nkb = (p.nchunk + 3) / 4;
   p.tiles_n = (int)((N + fp4gemm::BN - 1) / fp4gemm::BN);
+  p.nblk_b = (int)((N + 127) / 128);
   const int64_t tiles = Mp / fp4gemm::BM * p.tiles_n;
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;

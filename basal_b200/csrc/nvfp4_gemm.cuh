@@ -6,12 +6,20 @@
 // an instruction). A [Mp, K/2] and B [N, K/2] are packed e2m1 (even feature in the low nibble), K-major. The scales
 // are consumed as the reference stores them, in the 128 x 4 tile swizzle (512 bytes for 128 rows x 64 features):
 // that tile, moved into TMEM by tcgen05.cp's 32x128b.warpx4 shape, is the layout the MMA reads (lane l, column c,
-// byte j = scale of row 32 c + l % 32, feature group j). Persistent CTAs walk 128 x 128 output tiles:
-//   warp 0      producer: TMA of A / B (256 features = 128 bytes a stage, 128-byte swizzle) and plain bulk copies of
-//               the stage's 4 + 4 scale tiles into a 5-stage ring
-//   warp 1      MMA issuer: tcgen05.cp of the stage's scale tiles to TMEM, 4 MMAs, commit
-//   warp 2      TMEM allocation: 2 accumulators of 128 columns, then 32 scale columns per stage
-//   warps 4-11  epilogue: tcgen05.ld, times alpha, (+ bias), cast, store
+// byte j = scale of row 32 c + l % 32, feature group j); the 256 rows of a B tile take 8 columns, the first 128 rows
+// in the first 4. Persistent CTAs walk 128 x 256 output tiles:
+//   warp 0       producer: TMA of A / B (256 features = 128 bytes a stage, 128-byte swizzle) and plain bulk copies of
+//                the stage's 4 + 8 scale tiles into a 4-stage ring
+//   warps 2, 3   scale issuers: tcgen05.cp of the stage's scale tiles to its TMEM columns (warp 2 those of A and of
+//                the B tile's first 128 rows, warp 3 the second 128 rows), then a commit (sfready)
+//   warp 1       MMA issuer: 4 MMAs of 128 x 256 x 64 a stage once its scales are in TMEM, commit
+//   warps 4-19   epilogue: tcgen05.ld of 32 rows x 64 columns a warp, release of the accumulator, times alpha,
+//                (+ bias), cast, store
+// The tcgen05 instructions cost the issuing thread about as long to issue as a 128 x 128 x 64 MMA takes to run: a
+// 128 x 128 tile whose one thread issued a stage's 8 copies and 4 MMAs ran at 285 us (M = 8192, N = 12288,
+// K = 2048), 177 / 180 us with either half switched off. N = 256 halves the MMAs per product and the copies are
+// spread over two threads. The accumulator's 256 columns and 4 stages x 48 scale columns fill TMEM, so there is
+// one accumulator: the epilogue reads it out to registers and releases it before it stores.
 #pragma once
 #include "block_gemm.cuh"
 
@@ -19,28 +27,31 @@ namespace b200 {
 namespace fp4gemm {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = 256;
 constexpr int BKB = 128;  // bytes of K per stage (256 e2m1 values = 4 scale tiles)
-constexpr int STAGES = 5;
+constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB;
 constexpr int B_BYTES = BN * BKB;
-constexpr int SF_BYTES = 4 * 512;
-constexpr int NUM_THREADS = 384;
+constexpr int SF_BYTES = 4 * 512;  // 4 scale tiles of 128 rows
+constexpr int NUM_EPI_WARPS = 16;
 constexpr int EPI_WARP0 = 4;
-constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t SF_COL0 = 2 * BN;  // scale columns after the two accumulators
-constexpr uint32_t SF_COLS_PER_STAGE = 32;
+constexpr uint32_t SF_COL0 = BN;  // scale columns after the accumulator
+constexpr uint32_t SFA_COLS = 16;  // 4 chunks x 4 columns
+constexpr uint32_t SF_COLS_PER_STAGE = SFA_COLS + 32;  // + 4 chunks x 8 columns of B
+static_assert(SF_COL0 + STAGES * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
 
 struct Shared {
   uint8_t a[STAGES][A_BYTES];
   uint8_t b[STAGES][B_BYTES];
   uint8_t sfa[STAGES][SF_BYTES];
-  uint8_t sfb[STAGES][SF_BYTES];
+  uint8_t sfb[STAGES][2][SF_BYTES];  // the B tile's two 128-row halves
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t sfready[STAGES];
+  uint64_t tfull;
+  uint64_t tempty;
   uint64_t mdrain;
   uint32_t tmem_base;
   int abort;
@@ -53,7 +64,7 @@ struct Params {
   const float* alpha;  // [1]
   const void* bias;    // [N] output type, or null
   void* y;             // [M, N]
-  int M, N, nchunk, nkb, tiles_n, num_tiles;
+  int M, N, nchunk, nkb, tiles_n, num_tiles, nblk_b;  // nblk_b = ceil(N / 128)
 };
 
 template <int OUT>
@@ -69,12 +80,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
+      mbar_init(&sh.sfready[s], 2);  // the two scale issuers
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sh.tfull[b], 1);
-      mbar_init(&sh.tempty[b], NUM_EPI_WARPS);
-    }
-    mbar_init(&sh.mdrain, 1);
+    mbar_init(&sh.tfull, 1);
+    mbar_init(&sh.tempty, NUM_EPI_WARPS);
+    mbar_init(&sh.mdrain, 3);  // the MMA issuer and the two scale issuers
     sh.abort = 0;
     fence_barrier_init();
   }
@@ -99,17 +109,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
+        const bool b_hi = 2 * tn + 1 < p.nblk_b;  // the tile's second 128 rows of B exist
         for (int kb = 0; kb < p.nkb; ++kb) {
           const int nch = min(4, p.nchunk - kb * 4);
           if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + 2 * nch * 512);
+          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + (b_hi ? 3 : 2) * nch * 512);
           tma_load_2d(sh.a[stage], &tmA, &sh.full[stage], kb * BKB, tm * BM);
           tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BKB, tn * BN);
           bulk_load(sh.sfa[stage], p.sa + ((int64_t)tm * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
-          bulk_load(sh.sfb[stage], p.sb + ((int64_t)tn * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
+          bulk_load(sh.sfb[stage][0], p.sb + ((int64_t)(2 * tn) * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
+          if (b_hi)
+            bulk_load(sh.sfb[stage][1], p.sb + ((int64_t)(2 * tn + 1) * c4 + kb * 4) * 512, nch * 512,
+                      &sh.full[stage]);
           filled |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -130,10 +144,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0, acc = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const uint32_t buf = acc & 1, aph = (acc >> 1) & 1;
-        if (!mbar_wait(&sh.tempty[buf], aph ^ 1, abort_flag, kFaultTimeoutMma)) break;
+        if (!mbar_wait(&sh.tempty, (acc & 1) ^ 1, abort_flag, kFaultTimeoutMma)) break;
         tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < p.nkb; ++kb) {
+          const int nch = min(4, p.nchunk - kb * 4);
+          // the stage's operands have landed and its scales are in TMEM (the scale issuers' commits)
+          if (!mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma) ||
+              !mbar_wait(&sh.sfready[stage], phase, abort_flag, kFaultTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfcol = tmem + SF_COL0 + stage * SF_COLS_PER_STAGE;
+          const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
+          const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
+          for (int c = 0; c < nch; ++c)
+            mma_mxf4nvf4(tmem, ad + 2 * c, bd + 2 * c, idesc, sfcol + c * 4, sfcol + SFA_COLS + c * 8,
+                         (kb | c) != 0);
+          mma_commit(&sh.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&sh.tfull);
+        ++acc;
+      }
+      mma_commit(&sh.mdrain);
+      blockgemm::drain_wait(&sh.mdrain, 0);
+    }
+  } else if (warp < EPI_WARP0) {
+    // scale issuers: a stage's scale tiles go to its TMEM columns once the stage has landed. The columns' previous
+    // MMAs have finished by then (the producer refilled the stage only after their commit on `empty`).
+    if (lane == 0) {
+      const bool first = warp == 2;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int tn = tile % p.tiles_n;
+        const bool b_hi = 2 * tn + 1 < p.nblk_b;
         for (int kb = 0; kb < p.nkb; ++kb) {
           const int nch = min(4, p.nchunk - kb * 4);
           if (!mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma)) {
@@ -142,62 +193,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t sfcol = tmem + SF_COL0 + stage * SF_COLS_PER_STAGE;
-          for (int c = 0; c < nch; ++c) {
-            tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[stage] + c * 512)));
-            tmem_cp_32x128b_x4(sfcol + 16 + c * 4, desc_plain16(smem_u32(sh.sfb[stage] + c * 512)));
+          if (first) {
+            for (int c = 0; c < nch; ++c) {
+              tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[stage] + c * 512)));
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8, desc_plain16(smem_u32(sh.sfb[stage][0] + c * 512)));
+            }
+          } else if (b_hi) {  // else the columns stay stale: they scale only output columns >= N
+            for (int c = 0; c < nch; ++c)
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8 + 4, desc_plain16(smem_u32(sh.sfb[stage][1] + c * 512)));
           }
-          const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
-          const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
-          for (int c = 0; c < nch; ++c)
-            mma_mxf4nvf4(d, ad + 2 * c, bd + 2 * c, idesc, sfcol + c * 4, sfcol + 16 + c * 4, (kb | c) != 0);
-          mma_commit(&sh.empty[stage]);
+          mma_commit(&sh.sfready[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (!ok) break;
-        mma_commit(&sh.tfull[buf]);
-        ++acc;
       }
       mma_commit(&sh.mdrain);
       blockgemm::drain_wait(&sh.mdrain, 0);
     }
-  } else if (warp >= EPI_WARP0) {
+  } else {
     using OutT = typename blockgemm::Store<OUT>::T;
     const int ew = warp - EPI_WARP0;
-    const int half = ew >> 2;   // which 64 columns of the tile
-    const int quad = warp & 3;
+    const int part = ew >> 2;   // which 64 columns of the tile
+    const int quad = warp & 3;  // the TMEM lane quadrant this warp may read
     const float alpha = __ldg(p.alpha);
     uint32_t acc_cnt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int row = tm * BM + quad * 32 + lane;
-      const uint32_t buf = acc_cnt & 1, ph = (acc_cnt >> 1) & 1;
-      if (!blockgemm::warp_wait(&sh.tfull[buf], ph, abort_flag, kFaultTimeoutEpilogue)) break;
+      if (!blockgemm::warp_wait(&sh.tfull, acc_cnt & 1, abort_flag, kFaultTimeoutEpilogue)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + half * 64;
-      float v[64];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c * 16, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[c * 16 + j] = __fmul_rn(__uint_as_float(r[j]), alpha);
-      }
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + part * 64;
+      uint32_t r0[32], r1[32];
+      tmem_ld32_issue(taddr, r0);
+      tmem_ld32_issue(taddr + 32, r1);
+      tmem_ld_wait32(r0);
+      tmem_ld_wait32(r1);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.tempty[buf]);
+      if (lane == 0) mbar_arrive(&sh.tempty);
       ++acc_cnt;
-      const int n0 = tn * BN + half * 64;
+      const int n0 = tn * BN + part * 64;
       if (row < p.M) {
         OutT* dst = reinterpret_cast<OutT*>(p.y) + (int64_t)row * p.N + n0;
         const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
 #pragma unroll
         for (int c = 0; c < 64; c += 8) {
+          float v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            v[j] = __fmul_rn(__uint_as_float(c < 32 ? r0[c + j] : r1[c - 32 + j]), alpha);
           if (n0 + c < p.N)  // N % 16 == 0: an 8-column group is whole or absent
-            blockgemm::Store<OUT>::vec8(dst + c, v + c, bias ? bias + c : nullptr);
+            blockgemm::Store<OUT>::vec8(dst + c, v, bias ? bias + c : nullptr);
         }
       }
     }

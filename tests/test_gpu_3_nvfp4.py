@@ -81,3 +81,32 @@ def test_c3_sweep_by_row_samples(b2, M, N, K):
     got = y[rows.cuda()].float().cpu().numpy()
     err = np.abs(got - ref).max(1) / np.abs(ref).max(1)
     assert err.max() < 1e-2, err.max()
+
+
+@pytest.mark.parametrize("M, N", [(300, 640), (128, 272)])
+def test_output_casts_and_bias(b2, M, N):
+    """bf16 / fp16 outputs are the fp32 output cast; a bias in the output type is added to the cast value and rounded
+    again (torch adds a bias to the cast product). Called through the C-ABI entry point, which takes the bias."""
+    from basal_b200 import _lib
+    K = 512
+    g = torch.Generator().manual_seed(M + N)
+    w = torch.randn(N, K, generator=g) * 0.02
+    x = c3_input(M, K, seed=N)
+    codes, scales, wg = b2.nvfp4.quantize(w.cuda())
+    xg = onv.global_scale(float(x.float().abs().max()))
+    inv_g = torch.tensor([1.0 / xg], dtype=torch.float32).cuda()
+    alpha = (wg * xg).float().cuda()
+    q, s = b2.nvfp4.act_quant(x.cuda(), inv_g)
+    ws = scales.view(torch.uint8)
+    y32 = torch.ops.basal.nvfp4_gemm(q, s, codes, ws, alpha, M, torch.float32)
+    for dt in (torch.bfloat16, torch.float16):
+        bias = (torch.randn(N, generator=g) * 0.1).to(dt).cuda()
+        for b in (None, bias):
+            y = torch.empty(M, N, dtype=dt, device="cuda")
+            _lib.call("basal200_nvfp4_gemm", y.device, _lib.ptr(q), _lib.ptr(s), _lib.ptr(codes), _lib.ptr(ws),
+                      _lib.ptr(alpha), _lib.ptr(b), _lib.ptr(y), _lib.code(dt), M, N, K)
+            want = y32.to(dt)
+            if b is not None:
+                want = (want.float() + b.float()).to(dt)
+            assert torch.equal(y, want), dt
+    assert b2._lib.device_faults(0) == 0
