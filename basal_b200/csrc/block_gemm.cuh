@@ -95,14 +95,16 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
-// Casts and stores of fp32 results: vec8 writes 8 consecutive outputs (one 16- or 32-byte store); a bias in the
-// output type is added to the cast value and rounded again, as torch adds a bias to the cast product.
+// Casts and stores of fp32 results: pack casts the PER values of one 16-byte chunk, vec8 writes 8 consecutive
+// outputs (one 16- or 32-byte store); a bias in the output type is added to the cast value and rounded again, as
+// torch adds a bias to the cast product.
 template <int OUT>
 struct Store;
 template <>
 struct Store<BASAL200_BF16> {
   using T = __nv_bfloat16;
-  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+  static constexpr int PER = 8;
+  __device__ __forceinline__ static uint4 pack(const float* v, const T* bias) {
     uint4 u;
     uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
@@ -115,13 +117,17 @@ struct Store<BASAL200_BF16> {
       }
       w[i] = *reinterpret_cast<uint32_t*>(&h);
     }
-    *reinterpret_cast<uint4*>(dst) = u;
+    return u;
+  }
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+    *reinterpret_cast<uint4*>(dst) = pack(v, bias);
   }
 };
 template <>
 struct Store<BASAL200_F16> {
   using T = __half;
-  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+  static constexpr int PER = 8;
+  __device__ __forceinline__ static uint4 pack(const float* v, const T* bias) {
     uint4 u;
     uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
@@ -134,26 +140,66 @@ struct Store<BASAL200_F16> {
       }
       w[i] = *reinterpret_cast<uint32_t*>(&h);
     }
-    *reinterpret_cast<uint4*>(dst) = u;
+    return u;
+  }
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+    *reinterpret_cast<uint4*>(dst) = pack(v, bias);
   }
 };
 template <>
 struct Store<BASAL200_F32> {
   using T = float;
-  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
-#pragma unroll
-    for (int c = 0; c < 8; c += 4) {
-      float4 f = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-      if (bias) {
-        f.x = __fadd_rn(f.x, bias[c]);
-        f.y = __fadd_rn(f.y, bias[c + 1]);
-        f.z = __fadd_rn(f.z, bias[c + 2]);
-        f.w = __fadd_rn(f.w, bias[c + 3]);
-      }
-      *reinterpret_cast<float4*>(dst + c) = f;
+  static constexpr int PER = 4;
+  __device__ __forceinline__ static uint4 pack(const float* v, const T* bias) {
+    float4 f = make_float4(v[0], v[1], v[2], v[3]);
+    if (bias) {
+      f.x = __fadd_rn(f.x, bias[0]);
+      f.y = __fadd_rn(f.y, bias[1]);
+      f.z = __fadd_rn(f.z, bias[2]);
+      f.w = __fadd_rn(f.w, bias[3]);
     }
+    return make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+  }
+  __device__ __forceinline__ static void vec8(T* dst, const float* v, const T* bias) {
+    *reinterpret_cast<uint4*>(dst) = pack(v, bias);
+    *reinterpret_cast<uint4*>(dst + 4) = pack(v + 4, bias ? bias + 4 : nullptr);
   }
 };
+
+// Redistributes a warp's 32 rows x 8 chunks of 16 bytes (lane = row, c[j] = chunk j) so that lane L holds in c[i]
+// chunk L % 8 of row 4 i + L / 8, and a store of c[i] by the warp writes 4 whole row segments of 128 bytes: three
+// shuffle exchanges of a chunk-index bit with a lane bit (chunk bit k with lane bit k + 2), then one fixed lane
+// rotation.
+__device__ __forceinline__ void rows_to_segments(uint4 (&c)[8], int lane) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int m = 4 << k;
+    const bool hi = lane & m;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      if (s & (1 << k)) continue;
+      const int t = s | (1 << k);
+      const uint4 send = hi ? c[s] : c[t];
+      uint4 recv;
+      recv.x = __shfl_xor_sync(0xffffffffu, send.x, m);
+      recv.y = __shfl_xor_sync(0xffffffffu, send.y, m);
+      recv.z = __shfl_xor_sync(0xffffffffu, send.z, m);
+      recv.w = __shfl_xor_sync(0xffffffffu, send.w, m);
+      if (hi)
+        c[s] = recv;
+      else
+        c[t] = recv;
+    }
+  }
+  const int src = ((lane & 7) << 2) | (lane >> 3);
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    c[s].x = __shfl_sync(0xffffffffu, c[s].x, src);
+    c[s].y = __shfl_sync(0xffffffffu, c[s].y, src);
+    c[s].z = __shfl_sync(0xffffffffu, c[s].z, src);
+    c[s].w = __shfl_sync(0xffffffffu, c[s].w, src);
+  }
+}
 
 template <bool INT8, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)

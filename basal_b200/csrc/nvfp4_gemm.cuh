@@ -14,7 +14,7 @@
 //                the B tile's first 128 rows, warp 3 the second 128 rows), then a commit (sfready)
 //   warp 1       MMA issuer: 4 MMAs of 128 x 256 x 64 a stage once its scales are in TMEM, commit
 //   warps 4-19   epilogue: tcgen05.ld of 32 rows x 64 columns a warp, release of the accumulator, times alpha,
-//                (+ bias), cast, store
+//                (+ bias), cast, a warp transpose of 16-byte chunks, stores of whole 128-byte row segments
 // The tcgen05 instructions cost the issuing thread about as long to issue as a 128 x 128 x 64 MMA takes to run: a
 // 128 x 128 tile whose one thread issued a stage's 8 copies and 4 MMAs ran at 285 us (M = 8192, N = 12288,
 // K = 2048), 177 / 180 us with either half switched off. N = 256 halves the MMAs per product and the copies are
@@ -221,7 +221,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_cnt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-      const int row = tm * BM + quad * 32 + lane;
       if (!blockgemm::warp_wait(&sh.tfull, acc_cnt & 1, abort_flag, kFaultTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + part * 64;
@@ -234,18 +233,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tempty);
       ++acc_cnt;
-      const int n0 = tn * BN + part * 64;
-      if (row < p.M) {
-        OutT* dst = reinterpret_cast<OutT*>(p.y) + (int64_t)row * p.N + n0;
-        const OutT* bias = p.bias ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
+      // cast this lane's row, then trade chunks across the warp so that each store writes 4 rows x 128 bytes
+      // (a store of one 16-byte chunk from each of 32 rows kept the SM's write path busy for most of a tile)
+      constexpr int PER = blockgemm::Store<OUT>::PER;  // outputs per 16-byte chunk
+      const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
 #pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          float v[8];
+      for (int blk = 0; blk < 64 / (8 * PER); ++blk) {
+        const int nb = tn * BN + part * 64 + blk * 8 * PER;  // first column of the 8 chunks
+        uint4 c[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            v[j] = __fmul_rn(__uint_as_float(c < 32 ? r0[c + j] : r1[c - 32 + j]), alpha);
-          if (n0 + c < p.N)  // N % 16 == 0: an 8-column group is whole or absent
-            blockgemm::Store<OUT>::vec8(dst + c, v, bias ? bias + c : nullptr);
+        for (int j = 0; j < 8; ++j) {
+          float v[PER];
+#pragma unroll
+          for (int e = 0; e < PER; ++e) {
+            const int col = blk * 8 * PER + j * PER + e;
+            v[e] = __fmul_rn(__uint_as_float(col < 32 ? r0[col] : r1[col - 32]), alpha);
+          }
+          // N % 16 == 0: a chunk is whole or absent
+          c[j] = blockgemm::Store<OUT>::pack(v, bias && nb + j * PER < p.N ? bias + nb + j * PER : nullptr);
+        }
+        blockgemm::rows_to_segments(c, lane);
+        const int col = nb + (lane & 7) * PER;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = tm * BM + quad * 32 + 4 * i + (lane >> 3);
+          if (row < p.M && col < p.N)
+            *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.y) + (int64_t)row * p.N + col) = c[i];
         }
       }
     }
