@@ -8,8 +8,8 @@
 // that tile, moved into TMEM by tcgen05.cp's 32x128b.warpx4 shape, is the layout the MMA reads (lane l, column c,
 // byte j = scale of row 32 c + l % 32, feature group j); the 256 rows of a B tile take 8 columns, the first 128 rows
 // in the first 4. Persistent CTAs walk 128 x 256 output tiles:
-//   warp 0       producer: TMA of A / B (256 features = 128 bytes a stage, 128-byte swizzle) and plain bulk copies of
-//                the stage's 4 + 8 scale tiles into a 4-stage ring
+//   warp 0       producer: TMA of A / B (256 features = 128 bytes a stage, 128-byte swizzle) into a 4-stage ring and
+//                plain bulk copies of the next step's 4 + 8 scale tiles into a 5-slot ring
 //   warps 2, 3   scale issuers: tcgen05.cp of the stage's scale tiles to its TMEM columns (warp 2 those of A and of
 //                the B tile's first 128 rows, warp 3 the second 128 rows), then a commit (sfready)
 //   warp 1       MMA issuer: 4 MMAs of 128 x 256 x 64 a stage once its scales are in TMEM, commit
@@ -18,8 +18,11 @@
 // The tcgen05 instructions cost the issuing thread about as long to issue as a 128 x 128 x 64 MMA takes to run: a
 // 128 x 128 tile whose one thread issued a stage's 8 copies and 4 MMAs ran at 285 us (M = 8192, N = 12288,
 // K = 2048), 177 / 180 us with either half switched off. N = 256 halves the MMAs per product and the copies are
-// spread over two threads. The accumulator's 256 columns and 4 stages x 48 scale columns fill TMEM, so there is
-// one accumulator: the epilogue reads it out to registers and releases it before it stores.
+// spread over two threads. A step's scales are loaded one step ahead of its operands, into a ring one slot deeper than
+// the operands', so that they are in TMEM before the operands land (the operand ring's round trip was load latency +
+// copies + MMA issue; now it is load latency + MMA issue). The accumulator's 256 columns and 5 slots x 48 scale
+// columns fill TMEM, so there is one accumulator: the epilogue reads it out to registers and releases it before it
+// stores.
 #pragma once
 #include "block_gemm.cuh"
 
@@ -29,7 +32,8 @@ namespace fp4gemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BKB = 128;  // bytes of K per stage (256 e2m1 values = 4 scale tiles)
-constexpr int STAGES = 4;
+constexpr int STAGES = 4;     // operand (A / B) ring
+constexpr int SF_SLOTS = STAGES + 1;  // scale ring: a step's scales are loaded one step ahead of its operands
 constexpr int A_BYTES = BM * BKB;
 constexpr int B_BYTES = BN * BKB;
 constexpr int SF_BYTES = 4 * 512;  // 4 scale tiles of 128 rows
@@ -40,16 +44,17 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t SF_COL0 = BN;  // scale columns after the accumulator
 constexpr uint32_t SFA_COLS = 16;  // 4 chunks x 4 columns
 constexpr uint32_t SF_COLS_PER_STAGE = SFA_COLS + 32;  // + 4 chunks x 8 columns of B
-static_assert(SF_COL0 + STAGES * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
+static_assert(SF_COL0 + SF_SLOTS * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
 
 struct Shared {
   uint8_t a[STAGES][A_BYTES];
   uint8_t b[STAGES][B_BYTES];
-  uint8_t sfa[STAGES][SF_BYTES];
-  uint8_t sfb[STAGES][2][SF_BYTES];  // the B tile's two 128-row halves
+  uint8_t sfa[SF_SLOTS][SF_BYTES];
+  uint8_t sfb[SF_SLOTS][2][SF_BYTES];  // the B tile's two 128-row halves
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t sfready[STAGES];
+  uint64_t sffull[SF_SLOTS];
+  uint64_t sfready[SF_SLOTS];
   uint64_t tfull;
   uint64_t tempty;
   uint64_t mdrain;
@@ -57,6 +62,7 @@ struct Shared {
   int abort;
 };
 constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+static_assert(SMEM_BYTES <= 232448, "227 KB of shared memory a CTA");
 
 struct Params {
   const uint8_t* sa;   // swizzled scales of A: Mp/128 x (K/64) tiles
@@ -80,6 +86,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
+    }
+    for (int s = 0; s < SF_SLOTS; ++s) {
+      mbar_init(&sh.sffull[s], 1);
       mbar_init(&sh.sfready[s], 2);  // the two scale issuers
     }
     mbar_init(&sh.tfull, 1);
@@ -104,58 +113,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, filled = 0, last_phase = 0;
+      // step g = the g-th (tile, k-block) of this CTA: its operands go to stage g % STAGES, its scales (loaded one
+      // step earlier, after the wait on `empty` that frees step g - STAGES's slots) to slot g % SF_SLOTS
+      int stage = 0, slot = 0, sf_tile = blockIdx.x, sf_kb = 0;
+      uint32_t phase = 0, sf_phase = 0, filled = 0, last_phase = 0, sf_filled = 0, sf_last = 0;
+      auto load_scales = [&]() {
+        if (sf_tile >= p.num_tiles) return;
+        const int tm = sf_tile / p.tiles_n, tn = sf_tile - tm * p.tiles_n;
+        const bool b_hi = 2 * tn + 1 < p.nblk_b;  // the tile's second 128 rows of B exist
+        const int nch = min(4, p.nchunk - sf_kb * 4);
+        mbar_arrive_expect_tx(&sh.sffull[slot], (b_hi ? 3 : 2) * nch * 512);
+        bulk_load(sh.sfa[slot], p.sa + ((int64_t)tm * c4 + sf_kb * 4) * 512, nch * 512, &sh.sffull[slot]);
+        bulk_load(sh.sfb[slot][0], p.sb + ((int64_t)(2 * tn) * c4 + sf_kb * 4) * 512, nch * 512, &sh.sffull[slot]);
+        if (b_hi)
+          bulk_load(sh.sfb[slot][1], p.sb + ((int64_t)(2 * tn + 1) * c4 + sf_kb * 4) * 512, nch * 512,
+                    &sh.sffull[slot]);
+        sf_filled |= 1u << slot;
+        sf_last = (sf_last & ~(1u << slot)) | (sf_phase << slot);
+        if (++slot == SF_SLOTS) {
+          slot = 0;
+          sf_phase ^= 1;
+        }
+        if (++sf_kb == p.nkb) {
+          sf_kb = 0;
+          sf_tile += gridDim.x;
+        }
+      };
+      load_scales();  // step 0
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
-        const bool b_hi = 2 * tn + 1 < p.nblk_b;  // the tile's second 128 rows of B exist
         for (int kb = 0; kb < p.nkb; ++kb) {
-          const int nch = min(4, p.nchunk - kb * 4);
           if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES + (b_hi ? 3 : 2) * nch * 512);
+          mbar_arrive_expect_tx(&sh.full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sh.a[stage], &tmA, &sh.full[stage], kb * BKB, tm * BM);
           tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BKB, tn * BN);
-          bulk_load(sh.sfa[stage], p.sa + ((int64_t)tm * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
-          bulk_load(sh.sfb[stage][0], p.sb + ((int64_t)(2 * tn) * c4 + kb * 4) * 512, nch * 512, &sh.full[stage]);
-          if (b_hi)
-            bulk_load(sh.sfb[stage][1], p.sb + ((int64_t)(2 * tn + 1) * c4 + kb * 4) * 512, nch * 512,
-                      &sh.full[stage]);
           filled |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
+          load_scales();  // the next step's
         }
       }
       if (!ok) {
         for (int s = 0; s < STAGES; ++s)
           if (filled & (1u << s)) blockgemm::drain_wait(&sh.full[s], (last_phase >> s) & 1);
+        for (int s = 0; s < SF_SLOTS; ++s)
+          if (sf_filled & (1u << s)) blockgemm::drain_wait(&sh.sffull[s], (sf_last >> s) & 1);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_block_scaled(1, 1, BM, BN);  // e2m1 x e2m1, ue4m3 scales, f32 accumulate
-      int stage = 0;
-      uint32_t phase = 0, acc = 0;
+      int stage = 0, slot = 0;
+      uint32_t phase = 0, sf_phase = 0, acc = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         if (!mbar_wait(&sh.tempty, (acc & 1) ^ 1, abort_flag, kFaultTimeoutMma)) break;
         tc_fence_after();
         for (int kb = 0; kb < p.nkb; ++kb) {
           const int nch = min(4, p.nchunk - kb * 4);
-          // the stage's operands have landed and its scales are in TMEM (the scale issuers' commits)
-          if (!mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma) ||
-              !mbar_wait(&sh.sfready[stage], phase, abort_flag, kFaultTimeoutMma)) {
+          // the step's scales are in TMEM (the scale issuers' commits) and its operands have landed
+          if (!mbar_wait(&sh.sfready[slot], sf_phase, abort_flag, kFaultTimeoutMma) ||
+              !mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sfcol = tmem + SF_COL0 + stage * SF_COLS_PER_STAGE;
+          const uint32_t sfcol = tmem + SF_COL0 + slot * SF_COLS_PER_STAGE;
           const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
           const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
           for (int c = 0; c < nch; ++c)
@@ -166,6 +196,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (++slot == SF_SLOTS) {
+            slot = 0;
+            sf_phase ^= 1;
+          }
         }
         if (!ok) break;
         mma_commit(&sh.tfull);
@@ -175,37 +209,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       blockgemm::drain_wait(&sh.mdrain, 0);
     }
   } else if (warp < EPI_WARP0) {
-    // scale issuers: a stage's scale tiles go to its TMEM columns once the stage has landed. The columns' previous
-    // MMAs have finished by then (the producer refilled the stage only after their commit on `empty`).
+    // scale issuers: step g's scale tiles go to its slot's TMEM columns once they have landed. The columns' previous
+    // readers, the MMAs of step g - SF_SLOTS, have finished by then: the producer loaded these scales after its wait
+    // on `empty` for step g - 1, which those MMAs (step g - 1 - STAGES) had committed.
     if (lane == 0) {
       const bool first = warp == 2;
-      int stage = 0;
-      uint32_t phase = 0;
+      int slot = 0;
+      uint32_t sf_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int tn = tile % p.tiles_n;
         const bool b_hi = 2 * tn + 1 < p.nblk_b;
         for (int kb = 0; kb < p.nkb; ++kb) {
           const int nch = min(4, p.nchunk - kb * 4);
-          if (!mbar_wait(&sh.full[stage], phase, abort_flag, kFaultTimeoutMma)) {
+          if (!mbar_wait(&sh.sffull[slot], sf_phase, abort_flag, kFaultTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sfcol = tmem + SF_COL0 + stage * SF_COLS_PER_STAGE;
+          const uint32_t sfcol = tmem + SF_COL0 + slot * SF_COLS_PER_STAGE;
           if (first) {
             for (int c = 0; c < nch; ++c) {
-              tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[stage] + c * 512)));
-              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8, desc_plain16(smem_u32(sh.sfb[stage][0] + c * 512)));
+              tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[slot] + c * 512)));
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8, desc_plain16(smem_u32(sh.sfb[slot][0] + c * 512)));
             }
           } else if (b_hi) {  // else the columns stay stale: they scale only output columns >= N
             for (int c = 0; c < nch; ++c)
-              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8 + 4, desc_plain16(smem_u32(sh.sfb[stage][1] + c * 512)));
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8 + 4, desc_plain16(smem_u32(sh.sfb[slot][1] + c * 512)));
           }
-          mma_commit(&sh.sfready[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+          mma_commit(&sh.sfready[slot]);
+          if (++slot == SF_SLOTS) {
+            slot = 0;
+            sf_phase ^= 1;
           }
         }
       }
