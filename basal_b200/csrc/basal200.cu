@@ -137,6 +137,23 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
 // ------------------------------------------------------------------------------------------------------------
 // quantisers
 // ------------------------------------------------------------------------------------------------------------
+template <bool INT8, int PAIRS>
+int act_quant_launch(const void* x, int xt, int64_t groups, uint8_t* q, float* s, int grid, cudaStream_t st) {
+  switch (xt) {
+    case BASAL200_BF16:
+      return launch_pdl(act_quant_block_kernel<__nv_bfloat16, INT8, PAIRS>, grid, 256, 0, st,
+                        static_cast<const __nv_bfloat16*>(x), groups, q, s);
+    case BASAL200_F16:
+      return launch_pdl(act_quant_block_kernel<__half, INT8, PAIRS>, grid, 256, 0, st, static_cast<const __half*>(x),
+                        groups, q, s);
+    case BASAL200_F32:
+      return launch_pdl(act_quant_block_kernel<float, INT8, PAIRS>, grid, 256, 0, st, static_cast<const float*>(x),
+                        groups, q, s);
+    default:
+      return BASAL200_ERR_DTYPE;
+  }
+}
+
 template <bool INT8>
 int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cudaStream_t st) {
   if (M < 0 || K <= 0) return BASAL200_ERR_ARG;
@@ -147,22 +164,11 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   const int64_t groups = M * (K / 128);
-  const int grid = grid_for(dev, groups, 16);  // 8 warps a CTA, 2 groups a warp
   uint8_t* qb = static_cast<uint8_t*>(q);
-  switch (xt) {
-    case BASAL200_BF16:
-      return launch_pdl(act_quant_block_kernel<__nv_bfloat16, INT8>, grid, 256, 0, st,
-                        static_cast<const __nv_bfloat16*>(x), groups, qb, s);
-    case BASAL200_F16:
-      return launch_pdl(act_quant_block_kernel<__half, INT8>, grid, 256, 0, st, static_cast<const __half*>(x), groups,
-                        qb, s);
-    case BASAL200_F32:
-      return launch_pdl(act_quant_block_kernel<float, INT8>, grid, 256, 0, st, static_cast<const float*>(x), groups,
-                        qb, s);
-    default:
-      return BASAL200_ERR_DTYPE;
-  }
-  return launched();
+  // 8 warps a CTA, 2 x PAIRS groups a warp; 4 pairs once every SM gets 16 such CTAs
+  if (groups >= (int64_t)g_dev[dev].sms * 16 * 64)
+    return act_quant_launch<INT8, 4>(x, xt, groups, qb, s, grid_for(dev, groups, 64), st);
+  return act_quant_launch<INT8, 1>(x, xt, groups, qb, s, grid_for(dev, groups, 16), st);
 }
 
 template <bool INT8>
@@ -203,17 +209,26 @@ int nvfp4_act(const void* x, int xt, const float* inv_g, int64_t M, int64_t K, u
   if (Mp / 128 > 65535 || K / 64 > 65535) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
-  const dim3 grid((unsigned)(K / 64), (unsigned)(Mp / 128));
+  const int64_t tiles = K / 64;
+  // 2 tiles a CTA once that still gives every SM 4 CTAs
+  const bool two = (tiles / 2) * (Mp / 128) >= (int64_t)g_dev[dev].sms * 4;
+  const dim3 grid((unsigned)(two ? (tiles + 1) / 2 : tiles), (unsigned)(Mp / 128));
   switch (xt) {
     case BASAL200_BF16:
-      return launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16>, grid, 512, 0, st,
-                        static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s);
+      return two ? launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16, 2>, grid, 512, 0, st,
+                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s)
+                 : launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16, 1>, grid, 512, 0, st,
+                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s);
     case BASAL200_F16:
-      return launch_pdl(nvfp4_act_quant_kernel<__half>, grid, 512, 0, st, static_cast<const __half*>(x), inv_g, M, K,
-                        q, s);
+      return two ? launch_pdl(nvfp4_act_quant_kernel<__half, 2>, grid, 512, 0, st, static_cast<const __half*>(x),
+                              inv_g, M, K, q, s)
+                 : launch_pdl(nvfp4_act_quant_kernel<__half, 1>, grid, 512, 0, st, static_cast<const __half*>(x),
+                              inv_g, M, K, q, s);
     case BASAL200_F32:
-      return launch_pdl(nvfp4_act_quant_kernel<float>, grid, 512, 0, st, static_cast<const float*>(x), inv_g, M, K,
-                        q, s);
+      return two ? launch_pdl(nvfp4_act_quant_kernel<float, 2>, grid, 512, 0, st, static_cast<const float*>(x), inv_g,
+                              M, K, q, s)
+                 : launch_pdl(nvfp4_act_quant_kernel<float, 1>, grid, 512, 0, st, static_cast<const float*>(x), inv_g,
+                              M, K, q, s);
     default:
       return BASAL200_ERR_DTYPE;
   }

@@ -1,7 +1,9 @@
 // Quantisers of the block formats and of NVFP4, bit-exact to the reference's CPU arithmetic (rkinas/basal 2.8.1):
-// every division gives the code of an IEEE round-to-nearest division (__fdiv_rn, or a checked reciprocal product,
-// quotient_for_code), every product that the reference rounds on its own is __fmul_rn (no contraction into an FMA),
-// casts to e4m3 round to nearest even with saturation at +-448 (cvt.rn.satfinite), int8 rounds half to even.
+// every division gives the code of an IEEE round-to-nearest division (__fdiv_rn, or a reciprocal product checked
+// against the code's rounding boundaries: block_codes8, e2m1_cut_distance), every product that the reference rounds
+// on its own is __fmul_rn (no contraction into an FMA), casts to e4m3 round to nearest even with saturation at +-448
+// (cvt.rn.satfinite), e2m1 codes round to nearest even with saturation at 6 (cvt.rn.satfinite.e2m1x2), int8 rounds
+// half to even.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -12,6 +14,41 @@
 namespace b200 {
 
 // ---- element loads: n consecutive values as fp32 (16-byte vector loads) ----
+// 8 consecutive values as raw 16-byte words (one for 16-bit types, two for fp32), loaded ahead of their use so that
+// a thread has several loads in flight, then widened by unpack8.
+template <typename T>
+__device__ __forceinline__ void raw_load8(const T* p, uint4 (&w)[sizeof(T) / 2]) {
+#pragma unroll
+  for (int i = 0; i < (int)(sizeof(T) / 2); ++i) w[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+}
+__device__ __forceinline__ void unpack8(const uint4 (&w)[1], const __nv_bfloat16*, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w[0]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack8(const uint4 (&w)[1], const __half*, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w[0]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack8(const uint4 (&w)[2], const float*, float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    v[4 * i] = __uint_as_float(w[i].x);
+    v[4 * i + 1] = __uint_as_float(w[i].y);
+    v[4 * i + 2] = __uint_as_float(w[i].z);
+    v[4 * i + 3] = __uint_as_float(w[i].w);
+  }
+}
+
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
   const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -48,43 +85,53 @@ __device__ __forceinline__ uint8_t float_to_e4m3(float v) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
 }
 
-// v / sc rounded as an IEEE division, where that rounding can change the code; elsewhere the cheaper v * RN(1 / sc).
-// The product y is within 1.5 ulp of the correctly rounded quotient, so the two give the same code unless the
-// quotient lies within a few ulps of a rounding boundary of the code: an e4m3 midpoint (low 20 mantissa bits near
-// 0x80000) or the e4m3 subnormal range (FP8), a half-integer (INT8). Those few values (about 1e-4 of random data)
-// take the exact division; every code equals the one of the reference's x / s (checked against the oracle).
-template <bool INT8>
-__device__ __forceinline__ float quotient_for_code(float v, float sc, float rcp) {
-  const float y = __fmul_rn(v, rcp);
-  bool near;
-  if (INT8) {
-    near = fabsf(__fsub_rn(y, __fadd_rn(floorf(y), 0.5f))) < 0x1p-14f;
-  } else {
-    const uint32_t low = __float_as_uint(y) & 0xFFFFFu;
-    near = (low - 0x7FFFCu) <= 8u || (fabsf(y) < 0x1p-6f && y != 0.0f);
-  }
-  return near ? __fdiv_rn(v, sc) : y;
-}
-
-// 8 values of one group -> 8 code bytes: v / sc; INT8: round half to even, clamp to +-127, cast; FP8: cast two at a
-// time with cvt.rn.satfinite.e4m3x2, whose saturation at +-448 is the reference's clamp (the quotient never exceeds 448
-// by more than rounding).
+// 8 values of one group -> 8 code bytes of v / sc (an IEEE division in the reference); INT8: round half to even, clamp
+// to +-127, cast; FP8: cast two at a time with cvt.rn.satfinite.e4m3x2, whose saturation at +-448 is the reference's
+// clamp (the quotient never exceeds 448 by more than rounding).
+// The quotients are first taken as y = v * RN(1 / sc), within 1.5 ulp of the correctly rounded quotient, so y gives
+// the same code unless some quotient lies within a few ulps of a rounding boundary of the code: an e4m3 midpoint
+// (low 20 mantissa bits near 0x80000) or the e4m3 subnormal range |y| < 2^-6 (FP8), a half-integer (INT8). Then
+// (about 1e-4 of random data) the lane redoes its 8 values with the exact division; every code equals the one of
+// the reference's x / s (checked against the oracle).
 template <bool INT8>
 __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
   const float rcp = __frcp_rn(sc);
+  float y[8];
+  bool near = false;
+  if (INT8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      y[i] = __fmul_rn(v[i], rcp);
+      near |= fabsf(__fsub_rn(y[i], __fadd_rn(floorf(y[i]), 0.5f))) < 0x1p-14f;
+    }
+  } else {
+    uint32_t dmid = 0xFFFFFFFFu, dsub = 0xFFFFFFFFu;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      y[i] = __fmul_rn(v[i], rcp);
+      const uint32_t b = __float_as_uint(y[i]);
+      dmid = min(dmid, (b & 0xFFFFFu) - 0x7FFFCu);  // wraps above 8 unless within 4 ulp of a midpoint
+      dsub = min(dsub, (b & 0x7FFFFFFFu) - 1u);     // 0 < |y| < 2^-6 <=> below 0x3C800000 - 1
+    }
+    near = dmid <= 8u || dsub < 0x3C800000u - 1u;
+  }
+  if (near) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = __fdiv_rn(v[i], sc);
+  }
   uint32_t w[2] = {0u, 0u};
   if (INT8) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float t = fminf(fmaxf(rintf(quotient_for_code<true>(v[i], sc, rcp)), -127.0f), 127.0f);
+      const float t = fminf(fmaxf(rintf(y[i]), -127.0f), 127.0f);
       const uint32_t b = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(t))));
       w[i >> 2] |= b << (8 * (i & 3));
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-      const float2 t = make_float2(quotient_for_code<false>(v[i], sc, rcp), quotient_for_code<false>(v[i + 1], sc, rcp));
-      const uint32_t b = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(t, __NV_SATFINITE, __NV_E4M3));
+      const uint32_t b =
+          static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(y[i], y[i + 1]), __NV_SATFINITE, __NV_E4M3));
       w[i >> 2] |= b << (8 * (i & 3));
     }
   }
@@ -92,43 +139,57 @@ __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Activations, FP8 / INT8 block formats: one half-warp per 128-feature group (8 values a lane), amax by shuffles.
+// Activations, FP8 / INT8 block formats: one half-warp per 128-feature group (8 values a lane), amax by shuffles; a
+// warp loads PAIRS pairs of groups before it computes any (4 when there are enough groups to fill the GPU: 0.51 of
+// HBM against 0.47 with 1 at 8192 x 6144 bf16; 1 for a few rows, where fewer, longer warps cost latency).
 // basal/blockquant.py:118-123: s = max(amax, 1e-12) / qmax; q = cast(clamp(x / s)) (INT8: round first). The
 // activations are contiguous, so group g is the 128 values from element 128 g. (Measured on B200: this kernel is
 // bound by its per-value arithmetic, not by bytes in flight; staging chunks through shared memory did not speed it.)
 // ---------------------------------------------------------------------------------------------------------------
-template <typename T, bool INT8>
+template <typename T, bool INT8, int PAIRS>
 __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups,
                                                               uint8_t* __restrict__ q, float* __restrict__ s) {
-  pdl_launch();
   pdl_wait();
   constexpr float kQmax = INT8 ? 127.0f : 448.0f;
+  constexpr int W = sizeof(T) / 2;  // 16-byte words of a lane's 8 values
   const int lane = threadIdx.x & 31;
   const int half = lane >> 4, l = lane & 15;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t p = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; 2 * p < groups; p += warps) {
-    const int64_t g = 2 * p + half;
-    const bool valid = g < groups;
-    float v[8];
-    const int64_t off = g * 128 + l * 8;
-    if (valid) {
-      load8(x + off, v);
-    } else {
+  for (int64_t p = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * PAIRS; 2 * p < groups;
+       p += warps * PAIRS) {
+    // all the loads of the warp's PAIRS group pairs first (HBM wants bytes in flight), then the arithmetic
+    uint4 w[PAIRS][W];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    for (int u = 0; u < PAIRS; ++u) {
+      const int64_t g = 2 * (p + u) + half;
+      if (g < groups) {
+        raw_load8(x + g * 128 + l * 8, w[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < W; ++i) w[u][i] = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
-    float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int u = 0; u < PAIRS; ++u) {
+      const int64_t g = 2 * (p + u) + half;
+      float v[8];
+      unpack8(w[u], x, v);
+      float amax = 0.0f;
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
-    const uint2 codes = block_codes8<INT8>(v, sc);
-    if (valid) {
-      *reinterpret_cast<uint2*>(q + off) = codes;
-      if (l == 0) s[g] = sc;
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
+      const uint2 codes = block_codes8<INT8>(v, sc);
+      if (g < groups) {
+        *reinterpret_cast<uint2*>(q + g * 128 + l * 8) = codes;
+        if (l == 0) s[g] = sc;
+      }
     }
   }
+  // the next kernel (a GEMM whose CTAs each fill an SM while they wait for this grid) may launch once every CTA
+  // here has done its work: triggered at the start, its CTAs took the SMs from this grid's later waves
+  pdl_launch();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -178,6 +239,29 @@ __device__ __forceinline__ uint32_t e2m1_code(float u) {
   return c | ((u < 0.0f) ? 8u : 0u);
 }
 
+// 8 quotients -> 8 e2m1 codes, the first in the low nibble: the hardware conversion rounds to nearest even and
+// saturates at 6, which is the reference's CUTS (a > 0.25, a >= 0.75, a > 1.25, a >= 1.75, a > 2.5, a >= 3.5, a > 5).
+// The one difference, -0 (code 8 from the hardware, 0 from the reference), the caller removes: no quotient may be -0.
+__device__ __forceinline__ uint32_t e2m1_codes8(const float (&z)[8]) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(z[0]), "f"(z[1]), "f"(z[2]), "f"(z[3]), "f"(z[4]), "f"(z[5]), "f"(z[6]), "f"(z[7]));
+  return out;
+}
+
+// Distance, in units of y's last place, from y to the nearest value whose low 21 mantissa bits are zero (wrapped:
+// small means near). y = RN(v * RN(1 / sc)) is within 2 ulp of the exact quotient v / sc, and every e2m1 code
+// threshold (0.25 ... 5) is such a value, so y and the correctly rounded quotient give the same code when the
+// distance is above 16 (8 ulp). A zero y also lands at or below 16, so a zero or an underflowed product takes the
+// exact division too, which keeps the sign rule of the reference's quotient.
+__device__ __forceinline__ uint32_t e2m1_cut_distance(float y) { return (__float_as_uint(y) + 8u) & 0x1FFFFFu; }
+
 __device__ __forceinline__ float e2m1_value(uint32_t c) {
   const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   const float v = mag[c & 7];
@@ -190,61 +274,84 @@ __device__ __forceinline__ int64_t swizzled_scale_offset(int64_t r, int64_t j, i
   return ((r >> 7) * c4 + (j >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (j & 3);
 }
 
-// One CTA per 128 rows x 64 features, one thread per (row, 16-group): codes and the tile's 512 scale bytes, staged
-// in shared memory and written as 16-byte stores. Rows past M (up to the 128-row padding) get zeros.
-template <typename T>
+// One CTA per 128 rows x TILES tiles of 64 features, one thread per (row, 16-group) of each tile: all the thread's
+// loads first, then per tile the codes and the tile's 512 scale bytes, staged in shared memory and written as 16-byte
+// stores. Rows past M (up to the 128-row padding) get zeros. TILES = 2 when there are enough tiles to fill the GPU
+// (0.42 of HBM at 8192 x 6144 bf16, against 0.35 with 1 tile and 0.30 with 4), else 1.
+template <typename T, int TILES>
 __global__ void __launch_bounds__(512) nvfp4_act_quant_kernel(const T* __restrict__ x, const float* __restrict__ inv_g_p,
                                                               int64_t M, int64_t K, uint8_t* __restrict__ q,
                                                               uint8_t* __restrict__ s) {
-  pdl_launch();
   pdl_wait();
-  __shared__ __align__(16) uint8_t sbuf[512];
+  constexpr int W = sizeof(T) / 2;  // 16-byte words of 8 values
+  __shared__ __align__(16) uint8_t sbuf[TILES][512];
   const int64_t tile_r = blockIdx.y;
-  const int64_t c64 = blockIdx.x;
+  const int64_t c0 = (int64_t)blockIdx.x * TILES;  // first 64-feature tile
+  const int nt = (int)(K / 64 - c0 < TILES ? K / 64 - c0 : TILES);
   const int t = threadIdx.x;
   const int r = t >> 2, j = t & 3;
   const int64_t row = tile_r * 128 + r;
-  uint32_t scale_bits = 0, lo = 0, hi = 0;
-  if (row < M) {
-    const float inv_g = __ldg(inv_g_p);
-    float v[16];
-    const T* p = x + row * K + c64 * 64 + j * 16;
-    {
-      float a[8], b[8];
-      load8(p, a);
-      load8(p + 8, b);
+  const bool live = row < M;
+  uint4 w[TILES][2][W];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[i] = a[i];
-        v[8 + i] = b[i];
+  for (int c = 0; c < TILES; ++c) {
+    if (c < nt && live) {
+      const T* p = x + row * K + (c0 + c) * 64 + j * 16;
+      raw_load8(p, w[c][0]);
+      raw_load8(p + 8, w[c][1]);
+    }
+  }
+  const float inv_g = __ldg(inv_g_p);
+#pragma unroll
+  for (int c = 0; c < TILES; ++c) {
+    if (c >= nt) break;
+    uint32_t scale_bits = 0, lo = 0, hi = 0;
+    if (live) {
+      float v[16];
+      unpack8(w[c][0], x, *reinterpret_cast<float(*)[8]>(v));
+      unpack8(w[c][1], x, *reinterpret_cast<float(*)[8]>(v + 8));
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] = __fmul_rn(v[i], inv_g);
+        amax = fmaxf(amax, fabsf(v[i]));
       }
-    }
-    float amax = 0.0f;
+      const uint8_t sb = float_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
+      const float sf = e4m3_to_float(sb);
+      scale_bits = sb;
+      // u = v / sf as an IEEE division (nvfp4.py:106-112), 0 where sf is 0: RN(v * RN(1 / sf) + 0) (the + 0 turns
+      // a -0 into +0, the reference's code 0) unless a product lies near a code threshold or is 0, then the group
+      // takes the division
+      float u[16];
+      if (sf > 0.0f) {
+        const float rcp = __frcp_rn(sf);
+        uint32_t dmin = 0xFFFFFFFFu;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = __fmul_rn(v[i], inv_g);
-      amax = fmaxf(amax, fabsf(v[i]));
-    }
-    const uint8_t sb = float_to_e4m3(fminf(__fdiv_rn(amax, 6.0f), 448.0f));
-    const float sf = e4m3_to_float(sb);
-    scale_bits = sb;
+        for (int i = 0; i < 16; ++i) {
+          u[i] = __fmaf_rn(v[i], rcp, 0.0f);
+          dmin = min(dmin, e2m1_cut_distance(u[i]));
+        }
+        if (dmin <= 16u) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float u = sf > 0.0f ? __fdiv_rn(v[i], sf) : 0.0f;
-      const uint32_t c = e2m1_code(u);
-      if (i < 8)
-        lo |= c << (4 * i);
-      else
-        hi |= c << (4 * (i - 8));
+          for (int i = 0; i < 16; ++i) u[i] = __fadd_rn(__fdiv_rn(v[i], sf), 0.0f);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) u[i] = 0.0f;
+      }
+      lo = e2m1_codes8(*reinterpret_cast<const float(*)[8]>(u));
+      hi = e2m1_codes8(*reinterpret_cast<const float(*)[8]>(u + 8));
     }
+    *reinterpret_cast<uint2*>(q + row * (K / 2) + (c0 + c) * 32 + j * 8) = make_uint2(lo, hi);
+    sbuf[c][(r & 31) * 16 + (r >> 5) * 4 + j] = static_cast<uint8_t>(scale_bits);
   }
-  *reinterpret_cast<uint2*>(q + row * (K / 2) + c64 * 32 + j * 8) = make_uint2(lo, hi);
-  sbuf[(r & 31) * 16 + (r >> 5) * 4 + j] = static_cast<uint8_t>(scale_bits);
   __syncthreads();
-  if (t < 32) {
-    const int64_t tile = tile_r * (K / 64) + c64;
-    reinterpret_cast<uint4*>(s + tile * 512)[t] = reinterpret_cast<const uint4*>(sbuf)[t];
+  if (t < 32 * nt) {
+    const int c = t >> 5;
+    const int64_t tile = tile_r * (K / 64) + c0 + c;
+    reinterpret_cast<uint4*>(s + tile * 512)[t & 31] = reinterpret_cast<const uint4*>(sbuf[c])[t & 31];
   }
+  pdl_launch();  // after the work, as in act_quant_block_kernel
 }
 
 // ---- NVFP4 weights (basal/nvfp4.py:75-97) ----

@@ -315,6 +315,7 @@ CASES = {
     "int8_gemm": ("int8", 65536, 5120, 2048),
     "fp8_act_quant": ("fp8", 65536, 0, 2048),
     "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
+    "nvfp4_act_quant": ("nvfp4", 8192, 0, 6144),
 }
 
 
@@ -326,7 +327,11 @@ def run_case(name):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(M, K, device=dev, generator=g).bfloat16()
-    if N == 0:
+    if N == 0 and fmt == "nvfp4":
+        inv_g = torch.tensor([0.5], device=dev)
+        for _ in range(5):
+            b2.nvfp4.act_quant(x, inv_g)
+    elif N == 0:
         for _ in range(5):
             b2.fp8block.act_quant(x)
     elif fmt == "nvfp4":

@@ -61,7 +61,8 @@ def test_act_quant_golden(b2, fmt):
 @pytest.mark.parametrize("fmt", ["fp8", "int8"])
 @pytest.mark.parametrize("M, K, dtype", [(1, 128, torch.bfloat16), (37, 1024, torch.bfloat16),
                                          (1000, 2048, torch.bfloat16), (4099, 6144, torch.bfloat16),
-                                         (77, 512, torch.float16), (65, 384, torch.float32)])
+                                         (77, 512, torch.float16), (65, 384, torch.float32),
+                                         (9500, 2048, torch.float32), (10007, 2048, torch.float16)])
 def test_act_quant_bit_exact(b2, fmt, M, K, dtype):
     x = heavy(M, K, seed=M + K, dtype=dtype)
     q, s = fmt_mod(b2, fmt).act_quant(x.cuda())
@@ -108,9 +109,13 @@ def test_nvfp4_act_quant_golden(b2):
     assert np.array_equal(s.cpu().numpy(), g["act_s_swizzled"])
 
 
-@pytest.mark.parametrize("M, K", [(1, 64), (37, 512), (128, 2048), (1000, 2048), (4099, 6144)])
-def test_nvfp4_act_quant_bit_exact(b2, M, K):
-    x = heavy(M, K, seed=7 * M + K)
+@pytest.mark.parametrize("M, K, dtype", [(1, 64, torch.bfloat16), (37, 512, torch.bfloat16),
+                                         (128, 2048, torch.bfloat16), (1000, 2048, torch.bfloat16),
+                                         (4099, 6144, torch.bfloat16), (4099, 6208, torch.bfloat16),
+                                         (2500, 4160, torch.float32), (3000, 2048, torch.float16)])
+def test_nvfp4_act_quant_bit_exact(b2, M, K, dtype):
+    """Also the two-tiles-a-CTA kernel (large M x K) with an odd number of 64-feature tiles, and 16- / 32-bit input."""
+    x = heavy(M, K, seed=7 * M + K, dtype=dtype)
     inv_g = np.float32(1.0) / onv.global_scale(float(x.float().abs().max()))
     q, s = b2.nvfp4.act_quant(x.cuda(), torch.tensor([inv_g], device="cuda"))
     qo, so = onv.act_quant(x.float().numpy(), inv_g)
@@ -138,3 +143,31 @@ def test_nvfp4_weight_quantize_bit_exact(b2, N, K):
     assert np.array_equal(c.cpu().numpy(), co)
     assert np.array_equal(u8(s), so)
     assert np.array_equal(f32bits(wg), go.view(np.uint32))
+
+
+def test_nvfp4_act_quant_code_thresholds(b2):
+    """Quotients exactly at the e2m1 code thresholds (ties to even), one fp32 ulp either side, signed zeros and tiny
+    values, under scales 1, 1.25 and 0.875 (fp32 input, inv_g = 1): the kernel's product-then-check path must give
+    the codes of the reference's IEEE division."""
+    cuts = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    up, down = np.nextafter(cuts, np.float32(9)), np.nextafter(cuts, np.float32(0))
+    rows = []
+    for sc in (1.0, 1.25, 0.875):
+        for vals in (cuts, up, down, -cuts, -up, -down):
+            g = np.zeros(16, np.float32)
+            g[0] = 6.0 * sc                       # amax: the group's scale is e4m3(6 sc / 6) = sc
+            g[1:8] = vals * np.float32(sc)
+            g[8:15] = np.nextafter(vals * np.float32(sc), np.float32(0))
+            g[15] = -0.0
+            rows.append(g)
+    z = np.zeros(16, np.float32)
+    z[[1, 3, 5]] = -0.0
+    z[2], z[4], z[6] = np.float32(-1e-40), np.float32(1e-40), np.float32(-1e-30)
+    z[0] = 6.0
+    rows.append(z)
+    rows.append(np.linspace(-7, 7, 16, dtype=np.float32))
+    x = np.stack(rows).reshape(-1, 64)            # 20 groups: 5 rows of 64 features
+    q, s = b2.nvfp4.act_quant(torch.from_numpy(x).cuda(), torch.tensor([1.0], device="cuda"))
+    qo, so = onv.act_quant(x, np.float32(1.0))
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
