@@ -137,18 +137,23 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
 // ------------------------------------------------------------------------------------------------------------
 // quantisers
 // ------------------------------------------------------------------------------------------------------------
+// A quantiser lets the next kernel launch at its start when its grid is one resident wave (the next kernel's CTAs
+// then take no SM it still needs), else after its work. `per_sm` = the quantiser's CTAs an SM holds at once.
+int early_trigger(int dev, int64_t grid, int per_sm) { return grid <= (int64_t)g_dev[dev].sms * per_sm ? 1 : 0; }
+
 template <bool INT8, int PAIRS>
-int act_quant_launch(const void* x, int xt, int64_t groups, uint8_t* q, float* s, int grid, cudaStream_t st) {
+int act_quant_launch(const void* x, int xt, int64_t groups, uint8_t* q, float* s, int grid, cudaStream_t st,
+                     int early) {
   switch (xt) {
     case BASAL200_BF16:
       return launch_pdl(act_quant_block_kernel<__nv_bfloat16, INT8, PAIRS>, grid, 256, 0, st,
-                        static_cast<const __nv_bfloat16*>(x), groups, q, s);
+                        static_cast<const __nv_bfloat16*>(x), groups, q, s, early);
     case BASAL200_F16:
       return launch_pdl(act_quant_block_kernel<__half, INT8, PAIRS>, grid, 256, 0, st, static_cast<const __half*>(x),
-                        groups, q, s);
+                        groups, q, s, early);
     case BASAL200_F32:
       return launch_pdl(act_quant_block_kernel<float, INT8, PAIRS>, grid, 256, 0, st, static_cast<const float*>(x),
-                        groups, q, s);
+                        groups, q, s, early);
     default:
       return BASAL200_ERR_DTYPE;
   }
@@ -166,9 +171,12 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   const int64_t groups = M * (K / 128);
   uint8_t* qb = static_cast<uint8_t*>(q);
   // 8 warps a CTA, 2 x PAIRS groups a warp; 4 pairs once every SM gets 16 such CTAs
-  if (groups >= (int64_t)g_dev[dev].sms * 16 * 64)
-    return act_quant_launch<INT8, 4>(x, xt, groups, qb, s, grid_for(dev, groups, 64), st);
-  return act_quant_launch<INT8, 1>(x, xt, groups, qb, s, grid_for(dev, groups, 16), st);
+  if (groups >= (int64_t)g_dev[dev].sms * 16 * 64) {
+    const int grid = grid_for(dev, groups, 64);
+    return act_quant_launch<INT8, 4>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 3));
+  }
+  const int grid = grid_for(dev, groups, 16);
+  return act_quant_launch<INT8, 1>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 4));
 }
 
 template <bool INT8>
@@ -213,22 +221,23 @@ int nvfp4_act(const void* x, int xt, const float* inv_g, int64_t M, int64_t K, u
   // 2 tiles a CTA once that still gives every SM 4 CTAs
   const bool two = (tiles / 2) * (Mp / 128) >= (int64_t)g_dev[dev].sms * 4;
   const dim3 grid((unsigned)(two ? (tiles + 1) / 2 : tiles), (unsigned)(Mp / 128));
+  const int early = early_trigger(dev, (int64_t)grid.x * grid.y, 1);
   switch (xt) {
     case BASAL200_BF16:
       return two ? launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16, 2>, grid, 512, 0, st,
-                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s)
+                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s, early)
                  : launch_pdl(nvfp4_act_quant_kernel<__nv_bfloat16, 1>, grid, 512, 0, st,
-                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s);
+                              static_cast<const __nv_bfloat16*>(x), inv_g, M, K, q, s, early);
     case BASAL200_F16:
       return two ? launch_pdl(nvfp4_act_quant_kernel<__half, 2>, grid, 512, 0, st, static_cast<const __half*>(x),
-                              inv_g, M, K, q, s)
+                              inv_g, M, K, q, s, early)
                  : launch_pdl(nvfp4_act_quant_kernel<__half, 1>, grid, 512, 0, st, static_cast<const __half*>(x),
-                              inv_g, M, K, q, s);
+                              inv_g, M, K, q, s, early);
     case BASAL200_F32:
       return two ? launch_pdl(nvfp4_act_quant_kernel<float, 2>, grid, 512, 0, st, static_cast<const float*>(x), inv_g,
-                              M, K, q, s)
+                              M, K, q, s, early)
                  : launch_pdl(nvfp4_act_quant_kernel<float, 1>, grid, 512, 0, st, static_cast<const float*>(x), inv_g,
-                              M, K, q, s);
+                              M, K, q, s, early);
     default:
       return BASAL200_ERR_DTYPE;
   }

@@ -148,7 +148,9 @@ __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
 // ---------------------------------------------------------------------------------------------------------------
 template <typename T, bool INT8, int PAIRS>
 __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restrict__ x, int64_t groups,
-                                                              uint8_t* __restrict__ q, float* __restrict__ s) {
+                                                              uint8_t* __restrict__ q, float* __restrict__ s,
+                                                              int early) {
+  if (early) pdl_launch();  // one resident wave: the next kernel's set-up may overlap all of this grid
   pdl_wait();
   constexpr float kQmax = INT8 ? 127.0f : 448.0f;
   constexpr int W = sizeof(T) / 2;  // 16-byte words of a lane's 8 values
@@ -187,9 +189,9 @@ __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restric
       }
     }
   }
-  // the next kernel (a GEMM whose CTAs each fill an SM while they wait for this grid) may launch once every CTA
-  // here has done its work: triggered at the start, its CTAs took the SMs from this grid's later waves
-  pdl_launch();
+  // else the next kernel (a GEMM whose CTAs each fill an SM while they wait for this grid) may launch once every
+  // CTA here has done its work: triggered at the start, its CTAs took the SMs from this grid's later waves
+  if (!early) pdl_launch();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -281,7 +283,8 @@ __device__ __forceinline__ int64_t swizzled_scale_offset(int64_t r, int64_t j, i
 template <typename T, int TILES>
 __global__ void __launch_bounds__(512) nvfp4_act_quant_kernel(const T* __restrict__ x, const float* __restrict__ inv_g_p,
                                                               int64_t M, int64_t K, uint8_t* __restrict__ q,
-                                                              uint8_t* __restrict__ s) {
+                                                              uint8_t* __restrict__ s, int early) {
+  if (early) pdl_launch();  // as in act_quant_block_kernel
   pdl_wait();
   constexpr int W = sizeof(T) / 2;  // 16-byte words of 8 values
   __shared__ __align__(16) uint8_t sbuf[TILES][512];
@@ -351,7 +354,7 @@ __global__ void __launch_bounds__(512) nvfp4_act_quant_kernel(const T* __restric
     const int64_t tile = tile_r * (K / 64) + c0 + c;
     reinterpret_cast<uint4*>(s + tile * 512)[t & 31] = reinterpret_cast<const uint4*>(sbuf[c])[t & 31];
   }
-  pdl_launch();  // after the work, as in act_quant_block_kernel
+  if (!early) pdl_launch();
 }
 
 // ---- NVFP4 weights (basal/nvfp4.py:75-97) ----
