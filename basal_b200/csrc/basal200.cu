@@ -37,7 +37,7 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 11 };  // kSlotSmall .. kSlotSmall + 11
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14 };  // kSlotFp4 .. + 5, kSlotSmall .. + 11
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -367,14 +367,32 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   }
 }
 
-template <int OUT>
-int fp4_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const fp4gemm::Params& p,
+template <int OUT, int BN>
+int fp4_gemm_launch(int dev, const void* q, const void* w, int64_t Mp, int64_t N, int64_t K, fp4gemm::Params p,
                     cudaStream_t st) {
-  auto kern = fp4gemm::nvfp4_gemm_kernel<OUT>;
-  int rc = set_smem(dev, kSlotFp4 + OUT, kern, fp4gemm::SMEM_BYTES);
-  if (rc) return rc;
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = tmap_u8(&ta, q, (uint64_t)(K / 2), (uint64_t)Mp, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BM)))
+    return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), fp4gemm::BKB, BN))) return rc;
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t tiles = Mp / fp4gemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  auto kern = fp4gemm::nvfp4_gemm_kernel<OUT, BN>;
+  constexpr size_t smem = fp4gemm::Cfg<BN>::SMEM_BYTES;
+  if ((rc = set_smem(dev, kSlotFp4 + OUT * 2 + (BN == 256 ? 0 : 1), kern, smem))) return rc;
   const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
-  return launch_pdl(kern, grid, fp4gemm::NUM_THREADS, fp4gemm::SMEM_BYTES, st, ta, tb, p);
+  return launch_pdl(kern, grid, fp4gemm::NUM_THREADS, smem, st, ta, tb, p);
+}
+
+// 128 x 256 tiles, or 128 x 128 when the wide tiles would not give every SM one (few rows)
+template <int OUT>
+int fp4_gemm_pick(int dev, const void* q, const void* w, int64_t Mp, int64_t N, int64_t K, const fp4gemm::Params& p,
+                  cudaStream_t st) {
+  if (Mp / fp4gemm::BM * ((N + 255) / 256) < g_dev[dev].sms)
+    return fp4_gemm_launch<OUT, 128>(dev, q, w, Mp, N, K, p, st);
+  return fp4_gemm_launch<OUT, 256>(dev, q, w, Mp, N, K, p, st);
 }
 
 int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t* ws, const float* alpha,
@@ -390,11 +408,6 @@ int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   const int64_t Mp = (M + 127) / 128 * 128;
-  CUtensorMap ta, tb;
-  if ((rc = tmap_u8(&ta, q, (uint64_t)(K / 2), (uint64_t)Mp, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BM)))
-    return rc;
-  if ((rc = tmap_u8(&tb, w, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BN)))
-    return rc;
   fp4gemm::Params p;
   p.sa = s;
   p.sb = ws;
@@ -405,15 +418,11 @@ int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t
   p.N = (int)N;
   p.nchunk = (int)(K / 64);
   p.nkb = (p.nchunk + 3) / 4;
-  p.tiles_n = (int)((N + fp4gemm::BN - 1) / fp4gemm::BN);
   p.nblk_b = (int)((N + 127) / 128);
-  const int64_t tiles = Mp / fp4gemm::BM * p.tiles_n;
-  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
-  p.num_tiles = (int)tiles;
   switch (yt) {
-    case BASAL200_BF16: return fp4_gemm_launch<BASAL200_BF16>(dev, ta, tb, p, st);
-    case BASAL200_F16: return fp4_gemm_launch<BASAL200_F16>(dev, ta, tb, p, st);
-    case BASAL200_F32: return fp4_gemm_launch<BASAL200_F32>(dev, ta, tb, p, st);
+    case BASAL200_BF16: return fp4_gemm_pick<BASAL200_BF16>(dev, q, w, Mp, N, K, p, st);
+    case BASAL200_F16: return fp4_gemm_pick<BASAL200_F16>(dev, q, w, Mp, N, K, p, st);
+    case BASAL200_F32: return fp4_gemm_pick<BASAL200_F32>(dev, q, w, Mp, N, K, p, st);
     default: return BASAL200_ERR_DTYPE;
   }
 }

@@ -166,17 +166,20 @@ struct Store<BASAL200_F32> {
   }
 };
 
-// Redistributes a warp's 32 rows x 8 chunks of 16 bytes (lane = row, c[j] = chunk j) so that lane L holds in c[i]
-// chunk L % 8 of row 4 i + L / 8, and a store of c[i] by the warp writes 4 whole row segments of 128 bytes: three
-// shuffle exchanges of a chunk-index bit with a lane bit (chunk bit k with lane bit k + 2), then one fixed lane
-// rotation.
-__device__ __forceinline__ void rows_to_segments(uint4 (&c)[8], int lane) {
+// Redistributes a warp's 32 rows x CH chunks of 16 bytes (CH = 8 or 4; lane = row, c[j] = chunk j) so that lane L
+// holds in c[i] chunk L % CH of row (32 / CH) i + L / CH, and a store of c[i] by the warp writes 32 / CH whole row
+// segments of 16 CH bytes: log2(CH) shuffle exchanges of a chunk-index bit with a lane bit (chunk bit k with lane
+// bit 5 - log2(CH) + k), then one fixed lane rotation.
+template <int CH>
+__device__ __forceinline__ void rows_to_segments(uint4 (&c)[CH], int lane) {
+  static_assert(CH == 4 || CH == 8, "4 or 8 chunks a row");
+  constexpr int LCH = CH == 8 ? 3 : 2;
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    const int m = 4 << k;
+  for (int k = 0; k < LCH; ++k) {
+    const int m = 1 << (5 - LCH + k);
     const bool hi = lane & m;
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
+    for (int s = 0; s < CH; ++s) {
       if (s & (1 << k)) continue;
       const int t = s | (1 << k);
       const uint4 send = hi ? c[s] : c[t];
@@ -191,9 +194,9 @@ __device__ __forceinline__ void rows_to_segments(uint4 (&c)[8], int lane) {
         c[t] = recv;
     }
   }
-  const int src = ((lane & 7) << 2) | (lane >> 3);
+  const int src = ((lane & (CH - 1)) << (5 - LCH)) | (lane >> LCH);
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
+  for (int s = 0; s < CH; ++s) {
     c[s].x = __shfl_sync(0xffffffffu, c[s].x, src);
     c[s].y = __shfl_sync(0xffffffffu, c[s].y, src);
     c[s].z = __shfl_sync(0xffffffffu, c[s].z, src);

@@ -30,39 +30,46 @@ namespace b200 {
 namespace fp4gemm {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BKB = 128;  // bytes of K per stage (256 e2m1 values = 4 scale tiles)
-constexpr int STAGES = 4;     // operand (A / B) ring
-constexpr int SF_SLOTS = STAGES + 1;  // scale ring: a step's scales are loaded one step ahead of its operands
 constexpr int A_BYTES = BM * BKB;
-constexpr int B_BYTES = BN * BKB;
 constexpr int SF_BYTES = 4 * 512;  // 4 scale tiles of 128 rows
 constexpr int NUM_EPI_WARPS = 16;
 constexpr int EPI_WARP0 = 4;
 constexpr int NUM_THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t SF_COL0 = BN;  // scale columns after the accumulator
 constexpr uint32_t SFA_COLS = 16;  // 4 chunks x 4 columns
-constexpr uint32_t SF_COLS_PER_STAGE = SFA_COLS + 32;  // + 4 chunks x 8 columns of B
-static_assert(SF_COL0 + SF_SLOTS * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
 
-struct Shared {
-  uint8_t a[STAGES][A_BYTES];
-  uint8_t b[STAGES][B_BYTES];
-  uint8_t sfa[SF_SLOTS][SF_BYTES];
-  uint8_t sfb[SF_SLOTS][2][SF_BYTES];  // the B tile's two 128-row halves
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t sffull[SF_SLOTS];
-  uint64_t sfready[SF_SLOTS];
-  uint64_t tfull;
-  uint64_t tempty;
-  uint64_t mdrain;
-  uint32_t tmem_base;
-  int abort;
+// Tile width: BN = 256 (the rule), or 128 when 256-wide tiles would leave SMs idle (few rows): then a CTA streams
+// 128 weight rows, and the smaller stages make room for a deeper ring (the bytes in flight that bound a few-rows
+// GEMM). The arithmetic of an output element is the same in both.
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;  // operand (A / B) ring
+  static constexpr int SF_SLOTS = STAGES + 1;       // scale ring: a step's scales come one step ahead of its operands
+  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int BHALVES = BN / 128;          // 128-row scale tiles of a B tile
+  static constexpr uint32_t SF_COL0 = BN;           // scale columns after the accumulator
+  static constexpr uint32_t SF_COLS_PER_STAGE = SFA_COLS + BN / 8;  // + 4 chunks x BN / 32 columns of B
+  static constexpr int EPI_COLS = BN / 4;           // accumulator columns an epilogue warp reads
+  static_assert(SF_COL0 + SF_SLOTS * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
+  struct Shared {
+    uint8_t a[STAGES][A_BYTES];
+    uint8_t b[STAGES][B_BYTES];
+    uint8_t sfa[SF_SLOTS][SF_BYTES];
+    uint8_t sfb[SF_SLOTS][BHALVES][SF_BYTES];  // the B tile's 128-row halves
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t sffull[SF_SLOTS];
+    uint64_t sfready[SF_SLOTS];
+    uint64_t tfull;
+    uint64_t tempty;
+    uint64_t mdrain;
+    uint32_t tmem_base;
+    int abort;
+  };
+  static constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+  static_assert(SMEM_BYTES <= 232448, "227 KB of shared memory a CTA");
 };
-constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
-static_assert(SMEM_BYTES <= 232448, "227 KB of shared memory a CTA");
 
 struct Params {
   const uint8_t* sa;   // swizzled scales of A: Mp/128 x (K/64) tiles
@@ -73,10 +80,14 @@ struct Params {
   int M, N, nchunk, nkb, tiles_n, num_tiles, nblk_b;  // nblk_b = ceil(N / 128)
 };
 
-template <int OUT>
+template <int OUT, int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const Params p) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES, SF_SLOTS = C::SF_SLOTS, B_BYTES = C::B_BYTES;
+  constexpr uint32_t SF_COL0 = C::SF_COL0, SF_COLS_PER_STAGE = C::SF_COLS_PER_STAGE;
+  using Shared = typename C::Shared;
   extern __shared__ uint8_t smem_raw[];
   Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = warp_id();
@@ -120,13 +131,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       auto load_scales = [&]() {
         if (sf_tile >= p.num_tiles) return;
         const int tm = sf_tile / p.tiles_n, tn = sf_tile - tm * p.tiles_n;
-        const bool b_hi = 2 * tn + 1 < p.nblk_b;  // the tile's second 128 rows of B exist
+        const int64_t bb = (int64_t)tn * C::BHALVES;  // the tile's first 128-row block of B
+        const bool b_hi = C::BHALVES == 2 && bb + 1 < p.nblk_b;  // its second 128 rows exist
         const int nch = min(4, p.nchunk - sf_kb * 4);
         mbar_arrive_expect_tx(&sh.sffull[slot], (b_hi ? 3 : 2) * nch * 512);
         bulk_load(sh.sfa[slot], p.sa + ((int64_t)tm * c4 + sf_kb * 4) * 512, nch * 512, &sh.sffull[slot]);
-        bulk_load(sh.sfb[slot][0], p.sb + ((int64_t)(2 * tn) * c4 + sf_kb * 4) * 512, nch * 512, &sh.sffull[slot]);
+        bulk_load(sh.sfb[slot][0], p.sb + (bb * c4 + sf_kb * 4) * 512, nch * 512, &sh.sffull[slot]);
         if (b_hi)
-          bulk_load(sh.sfb[slot][1], p.sb + ((int64_t)(2 * tn + 1) * c4 + sf_kb * 4) * 512, nch * 512,
+          bulk_load(sh.sfb[slot][C::BHALVES - 1], p.sb + ((bb + 1) * c4 + sf_kb * 4) * 512, nch * 512,
                     &sh.sffull[slot]);
         sf_filled |= 1u << slot;
         sf_last = (sf_last & ~(1u << slot)) | (sf_phase << slot);
@@ -189,7 +201,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t ad = desc_sw128(smem_u32(sh.a[stage]));
           const uint64_t bd = desc_sw128(smem_u32(sh.b[stage]));
           for (int c = 0; c < nch; ++c)
-            mma_mxf4nvf4(tmem, ad + 2 * c, bd + 2 * c, idesc, sfcol + c * 4, sfcol + SFA_COLS + c * 8,
+            mma_mxf4nvf4(tmem, ad + 2 * c, bd + 2 * c, idesc, sfcol + c * 4, sfcol + SFA_COLS + c * (BN / 32),
                          (kb | c) != 0);
           mma_commit(&sh.empty[stage]);
           if (++stage == STAGES) {
@@ -219,7 +231,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int tn = tile % p.tiles_n;
-        const bool b_hi = 2 * tn + 1 < p.nblk_b;
+        const bool b_hi = C::BHALVES == 2 && (int64_t)tn * 2 + 1 < p.nblk_b;
         for (int kb = 0; kb < p.nkb; ++kb) {
           const int nch = min(4, p.nchunk - kb * 4);
           if (!mbar_wait(&sh.sffull[slot], sf_phase, abort_flag, kFaultTimeoutMma)) {
@@ -228,14 +240,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t sfcol = tmem + SF_COL0 + slot * SF_COLS_PER_STAGE;
+          // warp 2: A's scales, and with BN = 256 those of B's first 128 rows; warp 3: the rest of B's
           if (first) {
             for (int c = 0; c < nch; ++c) {
               tmem_cp_32x128b_x4(sfcol + c * 4, desc_plain16(smem_u32(sh.sfa[slot] + c * 512)));
-              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8, desc_plain16(smem_u32(sh.sfb[slot][0] + c * 512)));
+              if (BN == 256)
+                tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8, desc_plain16(smem_u32(sh.sfb[slot][0] + c * 512)));
             }
+          } else if (BN == 128) {
+            for (int c = 0; c < nch; ++c)
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 4, desc_plain16(smem_u32(sh.sfb[slot][0] + c * 512)));
           } else if (b_hi) {  // else the columns stay stale: they scale only output columns >= N
             for (int c = 0; c < nch; ++c)
-              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8 + 4, desc_plain16(smem_u32(sh.sfb[slot][1] + c * 512)));
+              tmem_cp_32x128b_x4(sfcol + SFA_COLS + c * 8 + 4,
+                                 desc_plain16(smem_u32(sh.sfb[slot][C::BHALVES - 1] + c * 512)));
           }
           mma_commit(&sh.sfready[slot]);
           if (++slot == SF_SLOTS) {
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     using OutT = typename blockgemm::Store<OUT>::T;
     const int ew = warp - EPI_WARP0;
-    const int part = ew >> 2;   // which 64 columns of the tile
+    const int part = ew >> 2;   // which EPI_COLS columns of the tile
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may read
     const float alpha = __ldg(p.alpha);
     uint32_t acc_cnt = 0;
@@ -258,12 +276,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       if (!blockgemm::warp_wait(&sh.tfull, acc_cnt & 1, abort_flag, kFaultTimeoutEpilogue)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + part * 64;
+      constexpr int EC = C::EPI_COLS;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + part * EC;
       uint32_t r0[32], r1[32];
       tmem_ld32_issue(taddr, r0);
-      tmem_ld32_issue(taddr + 32, r1);
+      if (EC == 64) tmem_ld32_issue(taddr + 32, r1);
       tmem_ld_wait32(r0);
-      tmem_ld_wait32(r1);
+      if (EC == 64) tmem_ld_wait32(r1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tempty);
@@ -271,27 +290,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // cast this lane's row, then trade chunks across the warp so that each store writes 4 rows x 128 bytes
       // (a store of one 16-byte chunk from each of 32 rows kept the SM's write path busy for most of a tile)
       constexpr int PER = blockgemm::Store<OUT>::PER;  // outputs per 16-byte chunk
+      constexpr int CH = EC / PER < 8 ? EC / PER : 8;  // 16-byte chunks of a row a transpose moves (4 or 8)
+      constexpr int LCH = CH == 8 ? 3 : 2;
       const OutT* bias = reinterpret_cast<const OutT*>(p.bias);
 #pragma unroll
-      for (int blk = 0; blk < 64 / (8 * PER); ++blk) {
-        const int nb = tn * BN + part * 64 + blk * 8 * PER;  // first column of the 8 chunks
-        uint4 c[8];
+      for (int blk = 0; blk < EC / (CH * PER); ++blk) {
+        const int nb = tn * BN + part * EC + blk * CH * PER;  // first column of the CH chunks
+        uint4 c[CH];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < CH; ++j) {
           float v[PER];
 #pragma unroll
           for (int e = 0; e < PER; ++e) {
-            const int col = blk * 8 * PER + j * PER + e;
+            const int col = blk * CH * PER + j * PER + e;
             v[e] = __fmul_rn(__uint_as_float(col < 32 ? r0[col] : r1[col - 32]), alpha);
           }
           // N % 16 == 0: a chunk is whole or absent
           c[j] = blockgemm::Store<OUT>::pack(v, bias && nb + j * PER < p.N ? bias + nb + j * PER : nullptr);
         }
-        blockgemm::rows_to_segments(c, lane);
-        const int col = nb + (lane & 7) * PER;
+        blockgemm::rows_to_segments<CH>(c, lane);
+        const int col = nb + (lane & (CH - 1)) * PER;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int row = tm * BM + quad * 32 + 4 * i + (lane >> 3);
+        for (int i = 0; i < CH; ++i) {
+          const int row = tm * BM + quad * 32 + (32 / CH) * i + (lane >> LCH);
           if (row < p.M && col < p.N)
             *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(p.y) + (int64_t)row * p.N + col) = c[i];
         }

@@ -83,7 +83,7 @@ def test_c3_sweep_by_row_samples(b2, M, N, K):
     assert err.max() < 1e-2, err.max()
 
 
-@pytest.mark.parametrize("M, N", [(300, 640), (128, 272)])
+@pytest.mark.parametrize("M, N", [(300, 640), (128, 272), (4096, 2064)])
 def test_output_casts_and_bias(b2, M, N):
     """bf16 / fp16 outputs are the fp32 output cast; a bias in the output type is added to the cast value and rounded
     again (torch adds a bias to the cast product). Called through the C-ABI entry point, which takes the bias."""
@@ -110,3 +110,21 @@ def test_output_casts_and_bias(b2, M, N):
                 want = (want.float() + b.float()).to(dt)
             assert torch.equal(y, want), dt
     assert b2._lib.device_faults(0) == 0
+
+
+def test_tile_widths_give_the_same_bits(b2):
+    """Rows of a many-row GEMM (128 x 256 tiles) equal the same rows computed alone (128 x 128 tiles): a row's output
+    does not depend on the batch around it (tests/test_nvfp4.py:51)."""
+    M, N, K = 4096, 2048, 1024
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(N, K, generator=g) * 0.02
+    x = c3_input(M, K, seed=6)
+    lin = torch.nn.Linear(K, N, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    f = b2.nvfp4.NVFP4Linear.of(lin.cuda(), x.float().abs().amax())
+    xc = x.cuda()
+    y = f(xc)
+    rows = torch.tensor([0, 1, 777, 4095], device="cuda")
+    assert torch.equal(f(xc[rows]), y[rows])
+    assert torch.equal(f(xc[:1]), y[:1])
