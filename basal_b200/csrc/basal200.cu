@@ -277,7 +277,7 @@ int check_launch_regs(K kernel, int need) {
 }
 
 template <bool INT8, int OUT>
-int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::OutMaps& out,
                       const blockgemm::Params& p, cudaStream_t st) {
   auto kern = blockgemm::block_gemm_kernel<INT8, OUT>;
   const int slot = kSlotBlock + (INT8 ? 3 : 0) + OUT;
@@ -288,13 +288,14 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
   int rc = set_smem(dev, slot, kern, blockgemm::smem_bytes<OUT>());
   if (rc) return rc;
   const int grid = p.num_tiles < g_dev[dev].sms ? p.num_tiles : g_dev[dev].sms;
-  return launch_pdl(kern, grid, blockgemm::NUM_THREADS, blockgemm::smem_bytes<OUT>(), st, ta, tb, tc, p);
+  return launch_pdl(kern, grid, blockgemm::NUM_THREADS, blockgemm::smem_bytes<OUT>(), st, ta, tb, out, p);
 }
 
 // Few rows (M <= 64): the weight-streaming kernel, NT token rows a tile (32 or 64), one CTA per 128-row weight tile.
 template <bool INT8, int OUT, int NT>
 int small_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
-                      void* c, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+                      void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
+                      cudaStream_t st) {
   auto kern = smallgemm::small_gemm_kernel<INT8, OUT, NT>;
   constexpr size_t smem = smallgemm::smem_bytes<NT>();
   const int slot = kSlotSmall + (INT8 ? 6 : 0) + OUT * 2 + (NT == 32 ? 0 : 1);
@@ -307,7 +308,10 @@ int small_gemm_launch(int dev, const void* q, const float* s, const void* w, con
   p.s = s;
   p.ws = ws;
   p.bias = bias;
-  p.c = c;
+  for (int r = 0; r < blockgemm::kMaxPeers; ++r) p.cs[r] = r < npeers ? cs[r] : nullptr;
+  p.npeers = npeers;
+  p.ldc = ldc;
+  p.col_off = col_off;
   p.M = (int)M;
   p.N = (int)N;
   p.nkb = (int)(K / 128);
@@ -315,10 +319,11 @@ int small_gemm_launch(int dev, const void* q, const float* s, const void* w, con
 }
 
 template <bool INT8, int OUT>
-int small_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c,
-               int64_t M, int64_t N, int64_t K, cudaStream_t st) {
-  if (M <= 32) return small_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, c, M, N, K, st);
-  return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, c, M, N, K, st);
+int small_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
+               void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
+               cudaStream_t st) {
+  if (M <= 32) return small_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st);
+  return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st);
 }
 
 template <bool INT8>
@@ -332,21 +337,22 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
+  void* const cs[1] = {c};
   if (M <= smallgemm::MAX_ROWS && K / 128 <= smallgemm::MAX_KB && N / smallgemm::BW <= 65535) {
     switch (ct) {
-      case BASAL200_BF16: return small_gemm<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, c, M, N, K, st);
-      case BASAL200_F16: return small_gemm<INT8, BASAL200_F16>(dev, q, s, w, ws, bias, c, M, N, K, st);
-      case BASAL200_F32: return small_gemm<INT8, BASAL200_F32>(dev, q, s, w, ws, bias, c, M, N, K, st);
+      case BASAL200_BF16: return small_gemm<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, st);
+      case BASAL200_F16: return small_gemm<INT8, BASAL200_F16>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, st);
+      case BASAL200_F32: return small_gemm<INT8, BASAL200_F32>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, st);
       default: return BASAL200_ERR_DTYPE;
     }
   }
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb;
+  blockgemm::OutMaps out;
+  memset(&out, 0, sizeof(out));
   if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
   if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;
-  if (ct == BASAL200_F32)
-    memset(&tc, 0, sizeof(tc));  // fp32 outputs are stored directly, without TMA
-  else if ((rc = tmap_u16(&tc, c, (uint64_t)N, (uint64_t)M, 64, blockgemm::BM)))
-    return rc;
+  // fp32 outputs are stored directly, without TMA
+  if (ct != BASAL200_F32 && (rc = tmap_u16(&out.m[0], c, (uint64_t)N, (uint64_t)M, 64, blockgemm::BM))) return rc;
   blockgemm::Params p;
   p.s = s;
   p.ws = ws;
@@ -356,15 +362,65 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   p.N = (int)N;
   p.nkb = (int)(K / 128);
   p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
+  p.npeers = 1;
+  p.col_off = 0;
   const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;
   switch (ct) {
-    case BASAL200_BF16: return block_gemm_launch<INT8, BASAL200_BF16>(dev, ta, tb, tc, p, st);
-    case BASAL200_F16: return block_gemm_launch<INT8, BASAL200_F16>(dev, ta, tb, tc, p, st);
-    case BASAL200_F32: return block_gemm_launch<INT8, BASAL200_F32>(dev, ta, tb, tc, p, st);
+    case BASAL200_BF16: return block_gemm_launch<INT8, BASAL200_BF16>(dev, ta, tb, out, p, st);
+    case BASAL200_F16: return block_gemm_launch<INT8, BASAL200_F16>(dev, ta, tb, out, p, st);
+    case BASAL200_F32: return block_gemm_launch<INT8, BASAL200_F32>(dev, ta, tb, out, p, st);
     default: return BASAL200_ERR_DTYPE;
   }
+}
+
+// The FP8 block GEMM of one rank's column shard of a column-parallel linear (N of n_total weight rows, from column
+// col_off), its tiles stored into every rank's [M, n_total] output (outs: npeers device pointers, peer-mapped):
+// the linear's all-gather done by the GEMM's own stores, tile by tile, with no collective kernel. 16-bit outputs.
+int block_gemm_gather(const void* q, const float* s, const void* w, const float* ws, void* const* outs, int npeers,
+                      int64_t col_off, int64_t n_total, int ct, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (M < 0 || N <= 0 || K <= 0 || npeers < 1 || npeers > blockgemm::kMaxPeers || !outs) return BASAL200_ERR_ARG;
+  if (N % 128 || K % 128 || col_off % 128 || col_off + N > n_total) return BASAL200_ERR_SHAPE;
+  if (ct != BASAL200_BF16 && ct != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (M == 0) return BASAL200_OK;
+  if (!q || !s || !w || !ws) return BASAL200_ERR_ARG;
+  if (!aligned16(q) || !aligned16(w)) return BASAL200_ERR_ALIGN;
+  for (int r = 0; r < npeers; ++r)
+    if (!outs[r] || !aligned16(outs[r])) return BASAL200_ERR_ALIGN;
+  if (M > (int64_t)1 << 30 || n_total > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  if (M <= smallgemm::MAX_ROWS && K / 128 <= smallgemm::MAX_KB && N / smallgemm::BW <= 65535) {
+    if (ct == BASAL200_BF16)
+      return small_gemm<false, BASAL200_BF16>(dev, q, s, w, ws, nullptr, outs, npeers, n_total, (int)col_off, M, N, K,
+                                              st);
+    return small_gemm<false, BASAL200_F16>(dev, q, s, w, ws, nullptr, outs, npeers, n_total, (int)col_off, M, N, K,
+                                           st);
+  }
+  CUtensorMap ta, tb;
+  blockgemm::OutMaps out;
+  memset(&out, 0, sizeof(out));
+  if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;
+  for (int r = 0; r < npeers; ++r)
+    if ((rc = tmap_u16(&out.m[r], outs[r], (uint64_t)n_total, (uint64_t)M, 64, blockgemm::BM))) return rc;
+  blockgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = nullptr;
+  p.c = nullptr;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nkb = (int)(K / 128);
+  p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
+  p.npeers = npeers;
+  p.col_off = (int)col_off;
+  const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  if (ct == BASAL200_BF16) return block_gemm_launch<false, BASAL200_BF16>(dev, ta, tb, out, p, st);
+  return block_gemm_launch<false, BASAL200_F16>(dev, ta, tb, out, p, st);
 }
 
 template <int OUT, int BN>
@@ -529,6 +585,12 @@ int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t 
 int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
   return block_gemm<false>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));
+}
+
+int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
+                                   void* const* outs, int npeers, int64_t col_off, int64_t n_total, int c_dtype,
+                                   int64_t M, int64_t N, int64_t K, void* stream) {
+  return block_gemm_gather(q, s, w, ws, outs, npeers, col_off, n_total, c_dtype, M, N, K, as_stream(stream));
 }
 
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,

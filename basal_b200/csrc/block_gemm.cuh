@@ -70,8 +70,18 @@ struct Params {
   const float* s;   // [M, K/128]
   const float* ws;  // [N/128, K/128]
   const void* bias; // [N] in the output type, or null
-  void* c;          // [M, N]
+  void* c;          // [M, N] (fp32 outputs, stored directly)
   int M, N, nkb, tiles_n, num_tiles;
+  int npeers;       // 16-bit outputs: the output buffers the tiles are stored into (OutMaps), 1 or, for a column-
+  int col_off;      // parallel linear gathered on the fly, every rank's [M, n_total] output, at column col_off
+};
+
+// The tensor maps of the output buffers of a 16-bit output: one for a plain GEMM; one per rank for a GEMM whose
+// column shard is stored straight into every rank's full output (the all-gather of a column-parallel linear done by
+// the epilogue's TMA stores over NVLink, one plain store per rank and sub-tile).
+constexpr int kMaxPeers = 8;
+struct OutMaps {
+  CUtensorMap m[kMaxPeers];
 };
 
 // Bounded drain wait (the abort flag is already set when it runs).
@@ -207,7 +217,7 @@ __device__ __forceinline__ void rows_to_segments(uint4 (&c)[CH], int lane) {
 template <bool INT8, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     block_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmC, const Params p) {
+                      const __grid_constant__ OutMaps out, const Params p) {
   using S = SmemOf<OUT>;
   constexpr int STAGES = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -231,7 +241,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (S::STAGING) tma_prefetch_desc(&tmC);
+    if (S::STAGING)
+      for (int r = 0; r < p.npeers; ++r) tma_prefetch_desc(&out.m[r]);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
   pdl_launch();
@@ -385,8 +396,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         named_barrier(1 + half, 128);
         if (issuer) {
           if (nvalid) {
-            tma_store_2d(&tmC, sh.out[half * 2], n0, tm * BM);
-            tma_store_2d(&tmC, sh.out[half * 2 + 1], n0 + 64, tm * BM);
+            for (int r = 0; r < p.npeers; ++r) {
+              tma_store_2d(&out.m[r], sh.out[half * 2], p.col_off + n0, tm * BM);
+              tma_store_2d(&out.m[r], sh.out[half * 2 + 1], p.col_off + n0 + 64, tm * BM);
+            }
           }
           tma_store_commit();
         }

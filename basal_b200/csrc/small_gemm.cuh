@@ -75,7 +75,10 @@ struct Params {
   const float* s;    // [M, K/128] activation scales
   const float* ws;   // [N/128, K/128] weight scales
   const void* bias;  // [N] in the output type, or null
-  void* c;           // [M, N]
+  void* cs[blockgemm::kMaxPeers];  // the output buffers: [M, ldc] each, this GEMM's N columns from col_off (one, or
+  int npeers;                      // every rank's for a column-parallel linear gathered by the stores)
+  int64_t ldc;
+  int col_off;
   int M, N, nkb;
 };
 
@@ -268,8 +271,10 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
         for (int j = 0; j < 32; j += 2) {
           const float2 v = unpack_f2(acc[j / 2]);
           const int tok = half * 32 + j;
-          if (tok < p.M) store1<OUT>(p.c, (int64_t)tok * p.N + n, v.x, p.bias, n);
-          if (tok + 1 < p.M) store1<OUT>(p.c, (int64_t)(tok + 1) * p.N + n, v.y, p.bias, n);
+          for (int r = 0; r < p.npeers; ++r) {
+            if (tok < p.M) store1<OUT>(p.cs[r], (int64_t)tok * p.ldc + p.col_off + n, v.x, p.bias, n);
+            if (tok + 1 < p.M) store1<OUT>(p.cs[r], (int64_t)(tok + 1) * p.ldc + p.col_off + n, v.y, p.bias, n);
+          }
         }
       }
     }

@@ -10,8 +10,17 @@ never exchange data, so the hot path shards by rows with no collective. This mod
   sum_over_ranks(x, group)          the units all ranks processed
   check_peers(group, timeout_s)     a bounded barrier: a rank that died or never joined surfaces as an error on the
                                     others within timeout_s (gloo's monitored barrier; NCCL groups use a store key)
-Everything here is host logic; the GPUs run only libbasal200's kernels on their own rows.
+Everything above is host logic; the GPUs run only libbasal200's kernels on their own rows.
+
+For a model too large for one GPU's share of rows, the weights can also be split by output rows (N) across the
+ranks of a group that all serve the same rows (column parallelism, the tensor-parallel layout); every rank then needs
+the whole output of each linear before the next operation:
+  column_shard(n, world, rank)      the output rows a rank holds (whole 128-row scale blocks)
+  ColumnShardedFP8Linear            an FP8-block linear split that way whose GEMM stores its columns straight into
+                                    every rank's output (the all-gather done by the GEMM's epilogue over NVLink,
+                                    peer-mapped symmetric memory), and the NCCL all-gather baseline beside it
 """
+import ctypes
 import datetime
 
 import torch
@@ -75,3 +84,101 @@ def check_peers(group=None, timeout_s=30.0, tag="peers"):
         store.wait([f"{tag}/{r}" for r in range(world)], timeout)
     except Exception as e:  # the store raises its own timeout type
         raise RuntimeError(f"check_peers({tag}): a peer did not arrive within {timeout_s} s: {e}") from e
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# column shards
+# ---------------------------------------------------------------------------------------------------------------
+MAX_PEERS = 8  # output buffers one gathered GEMM stores into (libbasal200's limit)
+
+
+def column_shard(n, world, rank, unit=128):
+    """Output rows [start, stop) of `rank` when `n` rows are split across `world` ranks in whole `unit`-row blocks
+    (a weight-scale block), contiguous, block counts differing by at most one."""
+    if n % unit:
+        raise ValueError(f"{n} output rows are not whole {unit}-row blocks")
+    b0, b1 = shard_range(n // unit, world, rank)
+    return b0 * unit, b1 * unit
+
+
+class ColumnShardedFP8Linear(torch.nn.Module):
+    """An FP8-block linear (basal_b200.fp8block.BlockFP8Linear) whose output rows are split across the ranks of
+    `group`: each rank keeps its column shard (a part() view) and every rank's forward returns the whole output.
+
+      forward(x)       act_quant, then one GEMM that stores this rank's columns into every rank's [M, N] output
+                       buffer (peer-mapped symmetric memory: its stores cross NVLink tile by tile, no collective
+                       kernel), between two bounded barriers of the group (before: every rank is done with the
+                       previous output; after: every rank's columns have landed). The result is a view of the
+                       shared buffer, valid until the next forward of this module on any rank (clone to keep it).
+      forward_nccl(x)  the baseline: the shard's own linear, an NCCL all-gather, the copy that interleaves the
+                       ranks' columns.
+
+    Each output element is computed exactly as the unsplit linear computes it (same kernel arithmetic, same K order),
+    so both forwards equal BlockFP8Linear.forward bit for bit. Every rank runs the same forwards with the same rows
+    (SPMD); bias is not supported (the gathered GEMM has none)."""
+
+    def __init__(self, full, group=None, timeout_ms=10000):
+        super().__init__()
+        if full.bias is not None:
+            raise ValueError("ColumnShardedFP8Linear: bias is not supported")
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > MAX_PEERS:
+            raise ValueError(f"ColumnShardedFP8Linear: at most {MAX_PEERS} ranks, not {self.world}")
+        self.out_features, self.in_features = full.out_features, full.in_features
+        start, stop = column_shard(self.out_features, self.world, self.rank)
+        if stop == start:
+            raise ValueError(f"ColumnShardedFP8Linear: {self.out_features} rows leave rank {self.rank} none")
+        self.col_off = start
+        self.shard = full.part(start, stop - start)
+        self.timeout_ms = int(timeout_ms)
+        self._buf = None
+        self._hdl = None
+
+    def _buffer(self, rows, dtype, device):
+        """The [rows, N] symmetric output buffer of every rank (made, collectively, when it must grow)."""
+        if self._buf is None or self._buf.shape[0] < rows or self._buf.dtype != dtype:
+            import torch.distributed._symmetric_memory as symm_mem
+            size = max(rows, 2 * self._buf.shape[0]) if self._buf is not None and self._buf.dtype == dtype else rows
+            self._buf, self._hdl = None, None
+            buf = symm_mem.empty((size, self.out_features), dtype=dtype, device=device)
+            self._hdl = symm_mem.rendezvous(buf, self.group)
+            self._buf = buf
+        return self._buf, self._hdl
+
+    def forward(self, x):
+        from . import _lib, ops
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        M = x2.shape[0]
+        if x.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("ColumnShardedFP8Linear: bf16 or fp16 activations")
+        buf, hdl = self._buffer(M, x.dtype, x.device)
+        q, s = ops.fp8_act_quant(x2)
+        off = buf.data_ptr() - hdl.buffer_ptrs[hdl.rank]  # the tensor's place in its allocation, alike on all ranks
+        outs = (ctypes.c_void_p * self.world)(*[p + off for p in hdl.buffer_ptrs])
+        w = self.shard
+        hdl.barrier(channel=0, timeout_ms=self.timeout_ms)
+        _lib.call("basal200_fp8_block_gemm_gather", x.device, _lib.ptr(q), _lib.ptr(s), _lib.ptr(w.weight),
+                  _lib.ptr(w.weight_scale), outs, self.world, self.col_off, self.out_features, _lib.code(x.dtype),
+                  M, w.out_features, self.in_features)
+        hdl.barrier(channel=1, timeout_ms=self.timeout_ms)
+        return buf[:M].view(*shape[:-1], self.out_features)
+
+    def forward_nccl(self, x):
+        shape = x.shape
+        y = self.shard(x.reshape(-1, shape[-1]))
+        M, n = y.shape
+        if all(column_shard(self.out_features, self.world, r)[1] - column_shard(self.out_features, self.world, r)[0]
+               == n for r in range(self.world)):
+            parts = torch.empty((self.world, M, n), dtype=y.dtype, device=y.device)
+            dist.all_gather_into_tensor(parts, y, group=self.group)
+            out = parts.permute(1, 0, 2).reshape(M, self.out_features)
+        else:
+            parts = [torch.empty((M, column_shard(self.out_features, self.world, r)[1]
+                                  - column_shard(self.out_features, self.world, r)[0]), dtype=y.dtype, device=y.device)
+                     for r in range(self.world)]
+            dist.all_gather(parts, y, group=self.group)
+            out = torch.cat(parts, 1)
+        return out.view(*shape[:-1], self.out_features)

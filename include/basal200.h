@@ -56,6 +56,16 @@ int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t 
 int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* One rank's column shard of a column-parallel FP8 block linear (a tensor-parallel model's N-sharded linears; the
+ * reference keeps whole weights on every GPU, so there is no reference function: this replaces the pair
+ * "fp8_block_gemm of the shard, then all-gather of the outputs"): the shard's [M, N] result (its weight rows are the
+ * linear's rows col_off .. col_off + N - 1) is stored into each of the npeers buffers outs[r] ([M, n_total], c_dtype
+ * bf16 or fp16, row-major, peer-mapped device memory of every rank), at columns col_off .. col_off + N - 1, by the
+ * GEMM's own stores. The caller synchronises the ranks afterwards. N, col_off multiples of 128; npeers <= 8. */
+int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
+                                   void* const* outs, int npeers, int64_t col_off, int64_t n_total, int c_dtype,
+                                   int64_t M, int64_t N, int64_t K, void* stream);
+
 /* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:349): each slice's product exact in int32. */
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
                              void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);

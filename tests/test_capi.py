@@ -56,6 +56,12 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 4, 200, 256, null) == 2
     # NVFP4: K % 64
     assert lib.basal200_nvfp4_act_quant(null, 0, null, 4, 96, null, null, null) == 2
+    # column-parallel GEMM with gathered outputs: no output buffer; a shard past the full width; fp32 output
+    outs = (ctypes.c_void_p * 2)(None, None)
+    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 0, 0, 256, 0, 4, 128, 256, null) == 1
+    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 256, 256, 0, 4, 128, 256, null) == 2
+    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 2, 4, 128, 256, null) == 4
+    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 0, 0, 128, 256, null) == 0
     # readout: Kmax beyond 1024
     assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
 

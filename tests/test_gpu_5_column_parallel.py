@@ -1,0 +1,68 @@
+"""The column-parallel FP8 linear on 2 GPUs (child processes, one GPU each, NCCL): the gathered output of the GEMM
+whose epilogue stores each rank's columns into every rank's buffer equals the unsplit linear bit for bit, and so does
+the NCCL all-gather baseline; rows on the few-rows and the many-rows kernel. Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import basal_b200 as b2
+        from basal_b200 import shard
+        dev = torch.device("cuda", rank)
+        g = torch.Generator().manual_seed(3)
+        N, K = 1280, 1024
+        lin = torch.nn.Linear(K, N, bias=False)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(N, K, generator=g) * 0.02)
+        full = b2.fp8block.BlockFP8Linear.of(lin.to(dev))
+        m = shard.ColumnShardedFP8Linear(full, timeout_ms=20000)
+        res = []
+        for M in (16, 300, 37):
+            x = torch.randn(M, K, generator=g).bfloat16().to(dev)
+            want = full(x)
+            got = m(x).clone()
+            base = m.forward_nccl(x)
+            res.append((M, torch.equal(got, want), torch.equal(base, want)))
+        torch.cuda.synchronize()
+        res.append(("faults", b2._lib.device_faults(rank)))
+        out.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gathered_column_parallel_linear_equals_the_whole_linear():
+    world, port = 2, free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=300) for _ in procs), key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, rows in res:
+        assert rows[-1] == ("faults", 0)
+        for M, fused_ok, nccl_ok in rows[:-1]:
+            assert fused_ok, (rank, M)
+            assert nccl_ok, (rank, M)

@@ -87,3 +87,43 @@ def test_shard_range_edges():
     with pytest.raises(ValueError):
         shard.shard_range(4, 2, 2)
     assert shard.cu_seqlens(torch.tensor([3, 2])).tolist() == [0, 3, 5]
+
+
+def test_column_shards_are_whole_scale_blocks():
+    assert [shard.column_shard(5120, 8, r) for r in (0, 7)] == [(0, 640), (4480, 5120)]
+    assert shard.column_shard(19456, 8, 7) == (17024, 19456)                 # 152 blocks: 19 a rank
+    assert [shard.column_shard(640, 4, r) for r in range(4)] == [(0, 256), (256, 384), (384, 512), (512, 640)]
+    with pytest.raises(ValueError):
+        shard.column_shard(200, 2, 0)
+
+
+def _worker_column_module(rank, world, port, out):
+    _init(rank, world, port)
+    try:
+        from basal_b200.fp8block import BlockFP8Linear
+        N, K = 640, 256
+        w = torch.arange(N * K, dtype=torch.float32).reshape(N, K).to(torch.float8_e4m3fn)
+        s = torch.arange(N // 128 * K // 128, dtype=torch.float32).reshape(N // 128, K // 128)
+        m = shard.ColumnShardedFP8Linear(BlockFP8Linear(w, s), timeout_ms=5000)
+        start, stop = shard.column_shard(N, world, rank)
+        ok = (m.col_off == start and m.shard.out_features == stop - start
+              and torch.equal(m.shard.weight.view(torch.uint8), w[start:stop].view(torch.uint8))
+              and torch.equal(m.shard.weight_scale, s[start // 128: stop // 128]))
+        out.put((rank, ok, m.col_off, m.shard.out_features))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_sharded_linear_holds_its_rows_and_scale_blocks():
+    """Host side of the column-parallel linear on gloo ranks: each rank keeps the views of its whole scale blocks."""
+    world, port = 2, free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_column_module, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == [(0, True, 0, 384), (1, True, 384, 256)]
