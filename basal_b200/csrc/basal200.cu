@@ -593,6 +593,20 @@ int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8
   return block_gemm_gather(q, s, w, ws, outs, npeers, col_off, n_total, c_dtype, M, N, K, as_stream(stream));
 }
 
+int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t timeout_ns, void* stream) {
+  if (!pads || world < 1 || world > blockgemm::kMaxPeers || rank < 0 || rank >= world || timeout_ns <= 0)
+    return BASAL200_ERR_ARG;
+  blockgemm::PeerPads pp;
+  for (int r = 0; r < blockgemm::kMaxPeers; ++r) {
+    pp.p[r] = r < world ? pads[r] : nullptr;
+    if (r < world && (!pads[r] || (reinterpret_cast<uintptr_t>(pads[r]) & 3))) return BASAL200_ERR_ALIGN;
+  }
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  blockgemm::peer_barrier_kernel<<<1, 32, 0, as_stream(stream)>>>(pp, world, rank, (long long)timeout_ns);
+  return launched();
+}
+
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
                              void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
   return block_gemm<true>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));

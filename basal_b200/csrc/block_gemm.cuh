@@ -84,6 +84,47 @@ struct OutMaps {
   CUtensorMap m[kMaxPeers];
 };
 
+// ---------------------------------------------------------------------------------------------------------------
+// Peer barrier over peer-mapped signal pads: word r of rank q's pad holds the last call number rank r reached, word
+// kMaxPeers this rank's own call count. Thread r stores the call number into rank r's pad (release, system scope)
+// and waits for rank r's (acquire), giving up after timeout_ns with a fault bit.
+// ---------------------------------------------------------------------------------------------------------------
+struct PeerPads {
+  uint32_t* p[kMaxPeers];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerPads pads, int world, int rank,
+                                                          long long timeout_ns) {
+  __shared__ uint32_t call;
+  if (threadIdx.x == 0) {
+    call = pads.p[rank][kMaxPeers] + 1;  // only this rank's stream touches its count
+    pads.p[rank][kMaxPeers] = call;
+  }
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (r < world) {
+    __threadfence_system();
+    st_release_sys(pads.p[r] + rank, call);
+    const unsigned long long t0 = globaltimer();
+    while ((int)(ld_acquire_sys(pads.p[rank] + r) - call) < 0) {
+      if (globaltimer() - t0 > (unsigned long long)timeout_ns) {
+        atomicOr(&g_fault, kFaultTimeoutPeer);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // Bounded drain wait (the abort flag is already set when it runs).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();

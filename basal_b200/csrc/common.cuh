@@ -17,6 +17,7 @@ enum FaultBits : unsigned {
   kFaultTimeoutEpilogue = BASAL200_FAULT_TIMEOUT_EPILOGUE,
   kFaultTimeoutDrain = BASAL200_FAULT_TIMEOUT_DRAIN,
   kFaultBadId = BASAL200_FAULT_BAD_ID,
+  kFaultTimeoutPeer = BASAL200_FAULT_TIMEOUT_PEER,
 };
 
 // The library is one translation unit (csrc/basal200.cu includes every kernel header), so the word is defined here.

@@ -107,9 +107,11 @@ class ColumnShardedFP8Linear(torch.nn.Module):
 
       forward(x)       act_quant, then one GEMM that stores this rank's columns into every rank's [M, N] output
                        buffer (peer-mapped symmetric memory: its stores cross NVLink tile by tile, no collective
-                       kernel), between two bounded barriers of the group (before: every rank is done with the
-                       previous output; after: every rank's columns have landed). The result is a view of the
-                       shared buffer, valid until the next forward of this module on any rank (clone to keep it).
+                       kernel), between two barriers of the group (libbasal200's peer barrier on the buffers'
+                       signal pads: before, every rank is done with the previous output; after, every rank's
+                       columns have landed; a wait gives up after timeout_ms with a fault bit, never a trap). The
+                       result is a view of the shared buffer, valid until the next forward of this module on any rank
+                       (clone to keep it). It can be captured in a CUDA graph.
       forward_nccl(x)  the baseline: the shard's own linear, an NCCL all-gather, the copy that interleaves the
                        ranks' columns.
 
@@ -135,16 +137,24 @@ class ColumnShardedFP8Linear(torch.nn.Module):
         self.timeout_ms = int(timeout_ms)
         self._buf = None
         self._hdl = None
+        self._outs = None  # the C array of every rank's buffer pointer
+        self._pads = None  # the C array of every rank's signal pad pointer
 
     def _buffer(self, rows, dtype, device):
         """The [rows, N] symmetric output buffer of every rank (made, collectively, when it must grow)."""
         if self._buf is None or self._buf.shape[0] < rows or self._buf.dtype != dtype:
             import torch.distributed._symmetric_memory as symm_mem
             size = max(rows, 2 * self._buf.shape[0]) if self._buf is not None and self._buf.dtype == dtype else rows
-            self._buf, self._hdl = None, None
+            self._buf, self._hdl, self._outs, self._pads = None, None, None, None
             buf = symm_mem.empty((size, self.out_features), dtype=dtype, device=device)
-            self._hdl = symm_mem.rendezvous(buf, self.group)
-            self._buf = buf
+            hdl = symm_mem.rendezvous(buf, self.group)
+            off = buf.data_ptr() - hdl.buffer_ptrs[hdl.rank]  # the tensor's place in its allocation, alike everywhere
+            self._outs = (ctypes.c_void_p * self.world)(*[p + off for p in hdl.buffer_ptrs])
+            hdl.get_signal_pad(hdl.rank, (16,), dtype=torch.int32).zero_()  # the barrier's words, before any use
+            torch.cuda.synchronize(device)
+            check_peers(self.group, timeout_s=max(1.0, self.timeout_ms / 1000), tag="column-shard pads")
+            self._pads = (ctypes.c_void_p * self.world)(*hdl.signal_pad_ptrs)
+            self._buf, self._hdl = buf, hdl
         return self._buf, self._hdl
 
     def forward(self, x):
@@ -156,14 +166,14 @@ class ColumnShardedFP8Linear(torch.nn.Module):
             raise ValueError("ColumnShardedFP8Linear: bf16 or fp16 activations")
         buf, hdl = self._buffer(M, x.dtype, x.device)
         q, s = ops.fp8_act_quant(x2)
-        off = buf.data_ptr() - hdl.buffer_ptrs[hdl.rank]  # the tensor's place in its allocation, alike on all ranks
-        outs = (ctypes.c_void_p * self.world)(*[p + off for p in hdl.buffer_ptrs])
+        outs = self._outs
         w = self.shard
-        hdl.barrier(channel=0, timeout_ms=self.timeout_ms)
+        tmo = self.timeout_ms * 1000000
+        _lib.call("basal200_peer_barrier", x.device, self._pads, self.world, self.rank, tmo)
         _lib.call("basal200_fp8_block_gemm_gather", x.device, _lib.ptr(q), _lib.ptr(s), _lib.ptr(w.weight),
                   _lib.ptr(w.weight_scale), outs, self.world, self.col_off, self.out_features, _lib.code(x.dtype),
                   M, w.out_features, self.in_features)
-        hdl.barrier(channel=1, timeout_ms=self.timeout_ms)
+        _lib.call("basal200_peer_barrier", x.device, self._pads, self.world, self.rank, tmo)
         return buf[:M].view(*shape[:-1], self.out_features)
 
     def forward_nccl(self, x):

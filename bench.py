@@ -481,6 +481,84 @@ def run_sweep(fmts):
     print(json.dumps({"faults": b2._lib.device_faults(0), "hbm_peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}))
 
 
+# C5's projections (hidden 2560; 16 query and 4 key/value heads of 128; SwiGLU 9728), as (name, N, K)
+C5_PROJ = (("qkv", 3072, 2560), ("o", 2560, 2048), ("gate_up", 19456, 2560), ("down", 2560, 9728))
+
+
+def run_sweep_tp(rank, world, local_rank, steps=20):
+    """The column-parallel FP8 linears of C5's projections split over the `world` GPUs of a torchrun (every rank the
+    same rows): the GEMM whose epilogue stores each rank's columns into every rank's output (fused all-gather)
+    against the shard's GEMM + NCCL all-gather + interleave copy. One JSON line per (projection, rows) on rank 0:
+    us per forward (CUDA events over `steps` forwards, max over ranks), TFLOP/s of the whole linear, and the bound
+    = max(shard FLOPs / FP8 peak, bytes a rank sends over NVLink / 770 GB/s measured per direction)."""
+    import torch
+
+    import basal_b200 as b2
+    from basal_b200 import shard
+    dev = torch.device("cuda", local_rank)
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"] * 1e12
+    g = torch.Generator(device=dev).manual_seed(7)
+    for name, N, K in C5_PROJ:
+        lin = torch.nn.Linear(K, N, bias=False, device=dev)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, 0.02, generator=g)
+        full = b2.fp8block.BlockFP8Linear.of(lin)
+        del lin
+        m = shard.ColumnShardedFP8Linear(full, timeout_ms=30000)
+        n_local = m.shard.out_features
+        for M in (256, 4096):
+            x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+            times, how = {}, {}
+            for mode, fn in (("fused", m.forward), ("nccl", m.forward_nccl)):
+                for _ in range(3):
+                    fn(x)
+                torch.cuda.synchronize()
+                # `steps` forwards captured in one CUDA graph (the device time, not Python's); eager if capture fails
+                graph = None
+                try:
+                    side = torch.cuda.Stream()
+                    side.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.stream(side):
+                        graph = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(graph, stream=side):
+                            for _ in range(steps):
+                                fn(x)
+                    torch.cuda.current_stream().wait_stream(side)
+                    torch.cuda.synchronize()
+                except Exception:  # noqa: BLE001 - a library that cannot be captured: time it eagerly
+                    graph = None
+                    torch.cuda.synchronize()
+                ok = shard.max_over_ranks(0.0 if graph is not None else 1.0) == 0.0  # every rank captured
+                shard.check_peers(tag=f"tp-{name}-{M}-{mode}")
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                if ok:
+                    graph.replay()
+                else:
+                    for _ in range(steps):
+                        fn(x)
+                e1.record()
+                torch.cuda.synchronize()
+                del graph
+                times[mode] = shard.max_over_ranks(e0.elapsed_time(e1) / steps * 1e3)
+                how[mode] = "graph" if ok else "eager"
+            flops = 2 * M * N * K
+            bound_us = max(2 * M * n_local * K / fp8_peak, M * n_local * 2 * (world - 1) / 770e9) * 1e6
+            if rank == 0:
+                print(json.dumps({"sweep": "C5 column-parallel FP8 linear", "proj": name, "M": M, "N": N, "K": K,
+                                  "gpus": world, "fused_us": round(times["fused"], 2),
+                                  "nccl_us": round(times["nccl"], 2),
+                                  "fused_tflops": round(flops / times["fused"] / 1e6, 1),
+                                  "nccl_tflops": round(flops / times["nccl"] / 1e6, 1),
+                                  "bound_us": round(bound_us, 2),
+                                  "fused_of_bound": round(bound_us / times["fused"], 3),
+                                  "timing": how}), flush=True)
+        del m, full
+    if rank == 0:
+        print(json.dumps({"faults": b2._lib.device_faults(local_rank)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -489,8 +567,23 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
     ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout) "
-                    "instead of the benchmark")
+                    "instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
     args = ap.parse_args()
+    if args.sweep == "tp":  # under torchrun, 2 or more GPUs
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+        local_rank = int(os.environ.get("LOCAL_RANK", 0))
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+        try:
+            run_sweep_tp(rank, world, local_rank)
+        finally:
+            dist.destroy_process_group()
+        return
     if args.sweep:
         run_sweep(args.sweep.split(","))
         return

@@ -66,6 +66,13 @@ int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8
                                    void* const* outs, int npeers, int64_t col_off, int64_t n_total, int c_dtype,
                                    int64_t M, int64_t N, int64_t K, void* stream);
 
+/* A barrier of the `world` ranks that share peer-mapped signal pads (pads[r]: rank r's pad, at least 9 uint32 words,
+ * zero before the first call, used by nothing else): enqueued on `stream`, it returns (on the device) once every rank
+ * has reached the same call, with each rank's stream work before it visible to the others' work after it. A wait
+ * for a rank gives up after timeout_ns: the kernel records BASAL200_FAULT_TIMEOUT_PEER and ends (no trap). The call
+ * count lives in the pad, so a captured CUDA graph may replay the barrier. world <= 8. */
+int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t timeout_ns, void* stream);
+
 /* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:349): each slice's product exact in int32. */
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
                              void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
@@ -141,14 +148,15 @@ int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx
 
 /* ---- Diagnostics ---- */
 
-/* Fault bits (basal200_device_faults): a bounded wait of a GEMM gave up (producer, MMA issuer, epilogue, drain), or a
- * readout id was out of range. */
+/* Fault bits (basal200_device_faults): a bounded wait of a GEMM gave up (producer, MMA issuer, epilogue, drain), a
+ * readout id was out of range, or a peer barrier's wait for another rank gave up. */
 enum {
   BASAL200_FAULT_TIMEOUT_PRODUCER = 1,
   BASAL200_FAULT_TIMEOUT_MMA = 2,
   BASAL200_FAULT_TIMEOUT_EPILOGUE = 4,
   BASAL200_FAULT_TIMEOUT_DRAIN = 8,
-  BASAL200_FAULT_BAD_ID = 16
+  BASAL200_FAULT_BAD_ID = 16,
+  BASAL200_FAULT_TIMEOUT_PEER = 32
 };
 
 /* The fault bits kernels on `device` recorded when a bounded wait gave up (0: none); clear != 0 resets them.

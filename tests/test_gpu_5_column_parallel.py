@@ -66,3 +66,24 @@ def test_gathered_column_parallel_linear_equals_the_whole_linear():
         for M, fused_ok, nccl_ok in rows[:-1]:
             assert fused_ok, (rank, M)
             assert nccl_ok, (rank, M)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA")
+def test_peer_barrier_gives_up_on_an_absent_rank():
+    """The barrier's wait for a rank that never arrives (a second pad that nothing writes, local memory, one GPU) ends
+    after its limit with the peer-timeout fault bit, and the context stays usable; a one-rank barrier passes."""
+    import ctypes
+
+    import basal_b200 as b2
+    from basal_b200 import _lib
+    b2._lib.device_faults(0)  # clear
+    pads = [torch.zeros(16, dtype=torch.int32, device="cuda") for _ in range(2)]
+    arr = (ctypes.c_void_p * 2)(*[p.data_ptr() for p in pads])
+    _lib.call("basal200_peer_barrier", torch.device("cuda", 0), arr, 1, 0, 50_000_000)
+    assert b2._lib.device_faults(0) == 0
+    assert int(pads[0][0]) == 1 and int(pads[0][8]) == 1  # its own arrival and call count
+    _lib.call("basal200_peer_barrier", torch.device("cuda", 0), arr, 2, 0, 50_000_000)  # rank 1 never comes
+    assert b2._lib.device_faults(0) == 32                                                  # BASAL200_FAULT_TIMEOUT_PEER
+    assert int(pads[1][0]) == 2                         # it told the absent rank it arrived (call 2)
+    y = torch.ones(4, device="cuda") * 2
+    assert float(y.sum()) == 8.0
