@@ -27,12 +27,12 @@ SIGNATURES = {
     "basal200_int8_act_quant": [_P, _I, _I64, _I64, _P, _P, _P],
     "basal200_fp8_block_quantize": [_P, _I, _I64, _I64, _P, _P, _P],
     "basal200_int8_block_quantize": [_P, _I, _I64, _I64, _P, _P, _P],
-    "basal200_fp8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
+    "basal200_fp8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I64, _P],
     "basal200_fp8_block_gemm_gather": [_P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I64, _I64, _I64, _P],
     "basal200_peer_barrier": [_P, _I, _I, _I64, _P],
-    "basal200_int8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
-    "basal200_fp8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
-    "basal200_int8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
+    "basal200_int8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I64, _P],
+    "basal200_fp8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
+    "basal200_int8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
     "basal200_fp8_block_linear_noalloc": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "basal200_nvfp4_act_quant": [_P, _I, _P, _I64, _I64, _P, _P, _P],
     "basal200_nvfp4_gemm": [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
@@ -58,6 +58,8 @@ def lib():
             f.argtypes, f.restype = args, ctypes.c_int
         L.basal200_status_string.argtypes, L.basal200_status_string.restype = [_I], ctypes.c_char_p
         L.basal200_version.argtypes, L.basal200_version.restype = [], _I
+        L.basal200_block_gemm_workspace_bytes.argtypes = [_I64, _I64, _I64]
+        L.basal200_block_gemm_workspace_bytes.restype = _I64
         L.basal200_device_faults.argtypes, L.basal200_device_faults.restype = [_I, _I], ctypes.c_uint
         _lib = L
     return _lib
@@ -90,6 +92,12 @@ def call(name, device, *args):
     if rc != OK:
         msg = f"{name}: {L.basal200_status_string(rc).decode()} (status {rc})"
         raise (ValueError if rc in _VALUE_ERRORS else RuntimeError)(msg)
+
+
+def gemm_workspace(M, N, K, device):
+    """A workspace tensor for the block GEMM of (M, N, K), or None when the shape takes none (ptr(None) is NULL)."""
+    n = int(lib().basal200_block_gemm_workspace_bytes(int(M), int(N), int(K)))
+    return torch.empty(n, dtype=torch.uint8, device=device) if n > 0 else None
 
 
 def device_faults(device=0, clear=True):

@@ -37,7 +37,8 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14 };  // kSlotFp4 .. + 5, kSlotSmall .. + 11
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26 };  // kSlotFp4 .. + 5, kSlotSmall .. + 11,
+                                                                     // kSlotSplit .. + 3
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -326,9 +327,68 @@ int small_gemm(int dev, const void* q, const float* s, const void* w, const floa
   return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st);
 }
 
+// Few rows and fewer weight tiles than this: the split kernels (every SM streams weights), when the caller's
+// workspace holds the products and they stay well inside L2.
+constexpr int64_t kSplitMaxTiles = 64;  // measured at N = 12288 (96 tiles): no faster than one CTA a tile
+constexpr int64_t kSplitMaxBytes = (int64_t)32 << 20;
+
+// Workspace bytes that make the few-rows GEMM of (M, N, K) take the split kernels; 0 for a shape that does not.
+int64_t split_workspace(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || M > smallgemm::MAX_ROWS || N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
+  const int64_t tiles = N / smallgemm::BW, nkb = K / 128;
+  if (nkb < 2 || nkb > smallgemm::MAX_KB || tiles > kSplitMaxTiles) return 0;
+  const int64_t bytes = smallgemm::split_prod_bytes(M, N, nkb);
+  return bytes <= kSplitMaxBytes ? bytes : 0;
+}
+
+template <bool INT8, int OUT, int NT>
+int split_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
+                      void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
+                      void* work, cudaStream_t st) {
+  auto kp = smallgemm::split_products_kernel<INT8, NT>;
+  constexpr size_t smem = smallgemm::split_smem_bytes<NT>();
+  const int slot = kSlotSplit + (INT8 ? 2 : 0) + (NT == 32 ? 0 : 1);
+  int rc = set_smem(dev, slot, kp, smem);
+  if (rc) return rc;
+  CUtensorMap tw, tt;
+  if ((rc = tmap_u8(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, smallgemm::BK, smallgemm::BW))) return rc;
+  if ((rc = tmap_u8(&tt, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, smallgemm::BK, NT))) return rc;
+  smallgemm::SplitParams sp;
+  sp.prod = static_cast<float*>(work);
+  sp.M = (int)M;
+  sp.nkb = (int)(K / 128);
+  sp.units = N / smallgemm::BW * sp.nkb;
+  const int64_t grid = sp.units < g_dev[dev].sms ? sp.units : g_dev[dev].sms;
+  if ((rc = launch_pdl(kp, (unsigned)grid, smallgemm::SplitCfg<NT>::THREADS, smem, st, tw, tt, sp))) return rc;
+  smallgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = bias;
+  for (int r = 0; r < blockgemm::kMaxPeers; ++r) p.cs[r] = r < npeers ? cs[r] : nullptr;
+  p.npeers = npeers;
+  p.ldc = ldc;
+  p.col_off = col_off;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nkb = sp.nkb;
+  const dim3 rgrid((unsigned)(N / smallgemm::BW), (unsigned)M);
+  return launch_pdl(smallgemm::split_reduce_kernel<OUT>, rgrid, smallgemm::REDUCE_THREADS, 0, st,
+                    static_cast<const float*>(work), p);
+}
+
+template <bool INT8, int OUT>
+int split_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c,
+               int64_t M, int64_t N, int64_t K, void* work, cudaStream_t st) {
+  void* const cs[1] = {c};
+  if (M <= 32) return split_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
+  return split_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
+}
+
+// work / work_bytes: the caller's workspace (may be null); when it holds split_workspace(M, N, K) > 0 bytes, the
+// few-rows GEMM runs split over the SMs, otherwise unsplit (the same bits either way).
 template <bool INT8>
 int block_gemm(const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c, int ct,
-               int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+               int64_t M, int64_t N, int64_t K, void* work, int64_t work_bytes, cudaStream_t st) {
   if (M < 0 || N <= 0 || K <= 0) return BASAL200_ERR_ARG;
   if (N % 128 || K % 128) return BASAL200_ERR_SHAPE;
   if (M == 0) return BASAL200_OK;
@@ -338,6 +398,16 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   void* const cs[1] = {c};
+  const int64_t split = split_workspace(M, N, K);
+  if (split > 0 && work && work_bytes >= split) {
+    if (!aligned16(work)) return BASAL200_ERR_ALIGN;
+    switch (ct) {
+      case BASAL200_BF16: return split_gemm<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, c, M, N, K, work, st);
+      case BASAL200_F16: return split_gemm<INT8, BASAL200_F16>(dev, q, s, w, ws, bias, c, M, N, K, work, st);
+      case BASAL200_F32: return split_gemm<INT8, BASAL200_F32>(dev, q, s, w, ws, bias, c, M, N, K, work, st);
+      default: return BASAL200_ERR_DTYPE;
+    }
+  }
   if (M <= smallgemm::MAX_ROWS && K / 128 <= smallgemm::MAX_KB && N / smallgemm::BW <= 65535) {
     switch (ct) {
       case BASAL200_BF16: return small_gemm<INT8, BASAL200_BF16>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, st);
@@ -582,9 +652,12 @@ int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t 
   return weight_quant<true>(w, w_dtype, N, K, q, s, as_stream(stream));
 }
 
+int64_t basal200_block_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) { return split_workspace(M, N, K); }
+
 int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
-                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
-  return block_gemm<false>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));
+                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+  return block_gemm<false>(q, s, w, ws, bias, c, c_dtype, M, N, K, workspace, workspace_bytes, as_stream(stream));
 }
 
 int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
@@ -608,26 +681,29 @@ int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t ti
 }
 
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
-                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
-  return block_gemm<true>(q, s, w, ws, bias, c, c_dtype, M, N, K, as_stream(stream));
+                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  return block_gemm<true>(q, s, w, ws, bias, c, c_dtype, M, N, K, workspace, workspace_bytes, as_stream(stream));
 }
 
 int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,
                               void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
-                              void* stream) {
+                              void* workspace, int64_t workspace_bytes, void* stream) {
   if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
   int rc = act_quant<false>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
   if (rc) return rc;
-  return block_gemm<false>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+  return block_gemm<false>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, workspace, workspace_bytes,
+                           as_stream(stream));
 }
 
 int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, const float* ws, const void* bias,
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
-                               void* stream) {
+                               void* workspace, int64_t workspace_bytes, void* stream) {
   if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
   int rc = act_quant<true>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
   if (rc) return rc;
-  return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+  return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, workspace, workspace_bytes,
+                          as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing
@@ -646,7 +722,7 @@ int basal200_fp8_block_linear_noalloc(const void* x, int x_dtype, const uint8_t*
   if ((rc = noalloc_scratch(dev, &q, &s))) return rc;
   rc = act_quant<false>(x, x_dtype, M, K, q, s, as_stream(stream));
   if (rc) return rc;
-  return block_gemm<false>(q, s, w, ws, bias, y, x_dtype, M, N, K, as_stream(stream));
+  return block_gemm<false>(q, s, w, ws, bias, y, x_dtype, M, N, K, nullptr, 0, as_stream(stream));
 }
 
 int basal200_nvfp4_act_quant(const void* x, int x_dtype, const float* inv_g, int64_t M, int64_t K, uint8_t* q,

@@ -4,8 +4,9 @@
 // The same arithmetic as block_gemm.cuh, element for element: per 128-deep slice kb the exact product of the codes
 // (tcgen05.mma, kind::f8f6f4 -> f32 or kind::i8 -> s32), then acc = fma(product, a_s * b_s, acc) in slice order from
 // zero, a_s * b_s rounded once. So a row's output is bit-identical whichever kernel computes it and whatever the other
-// rows are, as the reference requires (basal/blockquant.py:14-16, tests/test_fp8block.py:134-148): the reduction is
-// never split.
+// rows are, as the reference requires (basal/blockquant.py:14-16, tests/test_fp8block.py:134-148): the chain is never
+// reassociated (the split variant at the end of this file spreads the slices' products over the SMs, then runs the same
+// chain in order).
 //
 // Operands swapped: a tile is 128 weight rows (the MMA's M) x NT token rows (the MMA's N: 32 or 64, the rows past M
 // read as zeros). The products of two codes are exact and the MMA reduces along K either way, so the swap changes no
@@ -286,6 +287,227 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+
+// ---------------------------------------------------------------------------------------------------------------
+// The same GEMM with the slices spread over every SM, for weights of fewer 128-row tiles than the GPU has SMs (N <
+// 19,000 or so): the kernel above puts one CTA on each tile, so at N = 2048 16 SMs stream the weights and the rest
+// idle. Here the (tile, slice) units are dealt out in contiguous runs to min(#SMs, units) CTAs, each of which writes
+// the raw 128-deep product of each of its units (fp32; INT8's s32 products, below 2^21, converted exactly) to a
+// workspace; a second kernel then runs, per output, the same chain acc = fma(product_kb, a_s * b_s, acc) in slice
+// order from zero as both other kernels. So a row's bits still do not depend on the kernel or on the other rows.
+// The products cost 4 bytes per (token, output, slice) of workspace traffic, which stays in L2 at these sizes.
+// ---------------------------------------------------------------------------------------------------------------
+template <int NT>
+struct SplitCfg {
+  static constexpr int STAGE_BYTES = W_BYTES + NT * BK;
+  static constexpr int STAGES = NT == 32 ? 9 : 6;  // multiples of MMA_WARPS: each stage and each TMEM slot is served
+  static constexpr int TSLOTS = NT == 32 ? 15 : 6;  // by one issuer, so its barrier phases come in program order
+  static_assert(STAGES % MMA_WARPS == 0 && TSLOTS % MMA_WARPS == 0, "stage / slot ownership");
+  static_assert(TSLOTS * NT <= 512, "TMEM columns");
+  static constexpr int EPI_WARPS = NT / 32 * 4;
+  static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+template <int NT>
+struct SplitSmem {
+  static constexpr int STAGES = SplitCfg<NT>::STAGES;
+  static constexpr int TSLOTS = SplitCfg<NT>::TSLOTS;
+  uint8_t stage[STAGES][SplitCfg<NT>::STAGE_BYTES];  // [weights 128 x 128][tokens NT x 128], 128-byte swizzle each
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[TSLOTS];
+  uint64_t tempty[TSLOTS];
+  uint64_t mdrain;
+  uint32_t tmem_base;
+  int abort;
+};
+template <int NT>
+constexpr size_t split_smem_bytes() {
+  return sizeof(SplitSmem<NT>) + 1024;
+}
+
+struct SplitParams {
+  float* prod;    // [N/128][nkb][M][128] fp32: unit (tile, kb)'s product of token j and weight row r
+  int64_t units;  // (N / 128) * nkb
+  int M, nkb;
+};
+
+// Workspace bytes of the split kernels for M tokens, N outputs and nkb slices.
+__host__ __device__ constexpr int64_t split_prod_bytes(int64_t M, int64_t N, int64_t nkb) { return M * N * nkb * 4; }
+
+template <bool INT8, int NT>
+__global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
+    split_products_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
+                          const SplitParams p) {
+  using S = SplitSmem<NT>;
+  using C = SplitCfg<NT>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int TSLOTS = C::TSLOTS;
+  extern __shared__ uint8_t smem_raw[];
+  S& sh = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int nkb = p.nkb;
+  // this CTA's run of units [u0, u0 + nu): unit u is slice u % nkb of weight tile u / nkb
+  const int64_t u0 = (int64_t)blockIdx.x * p.units / gridDim.x;
+  const int nu = (int)((int64_t)(blockIdx.x + 1) * p.units / gridDim.x - u0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int t = 0; t < TSLOTS; ++t) {
+      mbar_init(&sh.tfull[t], 1);
+      mbar_init(&sh.tempty[t], C::EPI_WARPS);
+    }
+    mbar_init(&sh.mdrain, MMA_WARPS);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmT);
+  }
+  if (warp == 2) tmem_alloc(&sh.tmem_base, C::TMEM_COLS);
+  pdl_launch();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t filled = 0, last_phase = 0;
+      // weights of the first ring of units before pdl_wait (no kernel that lets its successor start early writes
+      // weights); the tokens, an earlier kernel's output, after it
+      const int pre = nu < STAGES ? nu : STAGES;
+      for (int j = 0; j < pre; ++j) {
+        const int64_t u = u0 + j;
+        mbar_arrive_expect_tx(&sh.full[j], C::STAGE_BYTES);
+        tma_load_2d(sh.stage[j], &tmW, &sh.full[j], (int)(u % nkb) * BK, (int)(u / nkb) * BW);
+        filled |= 1u << j;
+      }
+      pdl_wait();
+      for (int j = 0; j < pre; ++j)
+        tma_load_2d(sh.stage[j] + W_BYTES, &tmT, &sh.full[j], (int)((u0 + j) % nkb) * BK, 0);
+      for (int j = pre; j < nu; ++j) {
+        const int stage = j % STAGES;
+        const uint32_t phase = (uint32_t)(j / STAGES) & 1;
+        if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) break;
+        const int64_t u = u0 + j;
+        mbar_arrive_expect_tx(&sh.full[stage], C::STAGE_BYTES);
+        tma_load_2d(sh.stage[stage], &tmW, &sh.full[stage], (int)(u % nkb) * BK, (int)(u / nkb) * BW);
+        tma_load_2d(sh.stage[stage] + W_BYTES, &tmT, &sh.full[stage], (int)(u % nkb) * BK, 0);
+        filled |= 1u << stage;
+        last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+      }
+      if (*abort_flag) {  // let the copies already issued land
+        for (int s = 0; s < STAGES; ++s)
+          if (filled & (1u << s)) blockgemm::drain_wait(&sh.full[s], (last_phase >> s) & 1);
+      }
+    }
+  } else if (warp < EPI_WARP0) {
+    // ---------------- MMA issuers: warp 1 + i issues units i, i + 3, ... ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = INT8 ? idesc_dense(2, 1, 1, BW, NT) : idesc_dense(1, 0, 0, BW, NT);
+      const int i = warp - 1;
+      for (int j = i; j < nu; j += MMA_WARPS) {
+        const int slot = j % TSLOTS;
+        if (!mbar_wait(&sh.tempty[slot], ((uint32_t)(j / TSLOTS) & 1) ^ 1, abort_flag, kFaultTimeoutMma)) break;
+        const int stage = j % STAGES;
+        if (!mbar_wait(&sh.full[stage], (uint32_t)(j / STAGES) & 1, abort_flag, kFaultTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(slot * NT);
+        const uint64_t ad = desc_sw128(smem_u32(sh.stage[stage]));
+        const uint64_t bd = desc_sw128(smem_u32(sh.stage[stage] + W_BYTES));
+#pragma unroll
+        for (int k = 0; k < BK / 32; ++k) {
+          if (INT8)
+            mma_i8(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+          else
+            mma_f8f6f4(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
+        }
+        mma_commit(&sh.empty[stage]);
+        mma_commit(&sh.tfull[slot]);
+      }
+      // every MMA this thread issued has finished before TMEM and shared memory are released
+      mma_commit(&sh.mdrain);
+      blockgemm::drain_wait(&sh.mdrain, 0);
+    }
+  } else {
+    // ---------------- product readout: thread = weight row, 32 tokens a warp ----------------
+    const int ew = warp - EPI_WARP0;
+    const int quad = warp & 3;       // TMEM lane quadrant: weight rows quad * 32 ..
+    const int half = ew >> 2;        // which 32 of the NT tokens
+    const int t = quad * 32 + lane;  // weight row of the tile
+    const int ntok = p.M - half * 32 < 32 ? p.M - half * 32 : 32;  // this warp's real tokens (may be <= 0)
+    const uint32_t tcol = tmem + ((uint32_t)(quad * 32) << 16) + half * 32;
+    pdl_wait();  // the workspace may still be read by the kernel before this one
+    for (int j = 0; j < nu; ++j) {
+      const int slot = j % TSLOTS;
+      if (!blockgemm::warp_wait(&sh.tfull[slot], (uint32_t)(j / TSLOTS) & 1, abort_flag, kFaultTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      uint32_t x[32];
+      tmem_ld32_issue(tcol + (uint32_t)(slot * NT), x);
+      tmem_ld_wait32(x);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty[slot]);
+      float* dst = p.prod + ((u0 + j) * p.M + half * 32) * BW + t;  // unit u0 + j = tile * nkb + kb
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        if (jj < ntok) __stcg(dst + (int64_t)jj * BW, INT8 ? __int2float_rn((int)x[jj]) : __uint_as_float(x[jj]));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Second kernel of the split GEMM: a CTA per (token, weight tile), thread = weight row. a_s * b_s of the token and tile
+// for every slice go to shared memory first; then every slice's product is loaded at once (one L2 round trip, not one
+// per slice) and summed in slice order, acc = fma(product, a_s * b_s, acc) from zero; then the cast (+ bias) and the
+// stores.
+constexpr int REDUCE_THREADS = BW;
+
+template <int OUT>
+__global__ void __launch_bounds__(REDUCE_THREADS)
+    split_reduce_kernel(const float* __restrict__ prod, const Params p) {
+  __shared__ float sc[MAX_KB];
+  pdl_launch();
+  pdl_wait();  // the products kernel has completed and its stores are visible
+  const int tile = blockIdx.x;
+  const int tok = blockIdx.y;
+  const int row = threadIdx.x;
+  const int nkb = p.nkb;
+  if (row < nkb) sc[row] = __fmul_rn(__ldg(p.s + (int64_t)tok * nkb + row), __ldg(p.ws + (int64_t)tile * nkb + row));
+  const int64_t kstride = (int64_t)p.M * BW;
+  const float* src = prod + ((int64_t)tile * nkb * p.M + tok) * BW + row;  // + kb * kstride
+  float pv[MAX_KB];
+#pragma unroll
+  for (int kb = 0; kb < MAX_KB; ++kb)
+    if (kb < nkb) pv[kb] = __ldcg(src + kb * kstride);
+  __syncthreads();
+  float acc = 0.f;
+#pragma unroll
+  for (int kb = 0; kb < MAX_KB; ++kb)
+    if (kb < nkb) acc = __fmaf_rn(pv[kb], sc[kb], acc);
+  const int n = tile * BW + row;
+#pragma unroll
+  for (int r = 0; r < blockgemm::kMaxPeers; ++r)  // constant indices keep the parameter block out of local memory
+    if (r < p.npeers) store1<OUT>(p.cs[r], (int64_t)tok * p.ldc + p.col_off + n, acc, p.bias, n);
 }
 
 }  // namespace smallgemm

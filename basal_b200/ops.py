@@ -78,7 +78,9 @@ def _block_gemm(q, s, w, ws, dtype, integer, bias=None):
     if bias is not None:
         bias = _c(bias.to(dtype))
     name = "basal200_int8_block_gemm" if integer else "basal200_fp8_block_gemm"
-    call(name, q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(bias), ptr(c), code(dtype), M, N, K)
+    work = _lib.gemm_workspace(M, N, K, q.device)
+    call(name, q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(bias), ptr(c), code(dtype), M, N, K, ptr(work),
+         0 if work is None else work.numel())
     return c
 
 
@@ -115,7 +117,9 @@ def _block_linear(x, w, ws, bias, integer):
     if bias is not None:
         bias = _c(bias.to(x.dtype))
     name = "basal200_int8_block_linear" if integer else "basal200_fp8_block_linear"
-    call(name, x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(bias), ptr(y), M, N, K, ptr(q), ptr(s))
+    work = _lib.gemm_workspace(M, N, K, x.device)
+    call(name, x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(bias), ptr(y), M, N, K, ptr(q), ptr(s),
+         ptr(work), 0 if work is None else work.numel())
     return y
 
 

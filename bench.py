@@ -336,6 +336,7 @@ CASES = {
     # GB on the device): 2 untimed launches, then 3 launches of the kernel under study
     "fp8_gemm": ("fp8", 65536, 5120, 2048),
     "fp8_gemm_few": ("fp8", 16, 12288, 2048),  # the few-rows (weight-streaming) kernel; ncu flushes L2 per pass
+    "fp8_gemm_split": ("fp8", 16, 2048, 6144),  # the few-rows GEMM split over the SMs (products + ordered sum)
     "int8_gemm": ("int8", 65536, 5120, 2048),
     "fp8_act_quant": ("fp8", 65536, 0, 2048),
     "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
@@ -369,9 +370,23 @@ def run_case(name):
         q, s = mod.quantize(torch.randn(N, K, device=dev, generator=g) * 0.02)
         qa, sa = mod.act_quant(x)
         for _ in range(5):
-            mod.gemm(qa, sa, q, s, torch.bfloat16)
+            if name == "fp8_gemm_few":  # the unsplit kernel, one CTA on each weight tile
+                unsplit_gemm(b2, fmt, qa, sa, q, s)
+            else:
+                mod.gemm(qa, sa, q, s, torch.bfloat16)
     torch.cuda.synchronize()
     print(json.dumps({"case": name, "M": M, "N": N, "K": K, "faults": b2._lib.device_faults(0)}))
+
+
+def unsplit_gemm(b2, fmt, qa, sa, q, s):
+    """The block GEMM through the C ABI with no workspace (bf16 out): for M <= 64, one CTA on each weight tile."""
+    import torch
+    M, K = qa.shape
+    c = torch.empty(M, q.shape[0], dtype=torch.bfloat16, device=qa.device)
+    name = "basal200_int8_block_gemm" if fmt == "int8" else "basal200_fp8_block_gemm"
+    b2._lib.call(name, qa.device, qa.data_ptr(), sa.data_ptr(), q.data_ptr(), s.data_ptr(), None, c.data_ptr(),
+                 b2._lib.BF16, M, q.shape[0], K, None, 0)
+    return c
 
 
 def run_sweep(fmts):
@@ -464,6 +479,9 @@ def run_sweep(fmts):
                     gemm = [lambda q=q, s=s: mod.gemm(qa, sa, q, s, torch.bfloat16) for q, s in qw]
                     linear = [lambda q=q, s=s: mod.linear(x, q, s) for q, s in qw]
                     wbytes, abytes = N * K + 4 * (N // 128) * (K // 128), M * K + 4 * M * (K // 128)
+                    split = b2._lib.lib().basal200_block_gemm_workspace_bytes(M, N, K) > 0
+                    # the same GEMM without a workspace: the few-rows kernel that puts one CTA on each weight tile
+                    whole = [lambda q=q, s=s: unsplit_gemm(b2, fmt, qa, sa, q, s) for q, s in qw] if split else None
 
                 def body(fns):
                     flush.sum()
@@ -472,12 +490,18 @@ def run_sweep(fmts):
                 tg = (graph_us(lambda: body(gemm)) - base) / reps
                 tl = (graph_us(lambda: body(linear)) - base) / reps
                 byts = wbytes + abytes + 2 * M * N
-                print(json.dumps({
+                line = {
                     "sweep": "C3" if fmt == "nvfp4" else ("C4" if fmt == "int8" else "C3/C4 shapes, FP8"),
                     "format": fmt, "M": M, "N": N, "K": K, "gemm_us": round(tg, 2),
                     "gemm_tflops": round(2 * M * N * K / tg / 1e6, 1), "gemm_gbs": round(byts / tg / 1e3, 1),
                     "gemm_hbm_frac": round(byts / tg / 1e3 / pk["hbm_gbs"], 3), "linear_us": round(tl, 2),
-                    "kernel": ("nvfp4" if fmt == "nvfp4" else ("few-rows" if M <= 64 else "block"))}), flush=True)
+                    "kernel": ("nvfp4" if fmt == "nvfp4" else
+                               ("few-rows split" if M <= 64 and split else ("few-rows" if M <= 64 else "block")))}
+                if fmt != "nvfp4" and whole:
+                    tw = (graph_us(lambda: body(whole)) - base) / reps
+                    line["unsplit_gemm_us"] = round(tw, 2)
+                    line["unsplit_hbm_frac"] = round(byts / tw / 1e3 / pk["hbm_gbs"], 3)
+                print(json.dumps(line), flush=True)
     print(json.dumps({"faults": b2._lib.device_faults(0), "hbm_peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}))
 
 

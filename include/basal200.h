@@ -50,11 +50,19 @@ int basal200_fp8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K
 int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* q, float* s,
                                  void* stream);
 
+/* Workspace bytes with which the block GEMMs and linears below spread a few-rows GEMM (M <= 64) over every SM; 0 for
+ * a shape that never takes it (M > 64, or weights of enough 128-row tiles to fill the GPU). Pure: no device call. */
+int64_t basal200_block_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
 /* C [M, N] (c_dtype) = sum over 128-deep K slices of (q_kb . w_kb^T) * s[m, kb] * ws[n/128, kb], fp32 accumulation,
  * then + bias[n] (c_dtype, may be NULL) rounded as torch adds a bias to the cast output. Replaces the torch op
- * basal::fp8_block_gemm (basal/blockquant.py:151-159, kernel :63-106). N % 128 == 0, K % 128 == 0; M may be 0. */
+ * basal::fp8_block_gemm (basal/blockquant.py:151-159, kernel :63-106). N % 128 == 0, K % 128 == 0; M may be 0.
+ * workspace (16-byte aligned, may be NULL): when it holds basal200_block_gemm_workspace_bytes(M, N, K) > 0 bytes, a
+ * few-rows GEMM writes each 128-deep slice's product there and sums them in a second kernel, in the same order and
+ * with the same roundings as without it: the output bits do not change, only which SMs stream the weights. */
 int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, const void* bias,
-                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+                            void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* workspace,
+                            int64_t workspace_bytes, void* stream);
 
 /* One rank's column shard of a column-parallel FP8 block linear (a tensor-parallel model's N-sharded linears; the
  * reference keeps whole weights on every GPU, so there is no reference function: this replaces the pair
@@ -75,20 +83,21 @@ int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t ti
 
 /* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:349): each slice's product exact in int32. */
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
-                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+                             void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* workspace,
+                             int64_t workspace_bytes, void* stream);
 
 /* The whole linear: act_quant of x into the caller's scratch (q_scratch [M, K] bytes, s_scratch [M, K/128] fp32),
- * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias. Replaces fp8block.linear / BlockFormat.linear
- * (basal/fp8block.py:285-296, basal/blockquant.py:175-183) and the op basal::fp8_block_linear_sm90
- * (fp8block.py:272-277). */
+ * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias; workspace as for basal200_fp8_block_gemm. Replaces
+ * fp8block.linear / BlockFormat.linear (basal/fp8block.py:285-296, basal/blockquant.py:175-183) and the op
+ * basal::fp8_block_linear_sm90 (fp8block.py:272-277). */
 int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,
                               void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
-                              void* stream);
+                              void* workspace, int64_t workspace_bytes, void* stream);
 
 /* int8block.linear (int8block.py:350 = BlockFormat.linear, basal/blockquant.py:175-183). */
 int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, const float* ws, const void* bias,
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
-                               void* stream);
+                               void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)

@@ -31,7 +31,8 @@ def test_every_declared_symbol_is_exported(lib):
 
 def test_binding_covers_the_header():
     from basal_b200 import _lib
-    bound = set(_lib.SIGNATURES) | {"basal200_status_string", "basal200_version", "basal200_device_faults"}
+    bound = set(_lib.SIGNATURES) | {"basal200_status_string", "basal200_version", "basal200_device_faults",
+                                    "basal200_block_gemm_workspace_bytes"}
     assert bound == set(declared())
 
 
@@ -51,9 +52,9 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_int8_act_quant(null, 0, -1, 128, null, null, null) == 1
     # M = 0 is an empty success
     assert lib.basal200_fp8_act_quant(null, 0, 0, 256, null, null, null) == 0
-    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 0, 256, 256, null) == 0
+    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 0, 256, 256, null, 0, null) == 0
     # N not a multiple of 128
-    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 4, 200, 256, null) == 2
+    assert lib.basal200_fp8_block_gemm(null, null, null, null, null, null, 0, 4, 200, 256, null, 0, null) == 2
     # NVFP4: K % 64
     assert lib.basal200_nvfp4_act_quant(null, 0, null, 4, 96, null, null, null) == 2
     # column-parallel GEMM with gathered outputs: no output buffer; a shard past the full width; fp32 output
@@ -64,6 +65,21 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 0, 0, 128, 256, null) == 0
     # readout: Kmax beyond 1024
     assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
+
+
+def test_split_workspace_sizes(lib):
+    """The few-rows GEMM asks for a workspace only where spreading its slices over the SMs pays: M <= 64, weights of
+    at most 64 tiles of 128 rows, at least 2 slices, products of at most 32 MiB (4 bytes per token, output, slice)."""
+    ws = lib.basal200_block_gemm_workspace_bytes
+    assert ws(16, 2048, 2048) == 16 * 2048 * 16 * 4
+    assert ws(64, 2048, 6144) == 64 * 2048 * 48 * 4
+    assert ws(1, 8192, 2048) == 8192 * 16 * 4
+    assert ws(1, 12288, 2048) == 0          # 96 tiles
+    assert ws(65, 2048, 2048) == 0          # the large-M kernel
+    assert ws(16, 8320, 2048) == 0          # 65 tiles
+    assert ws(16, 2048, 128) == 0           # one slice: nothing to spread
+    assert ws(64, 8192, 6144) == 0          # 96 MiB of products
+    assert ws(16, 200, 2048) == 0 and ws(0, 2048, 2048) == 0 and ws(16, 2048, 8320) == 0
 
 
 def test_header_is_plain_c():

@@ -80,6 +80,59 @@ def test_few_rows_kernel_equals_the_maths_and_the_large_kernel(b2, fmt, M):
     assert np.allclose(got, ref, rtol=TOL[fmt], atol=TOL[fmt]), np.abs(got - ref).max()
 
 
+def capi_gemm(fmt, qa, sa, q, s, dt, bias, work):
+    """The block GEMM through the C ABI, with the caller's workspace (a uint8 tensor) or none."""
+    from basal_b200 import _lib
+    M, K = qa.shape
+    N = q.shape[0]
+    c = torch.empty(M, N, dtype=dt, device=qa.device)
+    name = "basal200_int8_block_gemm" if fmt == "int8" else "basal200_fp8_block_gemm"
+    _lib.call(name, qa.device, _lib.ptr(qa), _lib.ptr(sa), _lib.ptr(q), _lib.ptr(s), _lib.ptr(bias), _lib.ptr(c),
+              _lib.code(dt), M, N, K, _lib.ptr(work), 0 if work is None else work.numel())
+    return c
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M, N, K", [(1, 2048, 2048), (16, 2048, 6144), (33, 1280, 2048), (64, 2048, 2048),
+                                     (16, 8192, 2048), (5, 640, 1152), (64, 256, 8192)])
+def test_split_few_rows_gemm_is_bit_identical_to_the_unsplit_kernel(b2, fmt, M, N, K):
+    """The few-rows GEMM spread over every SM (each slice's product into the workspace, then the slice-ordered sum in
+    a second kernel) gives the unsplit kernel's bits: fp32, bf16 and fp16 outputs, with and without bias, on two calls
+    in a row that share one workspace. The workspace starts as NaN bytes, so a product the sum reads without the call
+    having written it shows. Runs of units that cross weight tiles (N = 8192: 1024 units on the SMs) included."""
+    from basal_b200 import _lib
+    need = _lib.lib().basal200_block_gemm_workspace_bytes(M, N, K)
+    assert need == M * N * (K // 128) * 4
+    work = torch.full((need,), 0xFF, dtype=torch.uint8, device="cuda")
+    for seed in (1, 2):
+        x, q, s, qa, sa = operands(b2, fmt, M, N, K, seed=seed * 1000 + M)
+        for dt in (torch.float32, torch.bfloat16, torch.float16):
+            bias = None if dt == torch.float32 else torch.randn(N, generator=torch.Generator().manual_seed(seed)).to(
+                dt).cuda()
+            split = capi_gemm(fmt, qa, sa, q, s, dt, bias, work)
+            whole = capi_gemm(fmt, qa, sa, q, s, dt, bias, None)
+            assert torch.equal(split, whole), (dt, (split.float() - whole.float()).abs().max())
+        if seed == 1:  # within the maths' tolerance, fp32
+            ref = oracle_y(fmt, qa, sa, q, s)
+            got = capi_gemm(fmt, qa, sa, q, s, torch.float32, None, work).cpu().numpy()
+            assert np.allclose(got, ref, rtol=TOL[fmt], atol=TOL[fmt]), np.abs(got - ref).max()
+    assert b2._lib.device_faults(0) == 0
+
+
+def test_split_workspace_too_small_or_misaligned(b2):
+    """A workspace smaller than asked for runs the unsplit kernel (same bits); a misaligned one is refused."""
+    from basal_b200 import _lib
+    M, N, K = 16, 2048, 2048
+    x, q, s, qa, sa = operands(b2, "fp8", M, N, K, seed=9)
+    need = _lib.lib().basal200_block_gemm_workspace_bytes(M, N, K)
+    small = torch.empty(need - 16, dtype=torch.uint8, device="cuda")
+    assert torch.equal(capi_gemm("fp8", qa, sa, q, s, torch.bfloat16, None, small),
+                       capi_gemm("fp8", qa, sa, q, s, torch.bfloat16, None, None))
+    big = torch.empty(need + 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError, match="align"):
+        capi_gemm("fp8", qa, sa, q, s, torch.bfloat16, None, big[4:])
+
+
 @pytest.mark.parametrize("fmt", ["fp8", "int8"])
 @pytest.mark.parametrize("M", [517, 7])
 def test_bf16_linear_within_north_star_tolerance(b2, fmt, M):

@@ -41,7 +41,8 @@ def _allocating(lib, x, w, ws, bias, M, N, K):
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     q = torch.empty(M, K, dtype=torch.uint8, device="cuda")
     s = torch.empty(M, K // 128, dtype=torch.float32, device="cuda")
-    rc = lib.basal200_fp8_block_linear(_p(x), BF16, _p(w), _p(ws), _p(bias), _p(y), M, N, K, _p(q), _p(s), _stream())
+    rc = lib.basal200_fp8_block_linear(_p(x), BF16, _p(w), _p(ws), _p(bias), _p(y), M, N, K, _p(q), _p(s), None, 0,
+                                       _stream())
     assert rc == 0
     return y
 
