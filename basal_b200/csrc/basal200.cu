@@ -556,24 +556,36 @@ int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t
 // ------------------------------------------------------------------------------------------------------------
 // readout
 // ------------------------------------------------------------------------------------------------------------
+// code_logits: the warp-item kernel with CW codes an item (4, 8 or 16: the fewest that cover U, up to 16).
+template <typename TH, typename TW, typename TB>
+int logits_launch(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
+                  const int64_t* ids, int64_t U, const TB* bias, float softcap, float* z, cudaStream_t st) {
+  const int cw = U <= 4 ? 4 : (U <= 8 ? 8 : 16);
+  const int64_t items = (R + readout::PW - 1) / readout::PW * ((U + cw - 1) / cw);
+  const int64_t grid = (items + readout::IWARPS - 1) / readout::IWARPS;
+  if (grid > INT32_MAX) return BASAL200_ERR_LIMIT;
+  constexpr int threads = readout::IWARPS * 32;
+  if (cw == 4)
+    return launch_pdl(readout::code_logits_warp_kernel<TH, TW, TB, 4>, (unsigned)grid, threads, 0, st, h, R, D, ldh,
+                      head, V, ldw, ids, U, bias, softcap, z);
+  if (cw == 8)
+    return launch_pdl(readout::code_logits_warp_kernel<TH, TW, TB, 8>, (unsigned)grid, threads, 0, st, h, R, D, ldh,
+                      head, V, ldw, ids, U, bias, softcap, z);
+  return launch_pdl(readout::code_logits_warp_kernel<TH, TW, TB, 16>, (unsigned)grid, threads, 0, st, h, R, D, ldh,
+                    head, V, ldw, ids, U, bias, softcap, z);
+}
+
 template <typename TH, typename TW>
 int logits_typed(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
-                 const int64_t* ids,
-                 int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
-  const dim3 grid((unsigned)((U + readout::TU - 1) / readout::TU), (unsigned)((R + readout::TR - 1) / readout::TR));
-  constexpr int threads = readout::WARPS * 32;
+                 const int64_t* ids, int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
   if (!bias)
-    return launch_pdl(readout::code_logits_kernel<TH, TW, float>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
-                      ids, U, static_cast<const float*>(nullptr), softcap, z);
+    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(nullptr), softcap, z, st);
   if (bt == BASAL200_F32)
-    return launch_pdl(readout::code_logits_kernel<TH, TW, float>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
-                      ids, U, static_cast<const float*>(bias), softcap, z);
+    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(bias), softcap, z, st);
   if (bt == BASAL200_BF16)
-    return launch_pdl(readout::code_logits_kernel<TH, TW, __nv_bfloat16>, grid, threads, 0, st, h, R, D, ldh, head, V,
-                      ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z);
+    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z, st);
   if (bt == BASAL200_F16)
-    return launch_pdl(readout::code_logits_kernel<TH, TW, __half>, grid, threads, 0, st, h, R, D, ldh, head, V, ldw,
-                      ids, U, static_cast<const __half*>(bias), softcap, z);
+    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z, st);
   return BASAL200_ERR_DTYPE;
 }
 
@@ -767,8 +779,7 @@ int basal200_code_logits(const void* h, int h_dtype, int64_t R, int64_t D, int64
   if (R < 0 || U < 0 || V <= 0 || D <= 0 || ldh < D || ldw < D) return BASAL200_ERR_ARG;
   if (R == 0 || U == 0) return BASAL200_OK;
   if (!h || !head || !ids || !z) return BASAL200_ERR_ARG;
-  if ((U + readout::TU - 1) / readout::TU > INT32_MAX || (R + readout::TR - 1) / readout::TR > 65535)
-    return BASAL200_ERR_LIMIT;
+  if (R > INT32_MAX || U > INT32_MAX) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   cudaStream_t st = as_stream(stream);
@@ -795,8 +806,13 @@ int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx
   if (!z || !idx || !p) return BASAL200_ERR_ARG;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
-  return launch_pdl(readout::code_probs_kernel, (unsigned)((R + 7) / 8), 256, 0, as_stream(stream), z, R, U, idx, pad,
-                    Kmax, p);
+  const unsigned grid = (unsigned)((R + 7) / 8);
+  cudaStream_t st = as_stream(stream);
+  if (Kmax <= 32) return launch_pdl(readout::code_probs_kernel<1>, grid, 256, 0, st, z, R, U, idx, pad, Kmax, p);
+  if (Kmax <= 64) return launch_pdl(readout::code_probs_kernel<2>, grid, 256, 0, st, z, R, U, idx, pad, Kmax, p);
+  if (Kmax <= 128) return launch_pdl(readout::code_probs_kernel<4>, grid, 256, 0, st, z, R, U, idx, pad, Kmax, p);
+  if (Kmax <= 256) return launch_pdl(readout::code_probs_kernel<8>, grid, 256, 0, st, z, R, U, idx, pad, Kmax, p);
+  return launch_pdl(readout::code_probs_kernel<32>, grid, 256, 0, st, z, R, U, idx, pad, Kmax, p);
 }
 
 unsigned basal200_device_faults(int device, int clear) {

@@ -270,7 +270,7 @@ def code_probs(z: Tensor, idx: Tensor, pad: Tensor) -> Tensor:
     """Code logits z [R, U] -> each prompt's probabilities over its codes [R, Kmax] (padding 0)."""
     require_cuda(z, idx, pad)
     z, idx = _c(z.float()), _c(idx.to(torch.int64))
-    pad = _c(pad.to(torch.uint8))
+    pad = _c(pad).view(torch.uint8) if pad.dtype == torch.bool else _c(pad.to(torch.uint8))  # bool: 0 / 1 bytes
     R, U = z.shape
     Kmax = idx.shape[1]
     p = torch.empty((R, Kmax), dtype=torch.float32, device=z.device)

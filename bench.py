@@ -341,6 +341,7 @@ CASES = {
     "fp8_act_quant": ("fp8", 65536, 0, 2048),
     "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
     "nvfp4_act_quant": ("nvfp4", 8192, 0, 6144),
+    "readout": ("readout", 256, 255, 2048),  # C4's readout: R prompts, k option ids (N), D features (K)
 }
 
 
@@ -352,7 +353,15 @@ def run_case(name):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(M, K, device=dev, generator=g).bfloat16()
-    if N == 0 and fmt == "nvfp4":
+    if fmt == "readout":
+        head = torch.nn.Linear(K, 151936, bias=False, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            head.weight.normal_(0.0, 0.02, generator=g)
+        ro = b2.readout.CodeReadout(head)
+        rows, idx, pad = ro.rows([torch.randperm(151936, device=dev, generator=g)[:N].tolist()] * M)
+        for _ in range(5):
+            ro.probs_of(ro.logits(x, rows), idx, pad)
+    elif N == 0 and fmt == "nvfp4":
         inv_g = torch.tensor([0.5], device=dev)
         for _ in range(5):
             b2.nvfp4.act_quant(x, inv_g)

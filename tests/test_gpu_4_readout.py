@@ -76,3 +76,30 @@ def test_batch_invariance(b2, c4_head):
     assert batch == r.probs_each(hh, lids)
     for i in (0, 5, 63):
         assert r.probs(hh[i:i + 1], [lids[i]])[0] == batch[i]
+
+
+@pytest.mark.parametrize("D, hdt", [(2560, torch.bfloat16), (1000, torch.float32), (300, torch.bfloat16)])
+def test_code_tile_widths_agree_bit_for_bit(b2, D, hdt):
+    """One code's logit is the same bits whether it is read among 3, 7 or 37 codes (items of 4, 8 or 16 codes a
+    warp), at any position among them, for whole 256-feature chunks (D = 2560), a ragged tail (D = 1000, fp32 h) and a
+    row stride off the 16-byte boundary (D = 300 bf16 in a 301-wide buffer: every feature on the lane-strided path);
+    each within 1e-5 of the oracle's fp32 logits, with a bf16 bias and the Gemma soft cap."""
+    g = torch.Generator().manual_seed(D)
+    V = 5000
+    w = (torch.randn(V, D, generator=g) * 0.02).bfloat16()
+    bias = (torch.randn(V, generator=g) * 0.1).bfloat16()
+    hbuf = torch.randn(19, D + (1 if D == 300 else 0), generator=g).to(hdt)
+    h = hbuf[:, :D]
+    pool = torch.randperm(V, generator=g)[:37].tolist()
+    target = pool[2]
+    head = Head(w.cuda(), bias.cuda())
+    zs = []
+    for ids in (pool[:3], [pool[5], pool[6], target, pool[8], pool[9], pool[10], pool[11]], pool):
+        ids_t = torch.tensor(ids, dtype=torch.int64).cuda()
+        z = b2.ops.code_logits(h.cuda(), head.weight, ids_t, head.bias, 30.0)
+        zs.append(z[:, ids.index(target)].cpu())
+    assert torch.equal(zs[0], zs[1]) and torch.equal(zs[1], zs[2])
+    ref = oro.logits(h.float().numpy(), (w[pool].float().numpy(), bias[pool].float().numpy()), 30.0)
+    got = b2.ops.code_logits(h.cuda(), head.weight, torch.tensor(pool).cuda(), head.bias, 30.0).cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-5
+    assert b2._lib.device_faults(0) == 0
