@@ -3,6 +3,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "block_gemm.cuh"
@@ -19,7 +20,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int checked = 0;  // 1: sm_100, -1: another architecture
   int sms = 0;
-  unsigned smem_set = 0;  // kernels whose dynamic shared memory limit was raised on this device
+  uint64_t smem_set = 0;  // kernels whose dynamic shared memory limit was raised on this device
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -37,17 +38,17 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26 };  // kSlotFp4 .. + 5, kSlotSmall .. + 11,
-                                                                     // kSlotSplit .. + 3
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30 };
+// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7 (bits 30-37 of a 64-bit mask)
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
 int set_smem(int dev, int slot, K kernel, size_t bytes) {
   DeviceInfo& d = g_dev[dev];
-  if (d.smem_set & (1u << slot)) return BASAL200_OK;
+  if (d.smem_set & (1ull << slot)) return BASAL200_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
     return BASAL200_ERR_LAUNCH;
-  d.smem_set |= 1u << slot;
+  d.smem_set |= 1ull << slot;
   return BASAL200_OK;
 }
 
@@ -282,7 +283,7 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
                       const blockgemm::Params& p, cudaStream_t st) {
   auto kern = blockgemm::block_gemm_kernel<INT8, OUT>;
   const int slot = kSlotBlock + (INT8 ? 3 : 0) + OUT;
-  if (!(g_dev[dev].smem_set & (1u << slot))) {
+  if (!(g_dev[dev].smem_set & (1ull << slot))) {
     const int rc = check_launch_regs(kern, (int)blockgemm::LAUNCH_REGS);
     if (rc) return rc;
   }
@@ -341,25 +342,35 @@ int64_t split_workspace(int64_t M, int64_t N, int64_t K) {
   return bytes <= kSplitMaxBytes ? bytes : 0;
 }
 
-template <bool INT8, int OUT, int NT>
+// TX = void: q holds the activation codes (TMA-loaded). TX = __nv_bfloat16 / __half: the fused linear, q is the
+// activations themselves, quantised inside the products kernel, and their scales are written to s.
+template <bool INT8, int OUT, int NT, typename TX>
 int split_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
                       void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
                       void* work, cudaStream_t st) {
-  auto kp = smallgemm::split_products_kernel<INT8, NT>;
+  constexpr bool QUANT = !std::is_void<TX>::value;
+  auto kp = smallgemm::split_products_kernel<INT8, NT, TX>;
   constexpr size_t smem = smallgemm::split_smem_bytes<NT>();
-  const int slot = kSlotSplit + (INT8 ? 2 : 0) + (NT == 32 ? 0 : 1);
+  const int slot = (QUANT ? kSlotSplitQ + (std::is_same<TX, __half>::value ? 4 : 0) : kSlotSplit) + (INT8 ? 2 : 0) +
+                   (NT == 32 ? 0 : 1);
   int rc = set_smem(dev, slot, kp, smem);
   if (rc) return rc;
   CUtensorMap tw, tt;
   if ((rc = tmap_u8(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, smallgemm::BK, smallgemm::BW))) return rc;
-  if ((rc = tmap_u8(&tt, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, smallgemm::BK, NT))) return rc;
+  if (QUANT)
+    tt = tw;  // unused: the tokens are quantised in the kernel
+  else if ((rc = tmap_u8(&tt, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, smallgemm::BK, NT)))
+    return rc;
   smallgemm::SplitParams sp;
   sp.prod = static_cast<float*>(work);
   sp.M = (int)M;
   sp.nkb = (int)(K / 128);
   sp.units = N / smallgemm::BW * sp.nkb;
+  sp.x = QUANT ? q : nullptr;
+  sp.s = QUANT ? const_cast<float*>(s) : nullptr;
   const int64_t grid = sp.units < g_dev[dev].sms ? sp.units : g_dev[dev].sms;
-  if ((rc = launch_pdl(kp, (unsigned)grid, smallgemm::SplitCfg<NT>::THREADS, smem, st, tw, tt, sp))) return rc;
+  const int threads = smallgemm::SplitCfg<NT>::THREADS + (QUANT ? smallgemm::SplitCfg<NT>::QUANT_WARPS * 32 : 0);
+  if ((rc = launch_pdl(kp, (unsigned)grid, threads, smem, st, tw, tt, sp))) return rc;
   smallgemm::Params p;
   p.s = s;
   p.ws = ws;
@@ -376,12 +387,32 @@ int split_gemm_launch(int dev, const void* q, const float* s, const void* w, con
                     static_cast<const float*>(work), p);
 }
 
-template <bool INT8, int OUT>
+template <bool INT8, int OUT, typename TX = void>
 int split_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias, void* c,
                int64_t M, int64_t N, int64_t K, void* work, cudaStream_t st) {
   void* const cs[1] = {c};
-  if (M <= 32) return split_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
-  return split_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
+  if (M <= 32) return split_gemm_launch<INT8, OUT, 32, TX>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
+  return split_gemm_launch<INT8, OUT, 64, TX>(dev, q, s, w, ws, bias, cs, 1, N, 0, M, N, K, work, st);
+}
+
+// The few-rows linear with the activation quantiser fused into the split GEMM (16-bit x, output in x's type): one
+// launch fewer than act_quant + GEMM, the same codes, scales and output bits. Returns -1 when it does not apply.
+template <bool INT8>
+int fused_split_linear(const void* x, int xt, const void* w, const float* ws, const void* bias, void* y,
+                       int64_t M, int64_t N, int64_t K, float* s_scratch, void* work, int64_t work_bytes,
+                       cudaStream_t st) {
+  if (xt != BASAL200_BF16 && xt != BASAL200_F16) return -1;
+  if (M < 1 || K <= 0 || K % 128 || N % 128) return -1;
+  const int64_t split = split_workspace(M, N, K);
+  if (split <= 0 || !work || work_bytes < split) return -1;
+  if (!x || !w || !ws || !y || !s_scratch) return BASAL200_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || !aligned16(work) || (bias && !aligned16(bias)))
+    return BASAL200_ERR_ALIGN;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  if (xt == BASAL200_BF16)
+    return split_gemm<INT8, BASAL200_BF16, __nv_bfloat16>(dev, x, s_scratch, w, ws, bias, y, M, N, K, work, st);
+  return split_gemm<INT8, BASAL200_F16, __half>(dev, x, s_scratch, w, ws, bias, y, M, N, K, work, st);
 }
 
 // work / work_bytes: the caller's workspace (may be null); when it holds split_workspace(M, N, K) > 0 bytes, the
@@ -702,7 +733,10 @@ int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, cons
                               void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
                               void* workspace, int64_t workspace_bytes, void* stream) {
   if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
-  int rc = act_quant<false>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
+  int rc = fused_split_linear<false>(x, x_dtype, w, ws, bias, y, M, N, K, s_scratch, workspace, workspace_bytes,
+                                      as_stream(stream));
+  if (rc >= 0) return rc;
+  rc = act_quant<false>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
   if (rc) return rc;
   return block_gemm<false>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, workspace, workspace_bytes,
                            as_stream(stream));
@@ -712,7 +746,10 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                void* workspace, int64_t workspace_bytes, void* stream) {
   if (M > 0 && (N % 128)) return BASAL200_ERR_SHAPE;
-  int rc = act_quant<true>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
+  int rc = fused_split_linear<true>(x, x_dtype, w, ws, bias, y, M, N, K, s_scratch, workspace, workspace_bytes,
+                                      as_stream(stream));
+  if (rc >= 0) return rc;
+  rc = act_quant<true>(x, x_dtype, M, K, q_scratch, s_scratch, as_stream(stream));
   if (rc) return rc;
   return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, workspace, workspace_bytes,
                           as_stream(stream));

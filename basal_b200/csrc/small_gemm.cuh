@@ -27,6 +27,8 @@
 //     for NT = 32, 8 for NT = 64), thread = weight row; at the end the cast (and bias) and the stores, each token's 128
 //     outputs consecutive.
 #pragma once
+#include <type_traits>
+
 #include "block_gemm.cuh"
 
 namespace b200 {
@@ -308,6 +310,8 @@ struct SplitCfg {
   static_assert(TSLOTS * NT <= 512, "TMEM columns");
   static constexpr int EPI_WARPS = NT / 32 * 4;
   static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+  static constexpr int QUANT_WARPS = NT == 32 ? 8 : 4;  // the fused linear's activation quantisers, after the readout
+                                                        // warps (as many as the registers of the launch allow)
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
@@ -333,31 +337,45 @@ struct SplitParams {
   float* prod;    // [N/128][nkb][M][128] fp32: unit (tile, kb)'s product of token j and weight row r
   int64_t units;  // (N / 128) * nkb
   int M, nkb;
+  const void* x;  // fused linear only: the activations [M, nkb * 128] (16-bit), quantised here instead of loaded as
+  float* s;       // codes; their scales [M, nkb] are written to s for the second kernel
 };
 
 // Workspace bytes of the split kernels for M tokens, N outputs and nkb slices.
 __host__ __device__ constexpr int64_t split_prod_bytes(int64_t M, int64_t N, int64_t nkb) { return M * N * nkb * 4; }
 
-template <bool INT8, int NT>
-__global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
+// TX = void: the token codes of a unit come by TMA (tmT). TX = bf16 / f16: the fused linear; QUANT_WARPS more warps
+// quantise each unit's 128-wide slice of the activations (one half-warp a token: 16-byte loads of the next unit issued
+// before this unit's arithmetic, amax by shuffles, blockquant's codes by block_codes8, exactly as act_quant_block_kernel)
+// and write the codes into the stage where the TMA would have put them, in the same 128-byte swizzle.
+template <bool INT8, int NT, typename TX>
+__global__ void __launch_bounds__(SplitCfg<NT>::THREADS + (std::is_void<TX>::value ? 0 : SplitCfg<NT>::QUANT_WARPS * 32),
+                                  1)
     split_products_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
                           const SplitParams p) {
   using S = SplitSmem<NT>;
   using C = SplitCfg<NT>;
+  constexpr bool QUANT = !std::is_void<TX>::value;
   constexpr int STAGES = C::STAGES;
   constexpr int TSLOTS = C::TSLOTS;
+  constexpr uint32_t LOAD_BYTES = QUANT ? W_BYTES : C::STAGE_BYTES;  // TMA bytes a stage
   extern __shared__ uint8_t smem_raw[];
   S& sh = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = warp_id();
   const int lane = lane_id();
   const int nkb = p.nkb;
-  // this CTA's run of units [u0, u0 + nu): unit u is slice u % nkb of weight tile u / nkb
+  const int tiles = (int)(p.units / nkb);
+  // this CTA's run of units [u0, u0 + nu). TMA tokens: unit u is slice u % nkb of weight tile u / nkb (a run walks
+  // along K). Fused quantiser: slice u / tiles of tile u % tiles (a run walks across tiles at one or two slices, so
+  // each slice is quantised once a CTA, not once a unit).
   const int64_t u0 = (int64_t)blockIdx.x * p.units / gridDim.x;
   const int nu = (int)((int64_t)(blockIdx.x + 1) * p.units / gridDim.x - u0);
+  auto unit_kb = [&](int64_t u) { return QUANT ? (int)(u / tiles) : (int)(u % nkb); };
+  auto unit_tile = [&](int64_t u) { return QUANT ? (int)(u % tiles) : (int)(u / nkb); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.full[s], QUANT ? 1 + C::QUANT_WARPS : 1);
       mbar_init(&sh.empty[s], 1);
     }
     for (int t = 0; t < TSLOTS; ++t) {
@@ -367,6 +385,13 @@ __global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
     mbar_init(&sh.mdrain, MMA_WARPS);
     sh.abort = 0;
     fence_barrier_init();
+  }
+  if (QUANT) {  // token rows past M stay zero in every stage (the quantisers write rows < M only)
+    for (int i = threadIdx.x; i < STAGES * NT * BK / 16; i += blockDim.x) {
+      const int st = i / (NT * BK / 16), o = i - st * (NT * BK / 16);
+      reinterpret_cast<uint4*>(sh.stage[st] + W_BYTES)[o] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async();  // visible to the tensor cores' reads
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
@@ -389,21 +414,23 @@ __global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
       const int pre = nu < STAGES ? nu : STAGES;
       for (int j = 0; j < pre; ++j) {
         const int64_t u = u0 + j;
-        mbar_arrive_expect_tx(&sh.full[j], C::STAGE_BYTES);
-        tma_load_2d(sh.stage[j], &tmW, &sh.full[j], (int)(u % nkb) * BK, (int)(u / nkb) * BW);
+        mbar_arrive_expect_tx(&sh.full[j], LOAD_BYTES);
+        tma_load_2d(sh.stage[j], &tmW, &sh.full[j], unit_kb(u) * BK, unit_tile(u) * BW);
         filled |= 1u << j;
       }
-      pdl_wait();
-      for (int j = 0; j < pre; ++j)
-        tma_load_2d(sh.stage[j] + W_BYTES, &tmT, &sh.full[j], (int)((u0 + j) % nkb) * BK, 0);
+      if (!QUANT) {
+        pdl_wait();
+        for (int j = 0; j < pre; ++j)
+          tma_load_2d(sh.stage[j] + W_BYTES, &tmT, &sh.full[j], unit_kb(u0 + j) * BK, 0);
+      }
       for (int j = pre; j < nu; ++j) {
         const int stage = j % STAGES;
         const uint32_t phase = (uint32_t)(j / STAGES) & 1;
         if (!mbar_wait(&sh.empty[stage], phase ^ 1, abort_flag, kFaultTimeoutProducer)) break;
         const int64_t u = u0 + j;
-        mbar_arrive_expect_tx(&sh.full[stage], C::STAGE_BYTES);
-        tma_load_2d(sh.stage[stage], &tmW, &sh.full[stage], (int)(u % nkb) * BK, (int)(u / nkb) * BW);
-        tma_load_2d(sh.stage[stage] + W_BYTES, &tmT, &sh.full[stage], (int)(u % nkb) * BK, 0);
+        mbar_arrive_expect_tx(&sh.full[stage], LOAD_BYTES);
+        tma_load_2d(sh.stage[stage], &tmW, &sh.full[stage], unit_kb(u) * BK, unit_tile(u) * BW);
+        if (!QUANT) tma_load_2d(sh.stage[stage] + W_BYTES, &tmT, &sh.full[stage], unit_kb(u) * BK, 0);
         filled |= 1u << stage;
         last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
       }
@@ -440,6 +467,71 @@ __global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
       mma_commit(&sh.mdrain);
       blockgemm::drain_wait(&sh.mdrain, 0);
     }
+  } else if (QUANT && warp >= EPI_WARP0 + C::EPI_WARPS) {
+    // ------- activation quantisers (fused linear): token t = pass * 2 * QUANT_WARPS + qw * 2 + half -------
+    if constexpr (QUANT) {
+      constexpr int TPP = 2 * C::QUANT_WARPS;  // tokens a pass (a half-warp each)
+      constexpr int PASSES = NT / TPP;
+      constexpr int W = sizeof(TX) / 2;  // 16-byte words of a lane's 8 values (one: 16-bit activations)
+      static_assert(W == 1, "the fused quantiser takes 16-bit activations");
+      constexpr float kQmax = INT8 ? 127.0f : 448.0f;
+      const int qw = warp - EPI_WARP0 - C::EPI_WARPS;
+      const int hf = lane >> 4, l16 = lane & 15;
+      const TX* x = static_cast<const TX*>(p.x);
+      const int64_t ldx = (int64_t)nkb * BK;
+      uint4 raw[PASSES][1];  // the activations of the next slice to quantise, loaded ahead
+      uint2 codes[PASSES];   // the codes of slice kb_cur
+      auto load_slice = [&](int kb) {
+#pragma unroll
+        for (int ps = 0; ps < PASSES; ++ps) {
+          const int t = ps * TPP + qw * 2 + hf;
+          if (t < p.M)
+            raw_load8(x + t * ldx + kb * BK + l16 * 8, raw[ps]);
+          else
+            raw[ps][0] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      const int kb_last = nu > 0 ? unit_kb(u0 + nu - 1) : 0;
+      int kb_cur = -1;
+      pdl_wait();  // the activations are an earlier kernel's output; the scales go where it may still read
+      if (nu > 0) load_slice(unit_kb(u0));
+      for (int j = 0; j < nu; ++j) {
+        const int kb = unit_kb(u0 + j);
+        if (kb != kb_cur) {  // a new slice: quantise the loaded activations, then load the next slice's
+#pragma unroll
+          for (int ps = 0; ps < PASSES; ++ps) {
+            if (ps * TPP >= p.M) break;  // no token of this pass is real (the same for every lane)
+            const int t = ps * TPP + qw * 2 + hf;
+            float v[8];
+            unpack8(raw[ps], x, v);
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+            for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
+            codes[ps] = block_codes8<INT8>(v, sc);
+            if (t < p.M && l16 == 0) p.s[(int64_t)t * nkb + kb] = sc;  // every CTA with slice kb: the same value
+          }
+          kb_cur = kb;
+          if (kb + 1 <= kb_last) load_slice(kb + 1);
+        }
+        const int stage = j % STAGES;
+        if (j >= STAGES &&
+            !blockgemm::warp_wait(&sh.empty[stage], ((uint32_t)(j / STAGES) & 1) ^ 1, abort_flag,
+                                  kFaultTimeoutProducer))
+          break;
+        uint8_t* tok = sh.stage[stage] + W_BYTES;
+#pragma unroll
+        for (int ps = 0; ps < PASSES; ++ps) {
+          const int t = ps * TPP + qw * 2 + hf;
+          if (t < p.M) *reinterpret_cast<uint2*>(tok + blockgemm::sw128(t, l16 >> 1) + (l16 & 1) * 8) = codes[ps];
+        }
+        fence_proxy_async();  // the codes, visible to the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.full[stage]);
+      }
+    }
   } else {
     // ---------------- product readout: thread = weight row, 32 tokens a warp ----------------
     const int ew = warp - EPI_WARP0;
@@ -460,7 +552,8 @@ __global__ void __launch_bounds__(SplitCfg<NT>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tempty[slot]);
-      float* dst = p.prod + ((u0 + j) * p.M + half * 32) * BW + t;  // unit u0 + j = tile * nkb + kb
+      const int64_t u = u0 + j;
+      float* dst = p.prod + (((int64_t)unit_tile(u) * nkb + unit_kb(u)) * p.M + half * 32) * BW + t;
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         if (jj < ntok) __stcg(dst + (int64_t)jj * BW, INT8 ? __int2float_rn((int)x[jj]) : __uint_as_float(x[jj]));

@@ -87,7 +87,9 @@ int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, c
                              int64_t workspace_bytes, void* stream);
 
 /* The whole linear: act_quant of x into the caller's scratch (q_scratch [M, K] bytes, s_scratch [M, K/128] fp32),
- * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias; workspace as for basal200_fp8_block_gemm. Replaces
+ * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias; workspace as for basal200_fp8_block_gemm. When the
+ * workspace makes the GEMM split and x is bf16 or fp16, the quantiser runs inside the GEMM kernel instead (one launch
+ * fewer; q_scratch is then not written, s_scratch is, and every bit of y and s_scratch is the same). Replaces
  * fp8block.linear / BlockFormat.linear (basal/fp8block.py:285-296, basal/blockquant.py:175-183) and the op
  * basal::fp8_block_linear_sm90 (fp8block.py:272-277). */
 int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,

@@ -119,6 +119,51 @@ def test_split_few_rows_gemm_is_bit_identical_to_the_unsplit_kernel(b2, fmt, M, 
     assert b2._lib.device_faults(0) == 0
 
 
+def capi_linear(fmt, x, q, s, bias, work):
+    """The block linear through the C ABI (output in x's type); returns the output and the activation scales."""
+    from basal_b200 import _lib
+    M, K = x.shape
+    N = q.shape[0]
+    y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    qs = torch.empty(M, K, dtype=torch.uint8, device=x.device)
+    ss = torch.full((M, K // 128), float("nan"), dtype=torch.float32, device=x.device)
+    name = "basal200_int8_block_linear" if fmt == "int8" else "basal200_fp8_block_linear"
+    _lib.call(name, x.device, _lib.ptr(x), _lib.code(x.dtype), _lib.ptr(q), _lib.ptr(s), _lib.ptr(bias), _lib.ptr(y),
+              M, N, K, _lib.ptr(qs), _lib.ptr(ss), _lib.ptr(work), 0 if work is None else work.numel())
+    return y, ss
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M, N, K", [(1, 2048, 2048), (16, 2048, 6144), (33, 1280, 2048), (64, 2048, 2048),
+                                     (7, 8192, 1152)])
+def test_fused_quantiser_linear_is_bit_identical(b2, fmt, M, N, K):
+    """A few-rows linear whose activation quantiser runs inside the split GEMM (16-bit x: codes written straight into
+    the GEMM's operand stages, scales into the scratch) gives the bits of the quantiser kernel + unsplit GEMM: the same
+    output and the same scales, bf16 and fp16 activations, with and without bias, on two calls in a row sharing a
+    workspace. Activations include an all-zero token, a tiny one and an outlier."""
+    from basal_b200 import _lib
+    need = _lib.lib().basal200_block_gemm_workspace_bytes(M, N, K)
+    assert need > 0
+    work = torch.full((need,), 0xFF, dtype=torch.uint8, device="cuda")
+    g = torch.Generator().manual_seed(M * 7 + K)
+    w = (torch.randn(N, K, generator=g) * 0.02).cuda()
+    q, s = mod(b2, fmt).quantize(w)
+    for seed in (1, 2):
+        x = torch.randn(M, K, generator=g) * (1 + seed)
+        x[0, :128] = 0.0
+        if M > 2:
+            x[1] *= 1e-30
+            x[2, 5] = 3e4
+        for dt in (torch.bfloat16, torch.float16):
+            xd = x.to(dt).cuda()
+            bias = None if seed == 1 else torch.randn(N, generator=g).to(dt).cuda()
+            fused, s_f = capi_linear(fmt, xd, q, s, bias, work)
+            plain, s_p = capi_linear(fmt, xd, q, s, bias, None)
+            assert torch.equal(s_f, s_p), (dt, seed)
+            assert torch.equal(fused, plain), (dt, seed, (fused.float() - plain.float()).abs().max())
+    assert b2._lib.device_faults(0) == 0
+
+
 def test_split_workspace_too_small_or_misaligned(b2):
     """A workspace smaller than asked for runs the unsplit kernel (same bits); a misaligned one is refused."""
     from basal_b200 import _lib
