@@ -38,8 +38,9 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30 };
-// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7 (bits 30-37 of a 64-bit mask)
+enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38 };
+// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11 (bits of a 64-bit
+// mask)
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -588,9 +589,30 @@ int fp4_gemm(const uint8_t* q, const uint8_t* s, const uint8_t* w, const uint8_t
 // readout
 // ------------------------------------------------------------------------------------------------------------
 // code_logits: the warp-item kernel with CW codes an item (4, 8 or 16: the fewest that cover U, up to 16).
+template <typename T>
+constexpr int type_index() {
+  return std::is_same<T, float>::value ? 0 : (std::is_same<T, __nv_bfloat16>::value ? 1 : 2);
+}
+
 template <typename TH, typename TW, typename TB>
-int logits_launch(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
+int logits_launch(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
                   const int64_t* ids, int64_t U, const TB* bias, float softcap, float* z, cudaStream_t st) {
+  if constexpr (sizeof(TH) == 2 && sizeof(TW) == 2) {
+    // many codes, whole 256-feature chunks, 16-byte aligned rows: the staged kernel (the same bits)
+    if (U > 8 && D % readout::CHUNK == 0 && aligned16(h) && aligned16(head) && (ldh * 2) % 16 == 0 &&
+        (ldw * 2) % 16 == 0) {
+      auto kern = readout::code_logits_staged_kernel<TH, TW, TB>;
+      constexpr size_t smem = sizeof(readout::StagedSmem<TH, TW>);
+      const int slot = kSlotLogits + (type_index<TH>() - 1) * 6 + (type_index<TW>() - 1) * 3 + type_index<TB>();
+      int rc = set_smem(dev, slot, kern, smem);
+      if (rc) return rc;
+      const int64_t gy = (R + readout::SR - 1) / readout::SR;
+      if (gy > 65535) return BASAL200_ERR_LIMIT;
+      const dim3 grid((unsigned)((U + readout::SU - 1) / readout::SU), (unsigned)gy);
+      return launch_pdl(kern, grid, readout::SWARPS * 32, smem, st, h, R, D, ldh, head, V, ldw, ids, U, bias, softcap,
+                        z);
+    }
+  }
   const int cw = U <= 4 ? 4 : (U <= 8 ? 8 : 16);
   const int64_t items = (R + readout::PW - 1) / readout::PW * ((U + cw - 1) / cw);
   const int64_t grid = (items + readout::IWARPS - 1) / readout::IWARPS;
@@ -607,30 +629,31 @@ int logits_launch(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head
 }
 
 template <typename TH, typename TW>
-int logits_typed(const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
+int logits_typed(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
                  const int64_t* ids, int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
   if (!bias)
-    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(nullptr), softcap, z, st);
+    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(nullptr), softcap, z, st);
   if (bt == BASAL200_F32)
-    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(bias), softcap, z, st);
+    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(bias), softcap, z, st);
   if (bt == BASAL200_BF16)
-    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z, st);
+    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z, st);
   if (bt == BASAL200_F16)
-    return logits_launch(h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z, st);
+    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z, st);
   return BASAL200_ERR_DTYPE;
 }
 
 template <typename TH>
-int logits_head(const TH* h, int64_t R, int64_t D, int64_t ldh, const void* head, int ht, int64_t V, int64_t ldw,
-                const int64_t* ids, int64_t U, const void* bias, int bt, float softcap, float* z, cudaStream_t st) {
+int logits_head(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const void* head, int ht, int64_t V,
+                int64_t ldw, const int64_t* ids, int64_t U, const void* bias, int bt, float softcap, float* z,
+                cudaStream_t st) {
   switch (ht) {
     case BASAL200_BF16:
-      return logits_typed(h, R, D, ldh, static_cast<const __nv_bfloat16*>(head), V, ldw, ids, U, bias, bt, softcap,
+      return logits_typed(dev, h, R, D, ldh, static_cast<const __nv_bfloat16*>(head), V, ldw, ids, U, bias, bt, softcap,
                           z, st);
     case BASAL200_F16:
-      return logits_typed(h, R, D, ldh, static_cast<const __half*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
+      return logits_typed(dev, h, R, D, ldh, static_cast<const __half*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
     case BASAL200_F32:
-      return logits_typed(h, R, D, ldh, static_cast<const float*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
+      return logits_typed(dev, h, R, D, ldh, static_cast<const float*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
     default:
       return BASAL200_ERR_DTYPE;
   }
@@ -822,13 +845,13 @@ int basal200_code_logits(const void* h, int h_dtype, int64_t R, int64_t D, int64
   cudaStream_t st = as_stream(stream);
   switch (h_dtype) {
     case BASAL200_BF16:
-      return logits_head(static_cast<const __nv_bfloat16*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+      return logits_head(dev, static_cast<const __nv_bfloat16*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
                          bias_dtype, softcap, z, st);
     case BASAL200_F16:
-      return logits_head(static_cast<const __half*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+      return logits_head(dev, static_cast<const __half*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
                          bias_dtype, softcap, z, st);
     case BASAL200_F32:
-      return logits_head(static_cast<const float*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
+      return logits_head(dev, static_cast<const float*>(h), R, D, ldh, head, head_dtype, V, ldw, ids, U, bias,
                          bias_dtype, softcap, z, st);
     default:
       return BASAL200_ERR_DTYPE;

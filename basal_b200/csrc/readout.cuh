@@ -97,9 +97,9 @@ __global__ void __launch_bounds__(IWARPS * 32) code_logits_warp_kernel(
     for (int j = 0; j < CW; ++j) {
       load8(head + woff[j] + d, b);
 #pragma unroll
-      for (int i = 0; i < PW; ++i)
+      for (int e = 0; e < 8; ++e)  // consecutive FMAs on the PW prompts' accumulators: independent, no stall
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[i * CW + j] = fmaf(a[i][e], b[e], acc[i * CW + j]);
+        for (int i = 0; i < PW; ++i) acc[i * CW + j] = fmaf(a[i][e], b[e], acc[i * CW + j]);
     }
   }
   for (int64_t d = dv + lane; d < D; d += 32) {
@@ -134,6 +134,127 @@ __global__ void __launch_bounds__(IWARPS * 32) code_logits_warp_kernel(
         if (softcap > 0.0f) v = __fmul_rn(tanhf(__fdiv_rn(v, softcap)), softcap);
         z[r * U + u] = v;
       }
+    }
+  }
+}
+
+// code_logits for 16-bit h and head with D a multiple of 256 and many codes (U > 8): a CTA of 8 warps takes 32 prompts x
+// 16 codes, warp w the prompts 4w .. 4w + 3 of it. The CTA's 48 rows are staged in shared memory by bulk copies,
+// 1024 features at a time in two buffers (one warp issues a row a lane), so every byte a chunk needs is requested at
+// once instead of in 8 dependent rounds of register loads. A lane then walks exactly the features it walks in
+// code_logits_warp_kernel (l * 8 .. l * 8 + 7 of every 256-feature chunk, in increasing order) and the partials meet
+// in the same halving reduction, so every z[r, u] is the same bits whichever of the two kernels computes it.
+constexpr int SR = 32;      // prompts a staged CTA
+constexpr int SU = 16;      // codes a staged CTA
+constexpr int SDC = 1024;   // features a staged chunk
+constexpr int SWARPS = SR / PW;
+
+template <typename TH, typename TW>
+struct StagedSmem {
+  TW w[2][SU][SDC];
+  TH h[2][SR][SDC];
+  uint64_t full[2];
+  int abort;
+};
+
+template <typename TH, typename TW, typename TB>
+__global__ void __launch_bounds__(SWARPS * 32) code_logits_staged_kernel(
+    const TH* __restrict__ h, int64_t R, int64_t D, int64_t ldh, const TW* __restrict__ head, int64_t V, int64_t ldw,
+    const int64_t* __restrict__ ids, int64_t U, const TB* __restrict__ bias, float softcap, float* __restrict__ z) {
+  static_assert(sizeof(TH) == 2 && sizeof(TW) == 2, "16-bit rows");
+  constexpr int NV = PW * SU;  // 64 values a warp
+  using S = StagedSmem<TH, TW>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  S& sh = *reinterpret_cast<S*>(smem_raw);
+  pdl_launch();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = (int64_t)blockIdx.y * SR, u0 = (int64_t)blockIdx.x * SU;
+  int64_t myid = -1;  // lane j < SU: the id of code u0 + j (-1: past U or out of range)
+  if (lane < SU && u0 + lane < U) {
+    const int64_t id = __ldg(ids + u0 + lane);
+    const bool ok = id >= 0 && id < V;
+    if (!ok && blockIdx.y == 0 && warp == 0) atomicOr(&g_fault, kFaultBadId);
+    myid = ok ? id : -1;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.full[0], 1);
+    mbar_init(&sh.full[1], 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int nch = (int)((D + SDC - 1) / SDC);
+  // chunk c into buffer c & 1: lane l copies prompt row r0 + l and (l < SU) code row u0 + l; rows past R or without a
+  // valid id copy row 0 (their results are not stored)
+  auto issue = [&](int c) {
+    const int b = c & 1;
+    const int64_t f0 = (int64_t)c * SDC;
+    const uint32_t bytes = (uint32_t)((D - f0 < SDC ? D - f0 : SDC) * 2);
+    const int64_t r = r0 + lane < R ? r0 + lane : 0;
+    bulk_load(sh.h[b][lane], h + r * ldh + f0, bytes, &sh.full[b]);
+    if (lane < SU) bulk_load(sh.w[b][lane], head + (myid >= 0 ? myid : 0) * ldw + f0, bytes, &sh.full[b]);
+    if (lane == 0) mbar_arrive_expect_tx(&sh.full[b], bytes * (SR + SU));
+  };
+  if (warp == 0) {
+    issue(0);
+    if (nch > 1) issue(1);
+  }
+  float acc[NV];
+#pragma unroll
+  for (int e = 0; e < NV; ++e) acc[e] = 0.0f;
+  for (int c = 0; c < nch; ++c) {
+    const int b = c & 1;
+    const bool ok = mbar_wait(&sh.full[b], (uint32_t)(c >> 1) & 1, &sh.abort, kFaultTimeoutEpilogue);
+    if (!__syncthreads_and(ok)) {  // a copy never landed: wait (bounded) for the ones in flight, store nothing
+      if (threadIdx.x == 0) {
+        blockgemm::drain_wait(&sh.full[b], (uint32_t)(c >> 1) & 1);
+        if (c + 1 < nch) blockgemm::drain_wait(&sh.full[b ^ 1], (uint32_t)((c + 1) >> 1) & 1);
+      }
+      __syncthreads();
+      return;
+    }
+    const int nsub = (int)((D - (int64_t)c * SDC < SDC ? D - (int64_t)c * SDC : SDC) / CHUNK);
+    for (int i = 0; i < nsub; ++i) {
+      const int f = i * CHUNK + lane * 8;
+      float a[PW][8], bv[8];
+#pragma unroll
+      for (int ii = 0; ii < PW; ++ii) {
+        const uint4 wv[1] = {*reinterpret_cast<const uint4*>(&sh.h[b][warp * PW + ii][f])};
+        unpack8(wv, h, a[ii]);
+      }
+#pragma unroll
+      for (int j = 0; j < SU; ++j) {
+        const uint4 wv[1] = {*reinterpret_cast<const uint4*>(&sh.w[b][j][f])};
+        unpack8(wv, head, bv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)  // consecutive FMAs on the PW prompts' accumulators: independent, no stall
+#pragma unroll
+          for (int ii = 0; ii < PW; ++ii) acc[ii * SU + j] = fmaf(a[ii][e], bv[e], acc[ii * SU + j]);
+      }
+    }
+    __syncthreads();  // every warp is done with buffer b
+    if (warp == 0 && c + 2 < nch) issue(c + 2);
+  }
+  halving_reduce<NV>(acc, lane);
+  constexpr int PER = NV / 32;
+  int64_t eid[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) eid[k] = __shfl_sync(0xffffffffu, myid, (lane * PER + k) % SU);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int e = lane * PER + k;
+    const int i = e / SU, j = e % SU;
+    const int64_t r = r0 + warp * PW + i, u = u0 + j;
+    if (r < R && u < U) {
+      float v = acc[k];
+      if (eid[k] < 0) {
+        v = __int_as_float(0x7fc00000);
+      } else if (bias) {
+        v = __fadd_rn(v, load1(bias + eid[k]));
+      }
+      if (softcap > 0.0f) v = __fmul_rn(tanhf(__fdiv_rn(v, softcap)), softcap);
+      z[r * U + u] = v;
     }
   }
 }
