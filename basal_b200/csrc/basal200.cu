@@ -370,7 +370,7 @@ int split_gemm_launch(int dev, const void* q, const float* s, const void* w, con
   sp.x = QUANT ? q : nullptr;
   sp.s = QUANT ? const_cast<float*>(s) : nullptr;
   const int64_t grid = sp.units < g_dev[dev].sms ? sp.units : g_dev[dev].sms;
-  const int threads = smallgemm::SplitCfg<NT>::THREADS + (QUANT ? smallgemm::SplitCfg<NT>::QUANT_WARPS * 32 : 0);
+  constexpr int threads = smallgemm::split_threads<NT, TX>();
   if ((rc = launch_pdl(kp, (unsigned)grid, threads, smem, st, tw, tt, sp))) return rc;
   smallgemm::Params p;
   p.s = s;
@@ -636,7 +636,8 @@ int logits_typed(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const 
   if (bt == BASAL200_F32)
     return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const float*>(bias), softcap, z, st);
   if (bt == BASAL200_BF16)
-    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap, z, st);
+    return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __nv_bfloat16*>(bias), softcap,
+                         z, st);
   if (bt == BASAL200_F16)
     return logits_launch(dev, h, R, D, ldh, head, V, ldw, ids, U, static_cast<const __half*>(bias), softcap, z, st);
   return BASAL200_ERR_DTYPE;
@@ -651,7 +652,8 @@ int logits_head(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const v
       return logits_typed(dev, h, R, D, ldh, static_cast<const __nv_bfloat16*>(head), V, ldw, ids, U, bias, bt, softcap,
                           z, st);
     case BASAL200_F16:
-      return logits_typed(dev, h, R, D, ldh, static_cast<const __half*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
+      return logits_typed(dev, h, R, D, ldh, static_cast<const __half*>(head), V, ldw, ids, U, bias, bt, softcap, z,
+                          st);
     case BASAL200_F32:
       return logits_typed(dev, h, R, D, ldh, static_cast<const float*>(head), V, ldw, ids, U, bias, bt, softcap, z, st);
     default:

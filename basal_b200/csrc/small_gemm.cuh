@@ -345,12 +345,16 @@ struct SplitParams {
 __host__ __device__ constexpr int64_t split_prod_bytes(int64_t M, int64_t N, int64_t nkb) { return M * N * nkb * 4; }
 
 // TX = void: the token codes of a unit come by TMA (tmT). TX = bf16 / f16: the fused linear; QUANT_WARPS more warps
-// quantise each unit's 128-wide slice of the activations (one half-warp a token: 16-byte loads of the next unit issued
-// before this unit's arithmetic, amax by shuffles, blockquant's codes by block_codes8, exactly as act_quant_block_kernel)
-// and write the codes into the stage where the TMA would have put them, in the same 128-byte swizzle.
+// quantise the activations slice by slice (one half-warp a token: the next slice's 16-byte loads issued while this one
+// is quantised, amax by shuffles, blockquant's codes by block_codes8, exactly as act_quant_block_kernel) and write the
+// codes into each unit's stage where the TMA would have put them, in the same 128-byte swizzle.
+template <int NT, typename TX>
+constexpr int split_threads() {
+  return SplitCfg<NT>::THREADS + (std::is_void<TX>::value ? 0 : SplitCfg<NT>::QUANT_WARPS * 32);
+}
+
 template <bool INT8, int NT, typename TX>
-__global__ void __launch_bounds__(SplitCfg<NT>::THREADS + (std::is_void<TX>::value ? 0 : SplitCfg<NT>::QUANT_WARPS * 32),
-                                  1)
+__global__ void __launch_bounds__(split_threads<NT, TX>(), 1)
     split_products_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
                           const SplitParams p) {
   using S = SplitSmem<NT>;
