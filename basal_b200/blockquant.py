@@ -92,6 +92,14 @@ class BlockFormat:
         y = f(x.reshape(-1, shape[-1]), w, ws, bias)
         return y.reshape(*shape[:-1], w.shape[0])
 
+    def linear_glu(self, x, w, ws, act):
+        """x [..., K] through a merged [gate; up] weight of this format [2I, K] -> act(gate) * up [..., I] in x's
+        dtype (act "silu" or "gelu_tanh"), the gate/up products paired in the GEMM's epilogue."""
+        shape = x.shape
+        f = ops.int8_block_linear_glu if self.integer else ops.fp8_block_linear_glu
+        y = f(x.reshape(-1, shape[-1]), w, ws, act)
+        return y.reshape(*shape[:-1], w.shape[0] // 2)
+
 
 class BlockLinear(torch.nn.Module):
     """A linear layer with a block-scaled weight of a format (the subclass's FORMAT) and an optional bias; part(o, n)
@@ -118,3 +126,10 @@ class BlockLinear(torch.nn.Module):
 
     def forward(self, x):
         return self.FORMAT.linear(x, self.weight, self.weight_scale, self.bias)
+
+    def glu(self, x, act="silu"):
+        """For a merged [gate; up] layer (fuse): act(gate) * up of x, in one GEMM (the bias, if any, is not part of
+        the gated form: None is required)."""
+        if self.bias is not None:
+            raise ValueError("the gated linear takes no bias")
+        return self.FORMAT.linear_glu(x, self.weight, self.weight_scale, act)

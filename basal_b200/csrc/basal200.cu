@@ -38,9 +38,11 @@ int current_device(int* dev) {
 }
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
-enum SmemSlot { kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38 };
-// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11 (bits of a 64-bit
-// mask)
+enum SmemSlot {
+  kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50
+};
+// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7
+// (bits of a 64-bit mask)
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -279,11 +281,12 @@ int check_launch_regs(K kernel, int need) {
   return BASAL200_OK;
 }
 
-template <bool INT8, int OUT>
+template <bool INT8, int OUT, int ACT = blockgemm::kActNone>
 int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::OutMaps& out,
                       const blockgemm::Params& p, cudaStream_t st) {
-  auto kern = blockgemm::block_gemm_kernel<INT8, OUT>;
-  const int slot = kSlotBlock + (INT8 ? 3 : 0) + OUT;
+  auto kern = blockgemm::block_gemm_kernel<INT8, OUT, ACT>;
+  const int slot = ACT == blockgemm::kActNone ? kSlotBlock + (INT8 ? 3 : 0) + OUT
+                                              : kSlotGlu + (INT8 ? 4 : 0) + (OUT == BASAL200_F16 ? 2 : 0) + ACT - 1;
   if (!(g_dev[dev].smem_set & (1ull << slot))) {
     const int rc = check_launch_regs(kern, (int)blockgemm::LAUNCH_REGS);
     if (rc) return rc;
@@ -466,6 +469,7 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
   p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
   p.npeers = 1;
   p.col_off = 0;
+  p.glu_up = 0;
   const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;
@@ -518,6 +522,7 @@ int block_gemm_gather(const void* q, const float* s, const void* w, const float*
   p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
   p.npeers = npeers;
   p.col_off = (int)col_off;
+  p.glu_up = 0;
   const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;
@@ -663,6 +668,88 @@ int logits_head(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const v
 
 }  // namespace
 
+// The gated linear y = act(x W_gate^T) * (x W_up^T) of a merged block-quantised [gate; up] weight w [2I, K]: the
+// activation quantiser, then the block GEMM whose epilogue pairs gate block n with up block n (any M: the many-rows
+// kernel; rows past M are clipped by the tensor maps).
+template <bool INT8, int OUT>
+int glu_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::OutMaps& out,
+               const blockgemm::Params& p, int act, cudaStream_t st) {
+  if (act == BASAL200_ACT_SILU) return block_gemm_launch<INT8, OUT, blockgemm::kActSilu>(dev, ta, tb, out, p, st);
+  return block_gemm_launch<INT8, OUT, blockgemm::kActGeluTanh>(dev, ta, tb, out, p, st);
+}
+
+// Few rows: the merged linear into a [M, 2I] temporary of the workspace (few-rows or split kernels, the same bits as
+// the gated epilogue's gate and up values), then glu_rows_kernel.
+int64_t glu_temp_bytes(int64_t M, int64_t I) { return (M * 2 * I * 2 + 255) / 256 * 256; }
+int64_t glu_workspace(int64_t M, int64_t I, int64_t K) {
+  if (M < 1 || M > smallgemm::MAX_ROWS || I <= 0 || K <= 0 || I % 128 || K % 128) return 0;
+  return glu_temp_bytes(M, I) + split_workspace(M, 2 * I, K);
+}
+
+template <int OUT>
+int glu_rows_launch(const void* t, void* y, int64_t M, int64_t I, int act, cudaStream_t st) {
+  const int64_t grid = (M * I / 8 + 255) / 256;
+  if (act == BASAL200_ACT_SILU)
+    return launch_pdl(blockgemm::glu_rows_kernel<OUT, blockgemm::kActSilu>, (unsigned)grid, 256, 0, st, t, y, M, I);
+  return launch_pdl(blockgemm::glu_rows_kernel<OUT, blockgemm::kActGeluTanh>, (unsigned)grid, 256, 0, st, t, y, M,
+                    I);
+}
+
+template <bool INT8>
+int block_linear_glu(const void* x, int xt, const void* w, const float* ws, void* y, int64_t M, int64_t I, int64_t K,
+                     int act, void* q, float* s, void* work, int64_t work_bytes, cudaStream_t st) {
+  if (M < 0 || I <= 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (act != BASAL200_ACT_SILU && act != BASAL200_ACT_GELU_TANH) return BASAL200_ERR_ARG;
+  if (I % 128 || K % 128) return BASAL200_ERR_SHAPE;
+  if (xt != BASAL200_BF16 && xt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (M == 0) return BASAL200_OK;
+  if (!x || !w || !ws || !y || !q || !s) return BASAL200_ERR_ARG;
+  if (!aligned16(w) || !aligned16(y) || !aligned16(q)) return BASAL200_ERR_ALIGN;
+  if (M > (int64_t)1 << 30 || I > (int64_t)1 << 29) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t need = glu_workspace(M, I, K);
+  if (need > 0 && work && work_bytes >= need) {  // few rows
+    if (!aligned16(work)) return BASAL200_ERR_ALIGN;
+    uint8_t* temp = static_cast<uint8_t*>(work);
+    uint8_t* split = temp + glu_temp_bytes(M, I);
+    const int64_t split_bytes = work_bytes - glu_temp_bytes(M, I);
+    if (INT8)
+      rc = basal200_int8_block_linear(x, xt, static_cast<const int8_t*>(w), ws, nullptr, temp, M, 2 * I, K,
+                                      static_cast<int8_t*>(q), s, split, split_bytes, st);
+    else
+      rc = basal200_fp8_block_linear(x, xt, static_cast<const uint8_t*>(w), ws, nullptr, temp, M, 2 * I, K,
+                                     static_cast<uint8_t*>(q), s, split, split_bytes, st);
+    if (rc) return rc;
+    return xt == BASAL200_BF16 ? glu_rows_launch<BASAL200_BF16>(temp, y, M, I, act, st)
+                               : glu_rows_launch<BASAL200_F16>(temp, y, M, I, act, st);
+  }
+  if ((rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
+  CUtensorMap ta, tb;
+  blockgemm::OutMaps out;
+  memset(&out, 0, sizeof(out));
+  if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)(2 * I), (uint64_t)K, blockgemm::BK, 128))) return rc;
+  if ((rc = tmap_u16(&out.m[0], y, (uint64_t)I, (uint64_t)M, 64, blockgemm::BM))) return rc;
+  blockgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = nullptr;
+  p.c = nullptr;
+  p.M = (int)M;
+  p.N = (int)I;
+  p.nkb = (int)(K / 128);
+  p.tiles_n = (int)(I / 128);
+  p.npeers = 1;
+  p.col_off = 0;
+  p.glu_up = (int)I;
+  const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  if (xt == BASAL200_BF16) return glu_launch<INT8, BASAL200_BF16>(dev, ta, tb, out, p, act, st);
+  return glu_launch<INT8, BASAL200_F16>(dev, ta, tb, out, p, act, st);
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // Allocation-free FP8-block linear: the activation codes and scales live in one file-scope device array instead of
 // caller scratch. The array is part of the loaded module, so every GPU that loads the library holds its
@@ -778,6 +865,22 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
   if (rc) return rc;
   return block_gemm<true>(q_scratch, s_scratch, w, ws, bias, y, x_dtype, M, N, K, workspace, workspace_bytes,
                           as_stream(stream));
+}
+
+int64_t basal200_block_linear_glu_workspace_bytes(int64_t M, int64_t I, int64_t K) { return glu_workspace(M, I, K); }
+
+int basal200_fp8_block_linear_glu(const void* x, int x_dtype, const uint8_t* w, const float* ws, void* y, int64_t M,
+                                  int64_t I, int64_t K, int act, uint8_t* q_scratch, float* s_scratch, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
+  return block_linear_glu<false>(x, x_dtype, w, ws, y, M, I, K, act, q_scratch, s_scratch, workspace,
+                                 workspace_bytes, as_stream(stream));
+}
+
+int basal200_int8_block_linear_glu(const void* x, int x_dtype, const int8_t* w, const float* ws, void* y, int64_t M,
+                                   int64_t I, int64_t K, int act, int8_t* q_scratch, float* s_scratch,
+                                   void* workspace, int64_t workspace_bytes, void* stream) {
+  return block_linear_glu<true>(x, x_dtype, w, ws, y, M, I, K, act, q_scratch, s_scratch, workspace,
+                                workspace_bytes, as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing

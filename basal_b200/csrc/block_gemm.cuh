@@ -74,7 +74,20 @@ struct Params {
   int M, N, nkb, tiles_n, num_tiles;
   int npeers;       // 16-bit outputs: the output buffers the tiles are stored into (OutMaps), 1 or, for a column-
   int col_off;      // parallel linear gathered on the fly, every rank's [M, n_total] output, at column col_off
+  int glu_up;       // gated linear (ACT != 0): the weight rows [gate; up] with up from row glu_up (= the output width)
 };
+
+// Gated-linear activations of the fused gate/up epilogue, in fp32 on the 16-bit-rounded gate, with the formulas and
+// operation order of torch's CUDA kernels (so that the cast result matches the unfused ops'): silu(x) = x / (1 +
+// e^-x); gelu, tanh form: 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).
+enum { kActNone = 0, kActSilu = 1, kActGeluTanh = 2 };
+template <int ACT>
+__device__ __forceinline__ float glu_act(float x) {
+  if (ACT == kActSilu) return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+  const float cube = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(0.044715f, cube)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
 
 // The tensor maps of the output buffers of a 16-bit output: one for a plain GEMM; one per rank for a GEMM whose
 // column shard is stored straight into every rank's full output (the all-gather of a column-parallel linear done by
@@ -217,6 +230,76 @@ struct Store<BASAL200_F32> {
   }
 };
 
+// The gated linear's second step for few rows: y [M, I] = act(gate) * up from the merged linear's 16-bit output
+// t [M, 2I] (gate columns 0 .. I-1, up I .. 2I-1), 8 outputs a thread, the same arithmetic as glu_apply.
+template <int OUT, int ACT>
+__global__ void __launch_bounds__(256) glu_rows_kernel(const void* __restrict__ t, void* __restrict__ y, int64_t M,
+                                                       int64_t I) {
+  using OutT = typename Store<OUT>::T;
+  pdl_launch();
+  pdl_wait();
+  const int64_t idx = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 8;  // first output of this thread
+  if (idx >= M * I) return;
+  const int64_t m = idx / I, c = idx - m * I;
+  const OutT* tr = static_cast<const OutT*>(t) + m * 2 * I;
+  const uint4 gw = *reinterpret_cast<const uint4*>(tr + c);
+  const uint4 uw = *reinterpret_cast<const uint4*>(tr + I + c);
+  const OutT* gh = reinterpret_cast<const OutT*>(&gw);
+  const OutT* uh = reinterpret_cast<const OutT*>(&uw);
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float a = static_cast<float>(static_cast<OutT>(glu_act<ACT>(static_cast<float>(gh[e]))));
+    v[e] = __fmul_rn(a, static_cast<float>(uh[e]));
+  }
+  Store<OUT>::vec8(static_cast<OutT*>(y) + idx, v, nullptr);
+}
+
+// The gated epilogue's two steps for one promotion thread (row r of the tile, 128 accumulator columns as packed
+// pairs): glu_send casts the 64 columns from group J0 (8 columns a group) into a staging sub-tile for the other
+// warpgroup; glu_apply combines this thread's 64 columns from group J0 with the other warpgroup's cast values
+// (`other`) into act(gate) * up, stored into sub-tile `dst` (OWN_GATE: this thread holds the gate).
+template <int OUT, int J0>
+__device__ __forceinline__ void glu_send(const uint64_t (&acc)[64], uint8_t* sub, int r) {
+  using OutT = typename Store<OUT>::T;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_f2(acc[(J0 + j) * 4 + i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    Store<OUT>::vec8(reinterpret_cast<OutT*>(sub + sw128(r, j)), v, nullptr);
+  }
+}
+
+template <int OUT, int ACT, int J0, bool OWN_GATE>
+__device__ __forceinline__ void glu_apply(const uint64_t (&acc)[64], const uint8_t* other, uint8_t* dst, int r) {
+  using OutT = typename Store<OUT>::T;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float own[8], y[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_f2(acc[(J0 + j) * 4 + i]);
+      own[2 * i] = f.x;
+      own[2 * i + 1] = f.y;
+    }
+    const uint4 ow = Store<OUT>::pack(own, nullptr);  // this thread's linear output, cast
+    const uint4 xw = *reinterpret_cast<const uint4*>(other + sw128(r, j));
+    const OutT* gh = reinterpret_cast<const OutT*>(OWN_GATE ? &ow : &xw);
+    const OutT* uh = reinterpret_cast<const OutT*>(OWN_GATE ? &xw : &ow);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float a = static_cast<float>(static_cast<OutT>(glu_act<ACT>(static_cast<float>(gh[e]))));
+      y[e] = __fmul_rn(a, static_cast<float>(uh[e]));
+    }
+    Store<OUT>::vec8(reinterpret_cast<OutT*>(dst + sw128(r, j)), y, nullptr);
+  }
+}
+
 // Redistributes a warp's 32 rows x CH chunks of 16 bytes (CH = 8 or 4; lane = row, c[j] = chunk j) so that lane L
 // holds in c[i] chunk L % CH of row (32 / CH) i + L / CH, and a store of c[i] by the warp writes 32 / CH whole row
 // segments of 16 CH bytes: log2(CH) shuffle exchanges of a chunk-index bit with a lane bit (chunk bit k with lane
@@ -255,10 +338,16 @@ __device__ __forceinline__ void rows_to_segments(uint4 (&c)[CH], int lane) {
   }
 }
 
-template <bool INT8, int OUT>
+// ACT != kActNone: the gated linear y = act(x W_gate^T) * (x W_up^T) of a merged [gate; up] weight (up from row
+// p.glu_up), for 16-bit outputs: a 256-wide tile holds gate block tn (accumulator columns 0-127, loaded as one
+// 128-row box) and up block tn (columns 128-255). The two promotion warpgroups trade half of their cast values
+// through the staging buffer, each computes act(gate) * up for 64 columns with the roundings of the unfused torch ops
+// (each linear output cast, act(.) cast, the product cast), and one 128-column output tile is stored.
+template <bool INT8, int OUT, int ACT = kActNone>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     block_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ OutMaps out, const Params p) {
+  static_assert(ACT == kActNone || OUT != BASAL200_F32, "the gated linear stores 16-bit outputs");
   using S = SmemOf<OUT>;
   constexpr int STAGES = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -311,7 +400,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           mbar_arrive_expect_tx(&sh.full[stage], STAGE_TX);
           tma_load_2d(sh.a[stage], &tmA, &sh.full[stage], kb * BK, tm * BM);
-          tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BK, tn * BN);
+          if (ACT != kActNone) {  // gate block tn, then up block tn (tmB's box: 128 rows)
+            tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BK, tn * 128);
+            tma_load_2d(sh.b[stage] + B_BYTES / 2, &tmB, &sh.full[stage], kb * BK, p.glu_up + tn * 128);
+          } else {
+            tma_load_2d(sh.b[stage], &tmB, &sh.full[stage], kb * BK, tn * BN);
+          }
           filled |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -379,10 +473,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int row = tm * BM + r;
-      const int n0 = tn * BN + half * 128;
+      const int n0 = ACT != kActNone ? tn * 128 : tn * BN + half * 128;  // gated: the output columns of the tile
       const bool nvalid = n0 < p.N;
       const float* srow = p.s + (int64_t)min(row, p.M - 1) * nkb;
-      const float* wsr = p.ws + (int64_t)min(n0 / 128, p.N / 128 - 1) * nkb;
+      const int wblk = ACT != kActNone ? (half ? p.glu_up / 128 + tn : tn) : min(n0 / 128, p.N / 128 - 1);
+      const float* wsr = p.ws + (int64_t)wblk * nkb;
       uint64_t acc[64];  // 128 fp32 accumulators as packed pairs
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0ull;
@@ -416,7 +511,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ++acc_cnt;
       }
       const OutT* bias = (p.bias && nvalid) ? reinterpret_cast<const OutT*>(p.bias) + n0 : nullptr;
-      if constexpr (S::STAGING) {
+      if constexpr (ACT != kActNone) {
+        // the up half casts its values into its two staging sub-tiles; the gate half turns them into the output.
+        // Both halves take every barrier below, so they agree on going on first (all 256 promotion threads).
+        if (issuer) tma_store_wait_read();     // the previous tile's stores have read the staging
+        ok = named_barrier_and(3, 256, ok);
+        if (!ok) break;
+        // each half activates 64 of the tile's 128 output columns: the gate half columns 0-63 (sub-tile 0), the up
+        // half 64-127 (sub-tile 1); first each casts the values the other half needs into staging sub-tile 2 (up,
+        // columns 0-63) or 3 (gate, columns 64-127). (Constant register indices in both branches: an index that
+        // depends on the half would put the accumulators in local memory.)
+        if (half) {
+          glu_send<OUT, 0>(acc, sh.out[2], r);
+        } else {
+          glu_send<OUT, 8>(acc, sh.out[3], r);
+        }
+        named_barrier(4, 256);  // the exchanged values are in shared memory
+        if (half) {
+          glu_apply<OUT, ACT, 8, false>(acc, sh.out[3], sh.out[1], r);
+        } else {
+          glu_apply<OUT, ACT, 0, true>(acc, sh.out[2], sh.out[0], r);
+        }
+        fence_proxy_async();
+        named_barrier(5, 256);  // both halves have read the exchanged values and written the output tile
+        if (half == 0 && issuer) {
+          for (int q = 0; q < p.npeers; ++q) {
+            tma_store_2d(&out.m[q], sh.out[0], p.col_off + n0, tm * BM);
+            tma_store_2d(&out.m[q], sh.out[1], p.col_off + n0 + 64, tm * BM);
+          }
+          tma_store_commit();
+        }
+      } else if constexpr (S::STAGING) {
         // cast (+ bias) into this half's two staging sub-tiles, then two TMA stores of 128 rows x 64 columns
         if (issuer) tma_store_wait_read();          // the previous tile's stores have read the staging
         ok = named_barrier_and(1 + half, 128, ok);  // the warpgroup agrees whether to go on

@@ -141,9 +141,10 @@ __global__ void __launch_bounds__(IWARPS * 32) code_logits_warp_kernel(
 // code_logits for 16-bit h and head with D a multiple of 256 and many codes (U > 8): a CTA of 8 warps takes 32
 // prompts x 16 codes, warp w the prompts 4w .. 4w + 3 of it. The CTA's 48 rows are staged in shared memory by bulk
 // copies, 1024 features at a time in two buffers (one warp issues a row a lane), so every byte a chunk needs is
-// requested at once instead of in 8 dependent rounds of register loads. A lane then walks exactly the features it walks in
-// code_logits_warp_kernel (l * 8 .. l * 8 + 7 of every 256-feature chunk, in increasing order) and the partials meet
-// in the same halving reduction, so every z[r, u] is the same bits whichever of the two kernels computes it.
+// requested at once instead of in 8 dependent rounds of register loads. A lane then walks exactly the features it
+// walks in code_logits_warp_kernel (l * 8 .. l * 8 + 7 of every 256-feature chunk, in increasing order) and the
+// partials meet in the same halving reduction, so every z[r, u] is the same bits whichever of the two kernels
+// computes it.
 constexpr int SR = 32;      // prompts a staged CTA
 constexpr int SU = 16;      // codes a staged CTA
 constexpr int SDC = 1024;   // features a staged chunk

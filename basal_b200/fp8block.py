@@ -6,6 +6,8 @@ to every 128-deep slice of the reduction and adds the slices in fp32.
   act_quant(x)           activations [M, K] -> (FP8 [M, K], scales [M, K / 128])
   gemm(q, s, w, ws, dt)  the op basal::fp8_block_gemm: [M, N] in dt
   linear(x, w, ws, b)    x [..., K] -> [..., N]: the op basal::fp8_block_linear (act_quant + GEMM + bias)
+  linear_glu(x, w, ws, a) a merged [gate; up] weight -> act(gate) * up: basal::fp8_block_linear_glu (no counterpart
+                         in the reference, which applies the activation after the merged linear)
   BlockFP8Linear         a linear layer holding (w, ws, bias); lean.linear runs its parameters in compiled layers
 
 The reference's Hopper branch (flashinfer's SM90 kernel, fp8block.py:37-71) has no counterpart: sm90() is False and
@@ -30,6 +32,11 @@ def sm90():
 def linear(x, w, ws, bias=None):
     """x [..., K] (bf16) through a block-scaled FP8 weight -> [..., N] in x's dtype."""
     return FORMAT.linear(x, w, ws, bias)
+
+
+def linear_glu(x, w, ws, act="silu"):
+    """x [..., K] through a merged block-FP8 [gate; up] weight [2I, K] -> act(gate) * up [..., I] in one GEMM."""
+    return FORMAT.linear_glu(x, w, ws, act)
 
 
 class BlockFP8Linear(BlockLinear):

@@ -6,6 +6,10 @@
   basal::fp8_block_linear(x, w, ws, bias)        act_quant + GEMM (+ bias): what fp8block.linear computes
                                                  (fp8block.py:285-296); takes the place of basal::fp8_block_linear_sm90
   basal::int8_block_linear(x, w, ws, bias)       the same for INT8 (BlockFormat.linear, blockquant.py:175-183)
+  basal::fp8_block_linear_glu(x, w, ws, act), basal::int8_block_linear_glu(...)
+                                                 act(gate) * up of a merged [gate; up] weight in one GEMM: what
+                                                 gemma4_graph.py:193-197 / gdn_graph.py:127-128 compute after the
+                                                 merged gate/up linear
   basal::fp8_act_quant(x), basal::int8_act_quant(x)
                                                  BlockFormat.act_quant (blockquant.py:137-144), as ops so that a
                                                  compiled layer keeps them whole
@@ -132,6 +136,52 @@ def fp8_block_linear(x: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor] = 
 @fp8_block_linear.register_fake
 def _(x, w, ws, bias=None):
     return x.new_empty((x.shape[0], w.shape[0]))
+
+
+_ACT = {"silu": 1, "gelu_tanh": 2}
+
+
+def _block_linear_glu(x, w, ws, act, integer):
+    require_cuda(x, w, ws)
+    if act not in _ACT:
+        raise ValueError(f"gated linear: act must be one of {sorted(_ACT)}, not {act!r}")
+    x, w, ws = _c(x), _c(w), _c(ws)
+    M, K = x.shape
+    if w.shape[0] % 256:
+        raise ValueError(f"gated linear: the merged [gate; up] weight has {w.shape[0]} rows, not a multiple of 256")
+    I = w.shape[0] // 2
+    y = torch.empty((M, I), dtype=x.dtype, device=x.device)
+    q = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((M, max(K // 128, 1)), dtype=torch.float32, device=x.device)
+    name = "basal200_int8_block_linear_glu" if integer else "basal200_fp8_block_linear_glu"
+    n = int(_lib.lib().basal200_block_linear_glu_workspace_bytes(M, I, K))
+    work = torch.empty(n, dtype=torch.uint8, device=x.device) if n > 0 else None
+    call(name, x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(y), M, I, K, _ACT[act], ptr(q), ptr(s),
+         ptr(work), n)
+    return y
+
+
+@torch.library.custom_op("basal::fp8_block_linear_glu", mutates_args=())
+def fp8_block_linear_glu(x: Tensor, w: Tensor, ws: Tensor, act: str) -> Tensor:
+    """x [M, K] through a merged block-FP8 [gate; up] weight [2I, K] -> act(gate) * up [M, I] in x's dtype, one GEMM
+    whose epilogue pairs the gate and up columns (act: "silu" or "gelu_tanh")."""
+    return _block_linear_glu(x, w, ws, act, False)
+
+
+@fp8_block_linear_glu.register_fake
+def _(x, w, ws, act):
+    return x.new_empty((x.shape[0], w.shape[0] // 2))
+
+
+@torch.library.custom_op("basal::int8_block_linear_glu", mutates_args=())
+def int8_block_linear_glu(x: Tensor, w: Tensor, ws: Tensor, act: str) -> Tensor:
+    """The INT8 format of fp8_block_linear_glu."""
+    return _block_linear_glu(x, w, ws, act, True)
+
+
+@int8_block_linear_glu.register_fake
+def _(x, w, ws, act):
+    return x.new_empty((x.shape[0], w.shape[0] // 2))
 
 
 @torch.library.custom_op("basal::int8_block_linear", mutates_args=())

@@ -438,6 +438,23 @@ def run_sweep(fmts):
 
     base = graph_us(lambda: flush.sum())
     gen = torch.Generator(device=dev).manual_seed(0)
+    if "glu" in fmts:
+        # C2's gate/up projection (2048 -> 2 x 6144) with the SwiGLU that follows it: the gated linear in one GEMM
+        # (basal::fp8_block_linear_glu) against the merged linear and torch's silu and product
+        K, I = 2048, 6144
+        qg, sg = b2.fp8block.quantize(torch.randn(2 * I, K, device=dev, generator=gen) * 0.02)
+        for M in (16, 1024, 8192, 77431):
+            x = torch.randn(M, K, device=dev, generator=gen).bfloat16()
+
+            def unfused():
+                y = b2.fp8block.linear(x, qg, sg)
+                return torch.nn.functional.silu(y[:, :I]) * y[:, I:]
+            tf = graph_us(lambda: (flush.sum(), b2.fp8block.linear_glu(x, qg, sg, "silu"))) - base
+            tu = graph_us(lambda: (flush.sum(), unfused())) - base
+            print(json.dumps({"sweep": "gated linear (C2 gate/up + SwiGLU)", "M": M, "I": I, "K": K,
+                              "fused_us": round(tf, 2), "unfused_us": round(tu, 2),
+                              "fused_tflops": round(2 * M * 2 * I * K / tf / 1e6, 1)}), flush=True)
+        fmts = [f for f in fmts if f != "glu"]
     if "readout" in fmts:
         # C4's readout: h [256, 2048] bf16 ~ N(0, 1) at the answer positions, a 151,936-row bf16 head ~ N(0, 0.02),
         # one code set of k ids shared by all rows; the device part (code_logits + code_probs) per call
@@ -599,8 +616,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
-    ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout) "
-                    "instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
+    ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout, "
+                    "glu) instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
     args = ap.parse_args()
     if args.sweep == "tp":  # under torchrun, 2 or more GPUs
         import datetime

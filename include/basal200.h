@@ -101,6 +101,31 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Activations of the gated linears. */
+enum { BASAL200_ACT_SILU = 1, BASAL200_ACT_GELU_TANH = 2 };
+
+/* The gated MLP input of a SwiGLU / GeGLU layer in one call: y [M, I] = act(x W_gate^T) * (x W_up^T) for a merged
+ * block-quantised weight w [2I, K] = [gate; up] (the layout of blockquant.fuse, basal/blockquant.py:43-51, with the
+ * scales ws [2I/128, K/128]), x [M, K] bf16 or fp16, y in x's type. act = BASAL200_ACT_SILU (Qwen,
+ * basal/gdn_graph.py:127-128) or BASAL200_ACT_GELU_TANH (Gemma, basal/gemma4_graph.py:193-197). Replaces the pair
+ * "linear of the merged gate/up weight, then act(gate) * up" with the same roundings (each linear output cast to
+ * x's type, act(.) cast, the product cast): the activation quantiser into the scratch (as basal200_fp8_block_linear),
+ * then one GEMM whose epilogue pairs gate and up columns, so the [M, 2I] intermediate is never written (few rows
+ * with a workspace: see basal200_block_linear_glu_workspace_bytes). I % 128 == 0, K % 128 == 0. */
+int basal200_fp8_block_linear_glu(const void* x, int x_dtype, const uint8_t* w, const float* ws, void* y, int64_t M,
+                                  int64_t I, int64_t K, int act, uint8_t* q_scratch, float* s_scratch, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+
+/* The INT8 format of the same (int8block.py:349-350). */
+int basal200_int8_block_linear_glu(const void* x, int x_dtype, const int8_t* w, const float* ws, void* y, int64_t M,
+                                   int64_t I, int64_t K, int act, int8_t* q_scratch, float* s_scratch,
+                                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes (16-byte aligned) with which the gated linears above run few rows (M <= 64) as the few-rows linear
+ * of the merged weight into a [M, 2I] temporary, then the activation: the same bits as without it, faster. 0 for
+ * M > 64. Pure: no device call. */
+int64_t basal200_block_linear_glu_workspace_bytes(int64_t M, int64_t I, int64_t K);
+
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)
 

@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 def test_binding_covers_the_header():
     from basal_b200 import _lib
     bound = set(_lib.SIGNATURES) | {"basal200_status_string", "basal200_version", "basal200_device_faults",
-                                    "basal200_block_gemm_workspace_bytes"}
+                                    "basal200_block_gemm_workspace_bytes", "basal200_block_linear_glu_workspace_bytes"}
     assert bound == set(declared())
 
 
@@ -63,6 +63,15 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 256, 256, 0, 4, 128, 256, null) == 2
     assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 2, 4, 128, 256, null) == 4
     assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 0, 0, 128, 256, null) == 0
+    # gated linear: an unknown activation; I not a multiple of 128; fp32 activations; M = 0 is an empty success
+    glu = lib.basal200_fp8_block_linear_glu
+    assert glu(null, 0, null, null, null, 4, 256, 256, 3, null, null, null, 0, null) == 1
+    assert glu(null, 0, null, null, null, 4, 200, 256, 1, null, null, null, 0, null) == 2
+    assert lib.basal200_int8_block_linear_glu(null, 2, null, null, null, 4, 256, 256, 2, null, null, null, 0, null) == 4
+    assert glu(null, 0, null, null, null, 0, 256, 256, 1, null, null, null, 0, null) == 0
+    gws = lib.basal200_block_linear_glu_workspace_bytes
+    assert gws(16, 6144, 2048) == 16 * 12288 * 2 and gws(65, 6144, 2048) == 0
+    assert gws(16, 1024, 2048) == 16 * 2048 * 2 + 16 * 2048 * 16 * 4  # plus the split products
     # readout: Kmax beyond 1024
     assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
 

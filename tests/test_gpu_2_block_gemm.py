@@ -232,3 +232,70 @@ def test_c2_projection_shapes_by_row_samples(b2, fmt, name, N, K):
     err = np.abs(got - ref).max(1) / np.abs(ref).max(1)
     assert err.max() < 1e-2, err.max()
     assert torch.equal(m.linear(x[rows.cuda()], q, s), y[rows.cuda()])
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("M, I, K, dt", [(1, 128, 256, torch.bfloat16), (37, 384, 1024, torch.bfloat16),
+                                         (300, 256, 512, torch.float16), (1000, 640, 2048, torch.bfloat16)])
+def test_gated_linear_equals_the_unfused_ops(b2, fmt, act, M, I, K, dt):
+    """act(gate) * up of a merged [gate; up] weight in one GEMM (the epilogue pairs gate block n with up block n):
+    within one unit in the last place of x's dtype of the unfused ops on the same GPU (the merged linear, cast, then
+    torch's activation and product on those tensors: the gate and up values are the same bits, only the activation's
+    implementation may differ), and within the north-star 1e-2 of the oracle's fp32 linear followed by the same ops
+    on CPU; rows past M and every 128-column output tile covered."""
+    g = torch.Generator().manual_seed(M + I + K)
+    x = torch.randn(M, K, generator=g).to(dt)
+    w = torch.randn(2 * I, K, generator=g) * 0.02
+    m = mod(b2, fmt)
+    q, s = m.quantize(w.cuda())
+    fused = m.FORMAT.linear_glu(x.cuda(), q, s, act)
+    assert fused.shape == (M, I) and fused.dtype == dt
+    f = torch.nn.functional.silu if act == "silu" else (lambda t: torch.nn.functional.gelu(t, approximate="tanh"))
+    full = m.linear(x.cuda(), q, s)
+    want = f(full[:, :I]) * full[:, I:]
+    eps = 2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10
+    diff = (fused.float() - want.float()).abs()
+    assert bool((diff <= eps * want.float().abs() + 1e-6).all()), diff.max()
+    qc = q.view(torch.uint8).cpu().numpy() if fmt == "fp8" else q.cpu().numpy()
+    ref_full = torch.from_numpy(obq.linear(x.float().numpy(), qc, s.cpu().numpy(), fmt)).to(dt)
+    ref = (f(ref_full[:, :I].float()).to(dt).float() * ref_full[:, I:].float()).to(dt).float()
+    err = (fused.float().cpu() - ref).abs().max() / ref.abs().max()
+    assert err < 1e-2, err
+    assert b2._lib.device_faults(0) == 0
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("I", [256, 6144])
+def test_gated_linear_rows_alone_and_among_others(b2, fmt, act, I):
+    """A row's gated output is the same bits alone (few rows: the merged linear into a temporary, then the activation
+    kernel; split over the SMs at I = 256) and among 300 rows (the large-M kernel's gated epilogue)."""
+    K = 1024
+    g = torch.Generator().manual_seed(I + len(act))
+    x = torch.randn(300, K, generator=g).bfloat16().cuda()
+    m = mod(b2, fmt)
+    q, s = m.quantize((torch.randn(2 * I, K, generator=g) * 0.02).cuda())
+    many = m.FORMAT.linear_glu(x, q, s, act)
+    for M in (1, 16, 64):
+        few = m.FORMAT.linear_glu(x[:M].contiguous(), q, s, act)
+        assert torch.equal(few, many[:M]), (M, (few.float() - many[:M].float()).abs().max())
+
+
+def test_gated_linear_module_and_refusals(b2):
+    """BlockFP8Linear.glu on a merged layer is the op; a bias, an odd row count or an unknown activation is refused."""
+    g = torch.Generator().manual_seed(5)
+    lin = torch.nn.Linear(512, 512, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(512, 512, generator=g) * 0.02)
+    layer = b2.fp8block.BlockFP8Linear.of(lin.cuda())
+    x = torch.randn(3, 7, 512, generator=g).bfloat16().cuda()
+    y = layer.glu(x, "gelu_tanh")
+    assert y.shape == (3, 7, 256)
+    assert torch.equal(y.reshape(21, 256),
+                       torch.ops.basal.fp8_block_linear_glu(x.reshape(21, 512), layer.weight, layer.weight_scale,
+                                                            "gelu_tanh"))
+    with pytest.raises(ValueError):
+        layer.glu(x, "relu")
+    with pytest.raises(ValueError):
+        torch.ops.basal.fp8_block_linear_glu(x.reshape(21, 512), layer.weight[:384], layer.weight_scale[:3], "silu")
