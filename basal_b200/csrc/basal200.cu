@@ -535,7 +535,9 @@ int fp4_gemm_launch(int dev, const void* q, const void* w, int64_t Mp, int64_t N
                     cudaStream_t st) {
   CUtensorMap ta, tb;
   int rc;
-  if ((rc = tmap_u8(&ta, q, (uint64_t)(K / 2), (uint64_t)Mp, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BM)))
+  // the activation map ends at row M: the TMA fills the rows of the last 128-row tile past M with zero codes (the
+  // bytes the quantiser wrote there) without reading them, which matters for few rows (M = 16: 16 of 128 rows)
+  if ((rc = tmap_u8(&ta, q, (uint64_t)(K / 2), (uint64_t)p.M, (uint64_t)(K / 2), fp4gemm::BKB, fp4gemm::BM)))
     return rc;
   if ((rc = tmap_u8(&tb, w, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), fp4gemm::BKB, BN))) return rc;
   p.tiles_n = (int)((N + BN - 1) / BN);

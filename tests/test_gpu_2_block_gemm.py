@@ -282,6 +282,25 @@ def test_gated_linear_rows_alone_and_among_others(b2, fmt, act, I):
         assert torch.equal(few, many[:M]), (M, (few.float() - many[:M].float()).abs().max())
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+def test_gated_linear_without_workspace(b2, fmt):
+    """Through the C ABI with no workspace, a few-rows gated linear runs the many-rows kernel's gated epilogue: the
+    same bits as the op (which passes a workspace: the few-rows linear into a temporary, then the activation)."""
+    from basal_b200 import _lib
+    M, I, K = 16, 384, 512
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    m = mod(b2, fmt)
+    q, s = m.quantize((torch.randn(2 * I, K, generator=g) * 0.02).cuda())
+    y = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    qs = torch.empty(M, K, dtype=torch.uint8, device="cuda")
+    ss = torch.empty(M, K // 128, dtype=torch.float32, device="cuda")
+    name = "basal200_int8_block_linear_glu" if fmt == "int8" else "basal200_fp8_block_linear_glu"
+    _lib.call(name, x.device, _lib.ptr(x), _lib.BF16, _lib.ptr(q), _lib.ptr(s), _lib.ptr(y), M, I, K, 1,
+              _lib.ptr(qs), _lib.ptr(ss), None, 0)
+    assert torch.equal(y, m.FORMAT.linear_glu(x, q, s, "silu"))
+
+
 def test_gated_linear_module_and_refusals(b2):
     """BlockFP8Linear.glu on a merged layer is the op; a bias, an odd row count or an unknown activation is refused."""
     g = torch.Generator().manual_seed(5)
