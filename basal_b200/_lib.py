@@ -36,6 +36,8 @@ SIGNATURES = {
     "basal200_fp8_block_linear_noalloc": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "basal200_fp8_block_linear_glu": [_P, _I, _P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _P, _I64, _P],
     "basal200_int8_block_linear_glu": [_P, _I, _P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _P, _I64, _P],
+    "basal200_fp8_block_linear_residual": [_P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
+    "basal200_int8_block_linear_residual": [_P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
     "basal200_nvfp4_act_quant": [_P, _I, _P, _I64, _I64, _P, _P, _P],
     "basal200_nvfp4_gemm": [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
     "basal200_nvfp4_linear": [_P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
@@ -64,6 +66,8 @@ def lib():
         L.basal200_block_gemm_workspace_bytes.restype = _I64
         L.basal200_block_linear_glu_workspace_bytes.argtypes = [_I64, _I64, _I64]
         L.basal200_block_linear_glu_workspace_bytes.restype = _I64
+        L.basal200_block_linear_residual_workspace_bytes.argtypes = [_I64, _I64, _I64]
+        L.basal200_block_linear_residual_workspace_bytes.restype = _I64
         L.basal200_device_faults.argtypes, L.basal200_device_faults.restype = [_I, _I], ctypes.c_uint
         _lib = L
     return _lib

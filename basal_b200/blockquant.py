@@ -92,6 +92,14 @@ class BlockFormat:
         y = f(x.reshape(-1, shape[-1]), w, ws, bias)
         return y.reshape(*shape[:-1], w.shape[0])
 
+    def linear_residual(self, x, w, ws, bias, residual):
+        """residual + (x [..., K] through a block-scaled weight of this format, + bias) -> [..., N] in x's dtype, the
+        sum in the GEMM's epilogue (the roundings of the linear followed by torch's addition)."""
+        shape = x.shape
+        f = ops.int8_block_linear_residual if self.integer else ops.fp8_block_linear_residual
+        y = f(x.reshape(-1, shape[-1]), w, ws, bias, residual.reshape(-1, w.shape[0]))
+        return y.reshape(*shape[:-1], w.shape[0])
+
     def linear_glu(self, x, w, ws, act):
         """x [..., K] through a merged [gate; up] weight of this format [2I, K] -> act(gate) * up [..., I] in x's
         dtype (act "silu" or "gelu_tanh"), the gate/up products paired in the GEMM's epilogue."""
@@ -126,6 +134,10 @@ class BlockLinear(torch.nn.Module):
 
     def forward(self, x):
         return self.FORMAT.linear(x, self.weight, self.weight_scale, self.bias)
+
+    def forward_residual(self, x, residual):
+        """residual + forward(x), the addition in the GEMM's epilogue (the same bits as the two steps)."""
+        return self.FORMAT.linear_residual(x, self.weight, self.weight_scale, self.bias, residual)
 
     def glu(self, x, act="silu"):
         """For a merged [gate; up] layer (fuse): act(gate) * up of x, in one GEMM (the bias, if any, is not part of

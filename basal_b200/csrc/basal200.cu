@@ -39,10 +39,11 @@ int current_device(int* dev) {
 
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
 enum SmemSlot {
-  kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50
+  kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50,
+  kSlotRes = 58
 };
-// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7
-// (bits of a 64-bit mask)
+// kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7,
+// kSlotRes .. + 3 (bits of a 64-bit mask)
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -281,12 +282,14 @@ int check_launch_regs(K kernel, int need) {
   return BASAL200_OK;
 }
 
-template <bool INT8, int OUT, int ACT = blockgemm::kActNone>
+template <bool INT8, int OUT, int ACT = blockgemm::kActNone, bool RES = false>
 int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, const blockgemm::OutMaps& out,
                       const blockgemm::Params& p, cudaStream_t st) {
-  auto kern = blockgemm::block_gemm_kernel<INT8, OUT, ACT>;
-  const int slot = ACT == blockgemm::kActNone ? kSlotBlock + (INT8 ? 3 : 0) + OUT
-                                              : kSlotGlu + (INT8 ? 4 : 0) + (OUT == BASAL200_F16 ? 2 : 0) + ACT - 1;
+  auto kern = blockgemm::block_gemm_kernel<INT8, OUT, ACT, RES>;
+  const int slot = RES ? kSlotRes + (INT8 ? 2 : 0) + (OUT == BASAL200_F16 ? 1 : 0)
+                       : ACT == blockgemm::kActNone
+                             ? kSlotBlock + (INT8 ? 3 : 0) + OUT
+                             : kSlotGlu + (INT8 ? 4 : 0) + (OUT == BASAL200_F16 ? 2 : 0) + ACT - 1;
   if (!(g_dev[dev].smem_set & (1ull << slot))) {
     const int rc = check_launch_regs(kern, (int)blockgemm::LAUNCH_REGS);
     if (rc) return rc;
@@ -752,6 +755,77 @@ int block_linear_glu(const void* x, int xt, const void* w, const float* ws, void
   return glu_launch<INT8, BASAL200_F16>(dev, ta, tb, out, p, act, st);
 }
 
+// The linear with the residual added in the epilogue: y = residual + linear(x) (+ bias), both 16-bit, with torch's
+// roundings (the linear's output cast, the sum cast). Many rows: the block GEMM whose epilogue loads the residual
+// tile; few rows with the workspace: the few-rows / split linear into a temporary, then add_rows_kernel (same bits).
+int64_t res_temp_bytes(int64_t M, int64_t N) { return (M * N * 2 + 255) / 256 * 256; }
+int64_t res_workspace(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || M > smallgemm::MAX_ROWS || N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
+  return res_temp_bytes(M, N) + split_workspace(M, N, K);
+}
+
+template <bool INT8>
+int block_linear_residual(const void* x, int xt, const void* w, const float* ws, const void* bias, const void* res,
+                          void* y, int64_t M, int64_t N, int64_t K, void* q, float* s, void* work, int64_t work_bytes,
+                          cudaStream_t st) {
+  if (M < 0 || N <= 0 || K <= 0) return BASAL200_ERR_ARG;
+  if (N % 128 || K % 128) return BASAL200_ERR_SHAPE;
+  if (xt != BASAL200_BF16 && xt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (M == 0) return BASAL200_OK;
+  if (!x || !w || !ws || !res || !y || !q || !s) return BASAL200_ERR_ARG;
+  if (!aligned16(w) || !aligned16(y) || !aligned16(res) || !aligned16(q) || (bias && !aligned16(bias)))
+    return BASAL200_ERR_ALIGN;
+  if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t need = res_workspace(M, N, K);
+  if (need > 0 && work && work_bytes >= need) {  // few rows
+    if (!aligned16(work)) return BASAL200_ERR_ALIGN;
+    uint8_t* temp = static_cast<uint8_t*>(work);
+    uint8_t* split = temp + res_temp_bytes(M, N);
+    const int64_t split_bytes = work_bytes - res_temp_bytes(M, N);
+    if (INT8)
+      rc = basal200_int8_block_linear(x, xt, static_cast<const int8_t*>(w), ws, bias, temp, M, N, K,
+                                      static_cast<int8_t*>(q), s, split, split_bytes, st);
+    else
+      rc = basal200_fp8_block_linear(x, xt, static_cast<const uint8_t*>(w), ws, bias, temp, M, N, K,
+                                     static_cast<uint8_t*>(q), s, split, split_bytes, st);
+    if (rc) return rc;
+    const int64_t grid = (M * N / 8 + 255) / 256;
+    if (xt == BASAL200_BF16)
+      return launch_pdl(blockgemm::add_rows_kernel<BASAL200_BF16>, (unsigned)grid, 256, 0, st,
+                        static_cast<const void*>(temp), res, y, M * N);
+    return launch_pdl(blockgemm::add_rows_kernel<BASAL200_F16>, (unsigned)grid, 256, 0, st,
+                      static_cast<const void*>(temp), res, y, M * N);
+  }
+  if ((rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
+  CUtensorMap ta, tb;
+  blockgemm::OutMaps out;
+  memset(&out, 0, sizeof(out));
+  if ((rc = tmap_u8(&ta, q, (uint64_t)K, (uint64_t)M, (uint64_t)K, blockgemm::BK, blockgemm::BM))) return rc;
+  if ((rc = tmap_u8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, blockgemm::BK, blockgemm::BN))) return rc;
+  if ((rc = tmap_u16(&out.m[0], y, (uint64_t)N, (uint64_t)M, 64, blockgemm::BM))) return rc;
+  if ((rc = tmap_u16(&out.m[1], res, (uint64_t)N, (uint64_t)M, 64, blockgemm::BM))) return rc;
+  blockgemm::Params p;
+  p.s = s;
+  p.ws = ws;
+  p.bias = bias;
+  p.c = nullptr;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.nkb = (int)(K / 128);
+  p.tiles_n = (int)((N + blockgemm::BN - 1) / blockgemm::BN);
+  p.npeers = 1;
+  p.col_off = 0;
+  p.glu_up = 0;
+  const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
+  if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
+  p.num_tiles = (int)tiles;
+  if (xt == BASAL200_BF16)
+    return block_gemm_launch<INT8, BASAL200_BF16, blockgemm::kActNone, true>(dev, ta, tb, out, p, st);
+  return block_gemm_launch<INT8, BASAL200_F16, blockgemm::kActNone, true>(dev, ta, tb, out, p, st);
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // Allocation-free FP8-block linear: the activation codes and scales live in one file-scope device array instead of
 // caller scratch. The array is part of the loaded module, so every GPU that loads the library holds its
@@ -870,6 +944,26 @@ int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, cons
 }
 
 int64_t basal200_block_linear_glu_workspace_bytes(int64_t M, int64_t I, int64_t K) { return glu_workspace(M, I, K); }
+
+int64_t basal200_block_linear_residual_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return res_workspace(M, N, K);
+}
+
+int basal200_fp8_block_linear_residual(const void* x, int x_dtype, const uint8_t* w, const float* ws,
+                                       const void* bias, const void* residual, void* y, int64_t M, int64_t N,
+                                       int64_t K, uint8_t* q_scratch, float* s_scratch, void* workspace,
+                                       int64_t workspace_bytes, void* stream) {
+  return block_linear_residual<false>(x, x_dtype, w, ws, bias, residual, y, M, N, K, q_scratch, s_scratch, workspace,
+                                      workspace_bytes, as_stream(stream));
+}
+
+int basal200_int8_block_linear_residual(const void* x, int x_dtype, const int8_t* w, const float* ws,
+                                        const void* bias, const void* residual, void* y, int64_t M, int64_t N,
+                                        int64_t K, int8_t* q_scratch, float* s_scratch, void* workspace,
+                                        int64_t workspace_bytes, void* stream) {
+  return block_linear_residual<true>(x, x_dtype, w, ws, bias, residual, y, M, N, K, q_scratch, s_scratch, workspace,
+                                     workspace_bytes, as_stream(stream));
+}
 
 int basal200_fp8_block_linear_glu(const void* x, int x_dtype, const uint8_t* w, const float* ws, void* y, int64_t M,
                                   int64_t I, int64_t K, int act, uint8_t* q_scratch, float* s_scratch, void* workspace,

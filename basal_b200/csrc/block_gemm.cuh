@@ -55,6 +55,7 @@ struct Smem {
   uint64_t empty[STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
+  uint64_t rfull[2];  // residual epilogue: each warpgroup's residual tile has landed in its staging sub-tiles
   uint64_t mdrain;
   uint32_t tmem_base;
   int abort;
@@ -255,6 +256,26 @@ __global__ void __launch_bounds__(256) glu_rows_kernel(const void* __restrict__ 
   Store<OUT>::vec8(static_cast<OutT*>(y) + idx, v, nullptr);
 }
 
+// The residual linear's second step for few rows: y = t + residual (both 16-bit, [n] elements, 8 a thread), rounded
+// as torch adds two 16-bit tensors; y may be the residual itself.
+template <int OUT>
+__global__ void __launch_bounds__(256) add_rows_kernel(const void* __restrict__ t, const void* res, void* y,
+                                                       int64_t n) {
+  using OutT = typename Store<OUT>::T;
+  pdl_launch();
+  pdl_wait();
+  const int64_t idx = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 8;
+  if (idx >= n) return;
+  const uint4 tw = *reinterpret_cast<const uint4*>(static_cast<const OutT*>(t) + idx);
+  const uint4 rw = *reinterpret_cast<const uint4*>(static_cast<const OutT*>(res) + idx);
+  const OutT* th = reinterpret_cast<const OutT*>(&tw);
+  const OutT* rh = reinterpret_cast<const OutT*>(&rw);
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(static_cast<float>(th[e]), static_cast<float>(rh[e]));
+  Store<OUT>::vec8(static_cast<OutT*>(y) + idx, v, nullptr);
+}
+
 // The gated epilogue's two steps for one promotion thread (row r of the tile, 128 accumulator columns as packed
 // pairs): glu_send casts the 64 columns from group J0 (8 columns a group) into a staging sub-tile for the other
 // warpgroup; glu_apply combines this thread's 64 columns from group J0 with the other warpgroup's cast values
@@ -343,11 +364,15 @@ __device__ __forceinline__ void rows_to_segments(uint4 (&c)[CH], int lane) {
 // 128-row box) and up block tn (columns 128-255). The two promotion warpgroups trade half of their cast values
 // through the staging buffer, each computes act(gate) * up for 64 columns with the roundings of the unfused torch ops
 // (each linear output cast, act(.) cast, the product cast), and one 128-column output tile is stored.
-template <bool INT8, int OUT, int ACT = kActNone>
+// RES: y = residual + (the linear's output cast, + bias), rounded as torch adds two 16-bit tensors; the residual
+// [M, N] is read through out.m[1] (the output's box), its tile TMA-loaded into the staging sub-tiles in the middle of
+// the tile's slices, added in place and stored (so y may be the residual itself).
+template <bool INT8, int OUT, int ACT = kActNone, bool RES = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     block_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ OutMaps out, const Params p) {
   static_assert(ACT == kActNone || OUT != BASAL200_F32, "the gated linear stores 16-bit outputs");
+  static_assert(!RES || (ACT == kActNone && OUT != BASAL200_F32), "the residual epilogue: 16-bit plain linears");
   using S = SmemOf<OUT>;
   constexpr int STAGES = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -363,6 +388,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh.tfull[b], 1);
       mbar_init(&sh.tempty[b], NUM_EPI_WARPS);
+      mbar_init(&sh.rfull[b], 1);
     }
     mbar_init(&sh.mdrain, 1);
     sh.abort = 0;
@@ -373,6 +399,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmB);
     if (S::STAGING)
       for (int r = 0; r < p.npeers; ++r) tma_prefetch_desc(&out.m[r]);
+    if (RES) tma_prefetch_desc(&out.m[1]);
   }
   if (warp == 2) tmem_alloc(&sh.tmem_base, TMEM_COLS);
   pdl_launch();
@@ -470,6 +497,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int nkb = p.nkb;
     uint32_t acc_cnt = 0;
     bool ok = true;
+    uint32_t res_phase = 0;    // residual epilogue: tiles of this warpgroup so far (the rfull phase)
+    bool res_pending = false;  // the issuer's residual load not yet waited for
+    const int res_kb = nkb / 2;  // the slice at whose start the residual tile is requested (mid-tile: time to land)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int row = tm * BM + r;
@@ -488,6 +518,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (kb + 1 < nkb) {
           sa = __ldg(srow + kb + 1);
           sb = __ldg(wsr + kb + 1);
+        }
+        if (RES && kb == res_kb && issuer) {  // the residual tile into this half's staging sub-tiles
+          tma_store_wait_read();  // the previous tile's stores have read them
+          if (nvalid) {
+            mbar_arrive_expect_tx(&sh.rfull[half], 2 * SUB_BYTES);
+            tma_load_2d(sh.out[half * 2], &out.m[1], &sh.rfull[half], n0, tm * BM);
+            tma_load_2d(sh.out[half * 2 + 1], &out.m[1], &sh.rfull[half], n0 + 64, tm * BM);
+          } else {
+            mbar_arrive(&sh.rfull[half]);
+          }
+          res_pending = true;
         }
         const uint32_t buf = acc_cnt & 1, ph = (acc_cnt >> 1) & 1;
         if (!warp_wait(&sh.tfull[buf], ph, abort_flag, kFaultTimeoutEpilogue)) {
@@ -544,8 +585,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       } else if constexpr (S::STAGING) {
         // cast (+ bias) into this half's two staging sub-tiles, then two TMA stores of 128 rows x 64 columns
         if (issuer) tma_store_wait_read();          // the previous tile's stores have read the staging
+        if (RES && ok) ok = mbar_wait(&sh.rfull[half], res_phase & 1, abort_flag, kFaultTimeoutEpilogue);
         ok = named_barrier_and(1 + half, 128, ok);  // the warpgroup agrees whether to go on
         if (!ok) break;
+        if (RES) {
+          ++res_phase;
+          res_pending = false;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float v[8];
@@ -556,7 +602,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             v[2 * i + 1] = f.y;
           }
           OutT* dst = reinterpret_cast<OutT*>(sh.out[half * 2 + (j >> 3)] + sw128(r, j & 7));
-          Store<OUT>::vec8(dst, v, bias ? bias + j * 8 : nullptr);
+          if (RES) {  // the linear's output as torch casts it (+ bias), then + the residual, cast again
+            const uint4 lw = Store<OUT>::pack(v, bias ? bias + j * 8 : nullptr);
+            const uint4 rw = *reinterpret_cast<const uint4*>(dst);
+            const OutT* lh = reinterpret_cast<const OutT*>(&lw);
+            const OutT* rh = reinterpret_cast<const OutT*>(&rw);
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(static_cast<float>(lh[e]), static_cast<float>(rh[e]));
+            Store<OUT>::vec8(dst, y, nullptr);
+          } else {
+            Store<OUT>::vec8(dst, v, bias ? bias + j * 8 : nullptr);
+          }
         }
         fence_proxy_async();
         named_barrier(1 + half, 128);
@@ -587,6 +644,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    if (RES && issuer && res_pending) drain_wait(&sh.rfull[half], res_phase & 1);  // an abort left a load in flight
     if (S::STAGING && issuer) tma_store_wait_all();
   }
 

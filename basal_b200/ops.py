@@ -10,6 +10,8 @@
                                                  act(gate) * up of a merged [gate; up] weight in one GEMM: what
                                                  gemma4_graph.py:193-197 / gdn_graph.py:127-128 compute after the
                                                  merged gate/up linear
+  basal::fp8_block_linear_residual(x, w, ws, bias, residual), basal::int8_block_linear_residual(...)
+                                                 residual + linear in one GEMM: gdn_graph.py:128, :439, :466
   basal::fp8_act_quant(x), basal::int8_act_quant(x)
                                                  BlockFormat.act_quant (blockquant.py:137-144), as ops so that a
                                                  compiled layer keeps them whole
@@ -182,6 +184,50 @@ def int8_block_linear_glu(x: Tensor, w: Tensor, ws: Tensor, act: str) -> Tensor:
 @int8_block_linear_glu.register_fake
 def _(x, w, ws, act):
     return x.new_empty((x.shape[0], w.shape[0] // 2))
+
+
+def _block_linear_residual(x, w, ws, bias, residual, integer):
+    require_cuda(x, w, ws, bias, residual)
+    x, w, ws, residual = _c(x), _c(w), _c(ws), _c(residual)
+    M, K = x.shape
+    N = w.shape[0]
+    if residual.shape != (M, N) or residual.dtype != x.dtype:
+        raise ValueError(f"residual linear: the residual must be [{M}, {N}] {x.dtype}, not "
+                         f"{list(residual.shape)} {residual.dtype}")
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    q = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    s = torch.empty((M, max(K // 128, 1)), dtype=torch.float32, device=x.device)
+    if bias is not None:
+        bias = _c(bias.to(x.dtype))
+    n = int(_lib.lib().basal200_block_linear_residual_workspace_bytes(M, N, K))
+    work = torch.empty(n, dtype=torch.uint8, device=x.device) if n > 0 else None
+    name = "basal200_int8_block_linear_residual" if integer else "basal200_fp8_block_linear_residual"
+    call(name, x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(bias), ptr(residual), ptr(y), M, N, K, ptr(q),
+         ptr(s), ptr(work), n)
+    return y
+
+
+@torch.library.custom_op("basal::fp8_block_linear_residual", mutates_args=())
+def fp8_block_linear_residual(x: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor], residual: Tensor) -> Tensor:
+    """residual + (x [M, K] through an FP8-block weight, + bias) -> [M, N] in x's dtype, the sum in the GEMM's
+    epilogue (torch's roundings: the linear's output cast, then the sum cast)."""
+    return _block_linear_residual(x, w, ws, bias, residual, False)
+
+
+@fp8_block_linear_residual.register_fake
+def _(x, w, ws, bias, residual):
+    return x.new_empty((x.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("basal::int8_block_linear_residual", mutates_args=())
+def int8_block_linear_residual(x: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor], residual: Tensor) -> Tensor:
+    """The INT8 format of fp8_block_linear_residual."""
+    return _block_linear_residual(x, w, ws, bias, residual, True)
+
+
+@int8_block_linear_residual.register_fake
+def _(x, w, ws, bias, residual):
+    return x.new_empty((x.shape[0], w.shape[0]))
 
 
 @torch.library.custom_op("basal::int8_block_linear", mutates_args=())

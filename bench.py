@@ -455,6 +455,21 @@ def run_sweep(fmts):
                               "fused_us": round(tf, 2), "unfused_us": round(tu, 2),
                               "fused_tflops": round(2 * M * 2 * I * K / tf / 1e6, 1)}), flush=True)
         fmts = [f for f in fmts if f != "glu"]
+    if "res" in fmts:
+        # C2's o projection (2048 -> 2048) added to the residual stream: the addition in the GEMM's epilogue
+        # (basal::fp8_block_linear_residual) against the linear and torch's addition, and the plain linear alone
+        K, N = 2048, 2048
+        qr, sr = b2.fp8block.quantize(torch.randn(N, K, device=dev, generator=gen) * 0.02)
+        for M in (16, 1024, 8192, 77431):
+            x = torch.randn(M, K, device=dev, generator=gen).bfloat16()
+            hres = torch.randn(M, N, device=dev, generator=gen).bfloat16()
+            tf = graph_us(lambda: (flush.sum(), b2.fp8block.FORMAT.linear_residual(x, qr, sr, None, hres))) - base
+            tu = graph_us(lambda: (flush.sum(), hres + b2.fp8block.linear(x, qr, sr))) - base
+            tl = graph_us(lambda: (flush.sum(), b2.fp8block.linear(x, qr, sr))) - base
+            print(json.dumps({"sweep": "residual linear (C2 o projection + residual)", "M": M, "N": N, "K": K,
+                              "fused_us": round(tf, 2), "unfused_us": round(tu, 2), "linear_alone_us": round(tl, 2)}),
+                  flush=True)
+        fmts = [f for f in fmts if f != "res"]
     if "readout" in fmts:
         # C4's readout: h [256, 2048] bf16 ~ N(0, 1) at the answer positions, a 151,936-row bf16 head ~ N(0, 0.02),
         # one code set of k ids shared by all rows; the device part (code_logits + code_probs) per call
@@ -617,7 +632,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
     ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout, "
-                    "glu) instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
+                    "glu,res) instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
     args = ap.parse_args()
     if args.sweep == "tp":  # under torchrun, 2 or more GPUs
         import datetime

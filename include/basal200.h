@@ -126,6 +126,28 @@ int basal200_int8_block_linear_glu(const void* x, int x_dtype, const int8_t* w, 
  * M > 64. Pure: no device call. */
 int64_t basal200_block_linear_glu_workspace_bytes(int64_t M, int64_t I, int64_t K);
 
+/* A linear whose output is added to the residual stream in the same kernel: y [M, N] = residual [M, N] + (x W^T
+ * (+ bias)), x, residual and y of x_dtype (bf16 or fp16), with torch's roundings (the linear's output cast, + bias,
+ * the sum cast) -- the pair "linear, then h + out" of a pre-norm decoder layer's output projections (the Qwen 3.5
+ * graph's MLP down, linear-attention out and attention o projections, basal/gdn_graph.py:128, :439, :466), which
+ * the reference runs as two kernels. y may be the residual itself (in place).
+ * The activation quantiser goes to the scratch as for basal200_fp8_block_linear; few rows (M <= 64) with
+ * basal200_block_linear_residual_workspace_bytes(M, N, K) of workspace run the few-rows linear into a temporary,
+ * then the addition (the same bits). N % 128 == 0, K % 128 == 0. No counterpart in the reference. */
+int basal200_fp8_block_linear_residual(const void* x, int x_dtype, const uint8_t* w, const float* ws,
+                                       const void* bias, const void* residual, void* y, int64_t M, int64_t N,
+                                       int64_t K, uint8_t* q_scratch, float* s_scratch, void* workspace,
+                                       int64_t workspace_bytes, void* stream);
+
+/* The INT8 format of the same (int8block.py:349-350). */
+int basal200_int8_block_linear_residual(const void* x, int x_dtype, const int8_t* w, const float* ws,
+                                        const void* bias, const void* residual, void* y, int64_t M, int64_t N,
+                                        int64_t K, int8_t* q_scratch, float* s_scratch, void* workspace,
+                                        int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes (16-byte aligned) for the few-rows path of the residual linears; 0 for M > 64. Pure. */
+int64_t basal200_block_linear_residual_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)
 

@@ -32,7 +32,8 @@ def test_every_declared_symbol_is_exported(lib):
 def test_binding_covers_the_header():
     from basal_b200 import _lib
     bound = set(_lib.SIGNATURES) | {"basal200_status_string", "basal200_version", "basal200_device_faults",
-                                    "basal200_block_gemm_workspace_bytes", "basal200_block_linear_glu_workspace_bytes"}
+                                    "basal200_block_gemm_workspace_bytes", "basal200_block_linear_glu_workspace_bytes",
+                                    "basal200_block_linear_residual_workspace_bytes"}
     assert bound == set(declared())
 
 
@@ -72,6 +73,12 @@ def test_argument_checks_before_device_work(lib):
     gws = lib.basal200_block_linear_glu_workspace_bytes
     assert gws(16, 6144, 2048) == 16 * 12288 * 2 and gws(65, 6144, 2048) == 0
     assert gws(16, 1024, 2048) == 16 * 2048 * 2 + 16 * 2048 * 16 * 4  # plus the split products
+    # residual linear: N not a multiple of 128; fp32 activations; M = 0 is an empty success
+    rl = lib.basal200_fp8_block_linear_residual
+    assert rl(null, 0, null, null, null, null, null, 4, 200, 256, null, null, null, 0, null) == 2
+    assert rl(null, 2, null, null, null, null, null, 4, 256, 256, null, null, null, 0, null) == 4
+    assert rl(null, 0, null, null, null, null, null, 0, 256, 256, null, null, null, 0, null) == 0
+    assert lib.basal200_block_linear_residual_workspace_bytes(16, 2048, 2048) == 16 * 2048 * 2 + 16 * 2048 * 16 * 4
     # readout: Kmax beyond 1024
     assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
 

@@ -318,3 +318,45 @@ def test_gated_linear_module_and_refusals(b2):
         layer.glu(x, "relu")
     with pytest.raises(ValueError):
         torch.ops.basal.fp8_block_linear_glu(x.reshape(21, 512), layer.weight[:384], layer.weight_scale[:3], "silu")
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+@pytest.mark.parametrize("M, N, K, dt, with_bias", [(1, 256, 256, torch.bfloat16, False),
+                                                    (16, 2048, 2048, torch.bfloat16, True),
+                                                    (64, 384, 1024, torch.float16, False),
+                                                    (300, 384, 512, torch.bfloat16, True),
+                                                    (1000, 2048, 1024, torch.float16, True)])
+def test_residual_linear_equals_linear_then_add(b2, fmt, M, N, K, dt, with_bias):
+    """residual + linear(x) with the sum in the GEMM's epilogue (many rows: the residual tile TMA-loaded into the
+    staging buffer; few rows: the few-rows linear into a temporary, then the addition) is bit for bit the linear
+    followed by torch's addition, with and without bias, N % 256 = 128 (a half tile past N), bf16 and fp16."""
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).to(dt).cuda()
+    h = torch.randn(M, N, generator=g).to(dt).cuda()
+    bias = torch.randn(N, generator=g).to(dt).cuda() if with_bias else None
+    m = mod(b2, fmt)
+    q, s = m.quantize((torch.randn(N, K, generator=g) * 0.02).cuda())
+    got = m.FORMAT.linear_residual(x, q, s, bias, h)
+    want = h + m.linear(x, q, s, bias)
+    assert torch.equal(got, want), (got.float() - want.float()).abs().max()
+    assert b2._lib.device_faults(0) == 0
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "int8"])
+def test_residual_linear_in_place(b2, fmt):
+    """Through the C ABI with y = the residual (h += o_proj(x)) and no workspace: the many-rows kernel reads each
+    residual tile before its output tile is stored, so the update in place equals the two-step result."""
+    from basal_b200 import _lib
+    M, N, K = 300, 640, 512
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    h = torch.randn(M, N, generator=g).bfloat16().cuda()
+    m = mod(b2, fmt)
+    q, s = m.quantize((torch.randn(N, K, generator=g) * 0.02).cuda())
+    want = h + m.linear(x, q, s)
+    qs = torch.empty(M, K, dtype=torch.uint8, device="cuda")
+    ss = torch.empty(M, K // 128, dtype=torch.float32, device="cuda")
+    name = "basal200_int8_block_linear_residual" if fmt == "int8" else "basal200_fp8_block_linear_residual"
+    _lib.call(name, x.device, _lib.ptr(x), _lib.BF16, _lib.ptr(q), _lib.ptr(s), None, _lib.ptr(h), _lib.ptr(h),
+              M, N, K, _lib.ptr(qs), _lib.ptr(ss), None, 0)
+    assert torch.equal(h, want)
