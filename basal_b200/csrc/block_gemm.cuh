@@ -500,24 +500,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t res_phase = 0;    // residual epilogue: tiles of this warpgroup so far (the rfull phase)
     bool res_pending = false;  // the issuer's residual load not yet waited for
     const int res_kb = nkb / 2;  // the slice at whose start the residual tile is requested (mid-tile: time to land)
+    // this thread's activation-scale row and weight-scale block of a tile
+    auto scale_rows = [&](int t, const float*& srow, const float*& wsr) {
+      const int tm = t / p.tiles_n, tn = t - tm * p.tiles_n;
+      const int n0 = ACT != kActNone ? tn * 128 : tn * BN + half * 128;
+      srow = p.s + (int64_t)min(tm * BM + r, p.M - 1) * nkb;
+      const int wblk = ACT != kActNone ? (half ? p.glu_up / 128 + tn : tn) : min(n0 / 128, p.N / 128 - 1);
+      wsr = p.ws + (int64_t)wblk * nkb;
+    };
+    // the first slice's scales of the next tile are loaded during the last slice of this one (not at its start,
+    // where their round trip would hold up the promotion of slice 0)
+    float sa_next = 0.0f, sb_next = 0.0f;
+    if ((int)blockIdx.x < p.num_tiles) {
+      const float *sr0, *ws0;
+      scale_rows(blockIdx.x, sr0, ws0);
+      sa_next = __ldg(sr0);
+      sb_next = __ldg(ws0);
+    }
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int tm = tile / p.tiles_n, tn = tile - tm * p.tiles_n;
       const int row = tm * BM + r;
       const int n0 = ACT != kActNone ? tn * 128 : tn * BN + half * 128;  // gated: the output columns of the tile
       const bool nvalid = n0 < p.N;
-      const float* srow = p.s + (int64_t)min(row, p.M - 1) * nkb;
-      const int wblk = ACT != kActNone ? (half ? p.glu_up / 128 + tn : tn) : min(n0 / 128, p.N / 128 - 1);
-      const float* wsr = p.ws + (int64_t)wblk * nkb;
+      const float *srow, *wsr;
+      scale_rows(tile, srow, wsr);
       uint64_t acc[64];  // 128 fp32 accumulators as packed pairs
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0ull;
-      float sa = __ldg(srow), sb = __ldg(wsr);
+      float sa = sa_next, sb = sb_next;
       for (int kb = 0; ok && kb < nkb; ++kb) {
         const float sc = sa * sb;
         const uint64_t sc2 = pack_f2(sc, sc);
         if (kb + 1 < nkb) {
           sa = __ldg(srow + kb + 1);
           sb = __ldg(wsr + kb + 1);
+        } else if (tile + (int)gridDim.x < p.num_tiles) {
+          const float *srn, *wsn;
+          scale_rows(tile + gridDim.x, srn, wsn);
+          sa_next = __ldg(srn);
+          sb_next = __ldg(wsn);
         }
         if (RES && kb == res_kb && issuer) {  // the residual tile into this half's staging sub-tiles
           tma_store_wait_read();  // the previous tile's stores have read them
