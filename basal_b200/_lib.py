@@ -28,7 +28,7 @@ SIGNATURES = {
     "basal200_fp8_block_quantize": [_P, _I, _I64, _I64, _P, _P, _P],
     "basal200_int8_block_quantize": [_P, _I, _I64, _I64, _P, _P, _P],
     "basal200_fp8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I64, _P],
-    "basal200_fp8_block_gemm_gather": [_P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I64, _I64, _I64, _P],
+    "basal200_fp8_block_gemm_gather": [_P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I64, _I64, _I64, _P, _P],
     "basal200_peer_barrier": [_P, _I, _I, _I64, _P],
     "basal200_int8_block_gemm": [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I64, _P],
     "basal200_fp8_block_linear": [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],

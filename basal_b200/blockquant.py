@@ -24,9 +24,8 @@ TILES = dict(BM=128, BN=256, BK=128, STAGES=4)
 
 
 def fits(lin):
-    """True for a weight a block format can hold: both dimensions multiples of 128."""
-    n, k = lin.weight.shape
-    return n % BLOCK == 0 and k % BLOCK == 0
+    """True for a weight a block format can hold: whole 128 x 128 blocks."""
+    return all(d % BLOCK == 0 for d in lin.weight.shape)
 
 
 def grid(M, N, config=TILES):
@@ -38,13 +37,16 @@ def grid(M, N, config=TILES):
 
 
 def fuse(mods):
-    """One weight for several linear layers that read the same input: their weights concatenated, the layers'
-    own weights become views of it -> (weight, output sizes) (basal/blockquant.py:43-51)."""
-    w = torch.cat([m.weight.detach() for m in mods])
-    sizes = [m.weight.shape[0] for m in mods]
-    for m, part in zip(mods, w.split(sizes)):
-        m.weight = torch.nn.Parameter(part, requires_grad=False)
-    return w, sizes
+    """One weight for several linear layers that read the same input -> (merged weight, each layer's output count).
+    The merged weight stacks the layers' weights by output rows; afterwards each layer's weight is a frozen view of
+    its rows of it, so no second copy is held (basal/blockquant.py:43-51)."""
+    sizes = [int(m.weight.shape[0]) for m in mods]
+    merged = torch.cat([m.weight.detach() for m in mods], dim=0)
+    start = 0
+    for m, rows in zip(mods, sizes):
+        m.weight = torch.nn.Parameter(merged.narrow(0, start, rows), requires_grad=False)
+        start += rows
+    return merged, sizes
 
 
 def _on_gpu(t):
@@ -110,27 +112,31 @@ class BlockFormat:
 
 
 class BlockLinear(torch.nn.Module):
-    """A linear layer with a block-scaled weight of a format (the subclass's FORMAT) and an optional bias; part(o, n)
-    is a view of output rows o..o + n (multiples of 128)."""
+    """A linear layer with a block-scaled weight of a format (the subclass's FORMAT) and an optional bias.
+
+    weight [N, K] codes and weight_scale [N / 128, K / 128] are frozen parameters; part(o, n) is a layer over output
+    rows o..o + n (multiples of 128) whose tensors are views of this one's."""
 
     FORMAT = None
 
     def __init__(self, weight, scale, bias=None):
         super().__init__()
-        self.weight = torch.nn.Parameter(weight, requires_grad=False)
-        self.weight_scale = torch.nn.Parameter(scale, requires_grad=False)
+        for name, t in (("weight", weight), ("weight_scale", scale)):
+            setattr(self, name, torch.nn.Parameter(t, requires_grad=False))
         self.bias = bias
-        self.out_features, self.in_features = weight.shape
+        self.out_features, self.in_features = (int(d) for d in weight.shape)
 
     @classmethod
     def of(cls, lin):
         """The block-scaled version of a torch.nn.Linear (the bf16 weight is not kept)."""
-        q, s = cls.FORMAT.quantize(lin.weight.detach())
-        return cls(q, s, None if lin.bias is None else lin.bias.detach())
+        bias = lin.bias.detach() if lin.bias is not None else None
+        return cls(*cls.FORMAT.quantize(lin.weight.detach()), bias)
 
     def part(self, o, n):
-        return type(self)(self.weight[o: o + n], self.weight_scale[o // BLOCK: (o + n) // BLOCK],
-                          None if self.bias is None else self.bias[o: o + n])
+        rows = slice(o, o + n)
+        blocks = slice(o // BLOCK, (o + n) // BLOCK)
+        return type(self)(self.weight[rows], self.weight_scale[blocks], self.bias[rows] if self.bias is not None
+                          else None)
 
     def forward(self, x):
         return self.FORMAT.linear(x, self.weight, self.weight_scale, self.bias)

@@ -304,7 +304,7 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
 template <bool INT8, int OUT, int NT>
 int small_gemm_launch(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
                       void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
-                      cudaStream_t st) {
+                      cudaStream_t st, const uint32_t* gate = nullptr) {
   auto kern = smallgemm::small_gemm_kernel<INT8, OUT, NT>;
   constexpr size_t smem = smallgemm::smem_bytes<NT>();
   const int slot = kSlotSmall + (INT8 ? 6 : 0) + OUT * 2 + (NT == 32 ? 0 : 1);
@@ -324,15 +324,17 @@ int small_gemm_launch(int dev, const void* q, const float* s, const void* w, con
   p.M = (int)M;
   p.N = (int)N;
   p.nkb = (int)(K / 128);
+  p.gate = gate;
   return launch_pdl(kern, (unsigned)(N / smallgemm::BW), smallgemm::Cfg<NT>::THREADS, smem, st, tw, tt, p);
 }
 
 template <bool INT8, int OUT>
 int small_gemm(int dev, const void* q, const float* s, const void* w, const float* ws, const void* bias,
                void* const* cs, int npeers, int64_t ldc, int col_off, int64_t M, int64_t N, int64_t K,
-               cudaStream_t st) {
-  if (M <= 32) return small_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st);
-  return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st);
+               cudaStream_t st, const uint32_t* gate = nullptr) {
+  if (M <= 32)
+    return small_gemm_launch<INT8, OUT, 32>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st, gate);
+  return small_gemm_launch<INT8, OUT, 64>(dev, q, s, w, ws, bias, cs, npeers, ldc, col_off, M, N, K, st, gate);
 }
 
 // Few rows and fewer weight tiles than this: the split kernels (every SM streams weights), when the caller's
@@ -487,8 +489,10 @@ int block_gemm(const void* q, const float* s, const void* w, const float* ws, co
 // The FP8 block GEMM of one rank's column shard of a column-parallel linear (N of n_total weight rows, from column
 // col_off), its tiles stored into every rank's [M, n_total] output (outs: npeers device pointers, peer-mapped):
 // the linear's all-gather done by the GEMM's own stores, tile by tile, with no collective kernel. 16-bit outputs.
+// pad: this rank's peer-barrier pad (or null); when its status word is set, the kernel stores nothing.
 int block_gemm_gather(const void* q, const float* s, const void* w, const float* ws, void* const* outs, int npeers,
-                      int64_t col_off, int64_t n_total, int ct, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+                      int64_t col_off, int64_t n_total, int ct, int64_t M, int64_t N, int64_t K, const uint32_t* pad,
+                      cudaStream_t st) {
   if (M < 0 || N <= 0 || K <= 0 || npeers < 1 || npeers > blockgemm::kMaxPeers || !outs) return BASAL200_ERR_ARG;
   if (N % 128 || K % 128 || col_off % 128 || col_off + N > n_total) return BASAL200_ERR_SHAPE;
   if (ct != BASAL200_BF16 && ct != BASAL200_F16) return BASAL200_ERR_DTYPE;
@@ -498,14 +502,17 @@ int block_gemm_gather(const void* q, const float* s, const void* w, const float*
   for (int r = 0; r < npeers; ++r)
     if (!outs[r] || !aligned16(outs[r])) return BASAL200_ERR_ALIGN;
   if (M > (int64_t)1 << 30 || n_total > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
+  if (pad && (reinterpret_cast<uintptr_t>(pad) & 3)) return BASAL200_ERR_ALIGN;
+  static_assert(blockgemm::kPadStatus == BASAL200_PAD_STATUS_WORD, "the pad layout of include/basal200.h");
+  const uint32_t* gate = pad ? pad + blockgemm::kPadStatus : nullptr;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   if (M <= smallgemm::MAX_ROWS && K / 128 <= smallgemm::MAX_KB && N / smallgemm::BW <= 65535) {
     if (ct == BASAL200_BF16)
       return small_gemm<false, BASAL200_BF16>(dev, q, s, w, ws, nullptr, outs, npeers, n_total, (int)col_off, M, N, K,
-                                              st);
+                                              st, gate);
     return small_gemm<false, BASAL200_F16>(dev, q, s, w, ws, nullptr, outs, npeers, n_total, (int)col_off, M, N, K,
-                                           st);
+                                           st, gate);
   }
   CUtensorMap ta, tb;
   blockgemm::OutMaps out;
@@ -526,6 +533,7 @@ int block_gemm_gather(const void* q, const float* s, const void* w, const float*
   p.npeers = npeers;
   p.col_off = (int)col_off;
   p.glu_up = 0;
+  p.gate = gate;
   const int64_t tiles = (M + blockgemm::BM - 1) / blockgemm::BM * p.tiles_n;
   if (tiles > INT32_MAX) return BASAL200_ERR_LIMIT;
   p.num_tiles = (int)tiles;
@@ -893,8 +901,9 @@ int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, 
 
 int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
                                    void* const* outs, int npeers, int64_t col_off, int64_t n_total, int c_dtype,
-                                   int64_t M, int64_t N, int64_t K, void* stream) {
-  return block_gemm_gather(q, s, w, ws, outs, npeers, col_off, n_total, c_dtype, M, N, K, as_stream(stream));
+                                   int64_t M, int64_t N, int64_t K, const uint32_t* barrier_pad, void* stream) {
+  return block_gemm_gather(q, s, w, ws, outs, npeers, col_off, n_total, c_dtype, M, N, K, barrier_pad,
+                           as_stream(stream));
 }
 
 int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t timeout_ns, void* stream) {

@@ -76,7 +76,16 @@ struct Params {
   int npeers;       // 16-bit outputs: the output buffers the tiles are stored into (OutMaps), 1 or, for a column-
   int col_off;      // parallel linear gathered on the fly, every rank's [M, n_total] output, at column col_off
   int glu_up;       // gated linear (ACT != 0): the weight rows [gate; up] with up from row glu_up (= the output width)
+  const uint32_t* gate = nullptr;  // gathered linear: this rank's peer-barrier status word (or null); non-zero = store nothing
 };
+
+// The number of output buffers a GEMM stores into: none when the peer barrier before a gathered GEMM recorded a
+// timeout (a rank that missed the barrier must not write into a peer's output while the peer may still read it).
+// Read after pdl_wait: the barrier kernel has completed and its store is visible.
+__device__ __forceinline__ int stored_peers(int npeers, const uint32_t* gate) {
+  if (gate && *reinterpret_cast<const volatile uint32_t*>(gate) != 0u) return 0;
+  return npeers;
+}
 
 // Gated-linear activations of the fused gate/up epilogue, in fp32 on the 16-bit-rounded gate, with the formulas and
 // operation order of torch's CUDA kernels (so that the cast result matches the unfused ops'): silu(x) = x / (1 +
@@ -100,9 +109,13 @@ struct OutMaps {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Peer barrier over peer-mapped signal pads: word r of rank q's pad holds the last call number rank r reached, word
-// kMaxPeers this rank's own call count. Thread r stores the call number into rank r's pad (release, system scope)
-// and waits for rank r's (acquire), giving up after timeout_ns with a fault bit.
+// kMaxPeers this rank's own call count, word kPadStatus a sticky status (0 = every barrier so far completed).
+// Thread r stores the call number into rank r's pad (release, system scope) and waits for rank r's (acquire), giving
+// up after timeout_ns with a fault bit. A rank whose status is set (a wait of this or an earlier call gave up, or a
+// peer's did) writes it into every peer's status word too, so every rank's gathered GEMMs stop storing and every
+// rank's host sees the failure.
 // ---------------------------------------------------------------------------------------------------------------
+constexpr int kPadStatus = kMaxPeers + 1;
 struct PeerPads {
   uint32_t* p[kMaxPeers];
 };
@@ -125,6 +138,9 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerPads pads, i
   }
   __syncthreads();
   const int r = threadIdx.x;
+  __shared__ int timed_out;
+  if (r == 0) timed_out = 0;
+  __syncthreads();
   if (r < world) {
     __threadfence_system();
     st_release_sys(pads.p[r] + rank, call);
@@ -132,11 +148,16 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerPads pads, i
     while ((int)(ld_acquire_sys(pads.p[rank] + r) - call) < 0) {
       if (globaltimer() - t0 > (unsigned long long)timeout_ns) {
         atomicOr(&g_fault, kFaultTimeoutPeer);
+        timed_out = 1;
         break;
       }
     }
   }
   __syncthreads();
+  if (timed_out && r == 0) pads.p[rank][kPadStatus] = 1u;
+  __syncthreads();
+  const uint32_t status = *reinterpret_cast<volatile uint32_t*>(pads.p[rank] + kPadStatus);
+  if (status != 0u && r < world && r != rank) st_release_sys(pads.p[r] + kPadStatus, status);
 }
 
 // Bounded drain wait (the abort flag is already set when it runs).
@@ -495,6 +516,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int r = quad * 32 + lane;  // row within the tile
     const bool issuer = (ew & 3) == 0 && lane == 0;
     const int nkb = p.nkb;
+    const int npeers = stored_peers(p.npeers, p.gate);  // after pdl_wait (above)
     uint32_t acc_cnt = 0;
     bool ok = true;
     uint32_t res_phase = 0;    // residual epilogue: tiles of this warpgroup so far (the rfull phase)
@@ -597,7 +619,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         fence_proxy_async();
         named_barrier(5, 256);  // both halves have read the exchanged values and written the output tile
         if (half == 0 && issuer) {
-          for (int q = 0; q < p.npeers; ++q) {
+          for (int q = 0; q < npeers; ++q) {
             tma_store_2d(&out.m[q], sh.out[0], p.col_off + n0, tm * BM);
             tma_store_2d(&out.m[q], sh.out[1], p.col_off + n0 + 64, tm * BM);
           }
@@ -640,7 +662,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         named_barrier(1 + half, 128);
         if (issuer) {
           if (nvalid) {
-            for (int r = 0; r < p.npeers; ++r) {
+            for (int r = 0; r < npeers; ++r) {
               tma_store_2d(&out.m[r], sh.out[half * 2], p.col_off + n0, tm * BM);
               tma_store_2d(&out.m[r], sh.out[half * 2 + 1], p.col_off + n0 + 64, tm * BM);
             }

@@ -83,6 +83,7 @@ struct Params {
   int64_t ldc;
   int col_off;
   int M, N, nkb;
+  const uint32_t* gate = nullptr;  // gathered linear: this rank's peer-barrier status word (or null); non-zero = store nothing
 };
 
 // One bf16 / f16 / f32 output, with the bias added to the cast value and rounded again (as blockgemm::Store).
@@ -234,6 +235,7 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
       // every a_s * b_s of the tile, while the first slices load (token j's scales are contiguous); the scales and
       // this thread's stores come after the kernels before this one
       pdl_wait();
+      const int npeers = blockgemm::stored_peers(p.npeers, p.gate);
       for (int idx = et; idx < NT * nkb; idx += ETHREADS) {
         const int j = idx / nkb, kb = idx - j * nkb;
         sh.sc[kb][j] = j < p.M ? __ldg(p.s + (int64_t)j * nkb + kb) * __ldg(p.ws + (int64_t)tile * nkb + kb) : 0.f;
@@ -274,7 +276,7 @@ __global__ void __launch_bounds__(Cfg<NT>::THREADS, 1)
         for (int j = 0; j < 32; j += 2) {
           const float2 v = unpack_f2(acc[j / 2]);
           const int tok = half * 32 + j;
-          for (int r = 0; r < p.npeers; ++r) {
+          for (int r = 0; r < npeers; ++r) {
             if (tok < p.M) store1<OUT>(p.cs[r], (int64_t)tok * p.ldc + p.col_off + n, v.x, p.bias, n);
             if (tok + 1 < p.M) store1<OUT>(p.cs[r], (int64_t)(tok + 1) * p.ldc + p.col_off + n, v.y, p.bias, n);
           }
@@ -602,9 +604,10 @@ __global__ void __launch_bounds__(REDUCE_THREADS)
   for (int kb = 0; kb < MAX_KB; ++kb)
     if (kb < nkb) acc = __fmaf_rn(pv[kb], sc[kb], acc);
   const int n = tile * BW + row;
+  const int npeers = blockgemm::stored_peers(p.npeers, p.gate);
 #pragma unroll
   for (int r = 0; r < blockgemm::kMaxPeers; ++r)  // constant indices keep the parameter block out of local memory
-    if (r < p.npeers) store1<OUT>(p.cs[r], (int64_t)tok * p.ldc + p.col_off + n, acc, p.bias, n);
+    if (r < npeers) store1<OUT>(p.cs[r], (int64_t)tok * p.ldc + p.col_off + n, acc, p.bias, n);
 }
 
 }  // namespace smallgemm

@@ -1,10 +1,10 @@
 """The torch ops of the hot path, under the reference's names where it has them, each a thin call of libbasal200.
 
   basal::fp8_block_gemm(q, s, w, ws, dtype)      reference op, basal/blockquant.py:151-159 (FP8 format)
-  basal::int8_block_gemm(q, s, w, ws, dtype)     reference op, same, INT8 format (int8block.py:349)
+  basal::int8_block_gemm(q, s, w, ws, dtype)     reference op, same, INT8 format (int8block.py:43)
   basal::nvfp4_linear(x, w, ws, alpha, inv_g)    reference op, basal/nvfp4.py:183-194
   basal::fp8_block_linear(x, w, ws, bias)        act_quant + GEMM (+ bias): what fp8block.linear computes
-                                                 (fp8block.py:285-296); takes the place of basal::fp8_block_linear_sm90
+                                                 (fp8block.py:74-85); takes the place of basal::fp8_block_linear_sm90
   basal::int8_block_linear(x, w, ws, bias)       the same for INT8 (BlockFormat.linear, blockquant.py:175-183)
   basal::fp8_block_linear_glu(x, w, ws, act), basal::int8_block_linear_glu(...)
                                                  act(gate) * up of a merged [gate; up] weight in one GEMM: what

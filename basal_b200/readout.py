@@ -18,32 +18,30 @@ from . import ops
 WROWS_BYTES = 64 << 20  # what an engine's code-row cache may hold (here: the ids, 8 bytes a code)
 
 
-def _nbytes(x):
-    if x is None:
-        return 0
+def _size(x):
+    """Bytes held by a cache entry: a tensor, None, or a tuple of them."""
     if isinstance(x, tuple):
-        return sum(_nbytes(y) for y in x)
-    return int(x.nbytes)
+        return sum(map(_size, x))
+    return 0 if x is None else int(x.nbytes)
 
 
 def code_rows(cache, key, make):
-    """cache[key], made by make() when missing; the most recently used entries within WROWS_BYTES are kept
+    """cache[key], made by make() when missing. The cache (a dict: insertion order = use order, newest last) keeps
+    the most recently used entries whose bytes fit within WROWS_BYTES; the entry just used always stays
     (basal/readout.py:23-36)."""
-    w = cache.pop(key, None)
-    if w is None:
-        w = make()
-    cache[key] = w
-    total = sum(_nbytes(x) for x in cache.values())
-    for old in list(cache):
-        if total <= WROWS_BYTES or old == key:
-            break
-        total -= _nbytes(cache.pop(old))
-    return w
+    entry = cache.pop(key) if key in cache else make()
+    cache[key] = entry
+    excess = sum(_size(v) for v in cache.values()) - WROWS_BYTES
+    while excess > 0 and len(cache) > 1:
+        excess -= _size(cache.pop(next(iter(cache))))
+    return entry
 
 
 def capped(z, softcap):
     """The model's final logit soft cap (Gemma: softcap x tanh(z / softcap)), applied once; none: z as it is."""
-    return torch.tanh(z / softcap) * softcap if softcap else z
+    if not softcap:
+        return z
+    return softcap * torch.tanh(z / softcap)
 
 
 class CodeReadout:
@@ -55,16 +53,18 @@ class CodeReadout:
         self.to_dev = to_dev or (lambda x: x.to(head.weight.device))
 
     def rows(self, lids):
-        key = tuple(sorted({i for ids in lids for i in ids}))
-
-        def make():
-            return self.to_dev(torch.tensor(key, dtype=torch.int64)), None
-        rows = code_rows(self.cache, key, make)
-        col = {t: j for j, t in enumerate(key)}
-        K = max(map(len, lids))
-        idx = self.to_dev(torch.tensor([[col[i] for i in ids] + [0] * (K - len(ids)) for ids in lids]))
-        pad = self.to_dev(torch.tensor([[False] * len(ids) + [True] * (K - len(ids)) for ids in lids]))
-        return rows, idx, pad
+        """(rows, idx, pad) for prompts whose option ids are lids: rows = (the sorted union of the ids on the device,
+        None); idx [n, widest] = each prompt's columns into that union, pad = True past a prompt's own count."""
+        union = tuple(sorted(set().union(*lids)))
+        rows = code_rows(self.cache, union, lambda: (self.to_dev(torch.tensor(union, dtype=torch.int64)), None))
+        column = {code: j for j, code in enumerate(union)}
+        width = max(len(ids) for ids in lids)
+        idx = torch.zeros(len(lids), width, dtype=torch.int64)
+        pad = torch.ones(len(lids), width, dtype=torch.bool)
+        for r, ids in enumerate(lids):
+            idx[r, :len(ids)] = torch.tensor([column[i] for i in ids], dtype=torch.int64)
+            pad[r, :len(ids)] = False
+        return rows, self.to_dev(idx), self.to_dev(pad)
 
     def logits(self, h, rows):
         ids, _ = rows

@@ -4,7 +4,7 @@ The reference serves several GPUs as independent replicas behind its router (bas
 never exchange data, so the hot path shards by rows with no collective. This module holds the host side of that:
 
   varlen_lengths(n, lo, hi, seed)   the seeded request lengths of a workload (torch.randint, inclusive hi)
-  cu_seqlens(lengths)               packed-row offsets of varlen requests (the compact rows of engine.py:1469-1475)
+  cu_seqlens(lengths)               packed-row offsets of varlen requests (the compact rows of engine.py:1470-1475)
   shard_range(n, world, rank)       the contiguous block of request indices rank `rank` serves
   max_over_ranks(x, group)          the slowest rank's time (all-reduce MAX), the bench's clock for N > 1
   sum_over_ranks(x, group)          the units all ranks processed
@@ -90,6 +90,7 @@ def check_peers(group=None, timeout_s=30.0, tag="peers"):
 # column shards
 # ---------------------------------------------------------------------------------------------------------------
 MAX_PEERS = 8  # output buffers one gathered GEMM stores into (libbasal200's limit)
+PAD_STATUS_WORD = 9  # BASAL200_PAD_STATUS_WORD: the sticky status word of a peer-barrier pad
 
 
 def column_shard(n, world, rank, unit=128):
@@ -111,7 +112,12 @@ class ColumnShardedFP8Linear(torch.nn.Module):
                        signal pads: before, every rank is done with the previous output; after, every rank's
                        columns have landed; a wait gives up after timeout_ms with a fault bit, never a trap). The
                        result is a view of the shared buffer, valid until the next forward of this module on any rank
-                       (clone to keep it). It can be captured in a CUDA graph.
+                       (clone to keep it). It can be captured in a CUDA graph. Once a barrier has given up on any
+                       rank, every rank's gathered GEMM stores nothing (a late rank must not overwrite a peer's
+                       output), and check() raises.
+      check()          synchronises the device and raises RuntimeError when a barrier of this module gave up on
+                       this rank or a peer (the pad's sticky status word) or a bounded wait recorded a fault bit:
+                       the outputs since the failure are not to be used.
       forward_nccl(x)  the baseline: the shard's own linear, an NCCL all-gather, the copy that interleaves the
                        ranks' columns.
 
@@ -172,9 +178,23 @@ class ColumnShardedFP8Linear(torch.nn.Module):
         _lib.call("basal200_peer_barrier", x.device, self._pads, self.world, self.rank, tmo)
         _lib.call("basal200_fp8_block_gemm_gather", x.device, _lib.ptr(q), _lib.ptr(s), _lib.ptr(w.weight),
                   _lib.ptr(w.weight_scale), outs, self.world, self.col_off, self.out_features, _lib.code(x.dtype),
-                  M, w.out_features, self.in_features)
+                  M, w.out_features, self.in_features, self._pads[self.rank])
         _lib.call("basal200_peer_barrier", x.device, self._pads, self.world, self.rank, tmo)
         return buf[:M].view(*shape[:-1], self.out_features)
+
+    def check(self):
+        """Raises RuntimeError when a peer barrier of this module gave up (on this rank or on a peer) or a bounded
+        wait of a kernel on this device recorded a fault bit; synchronises the device (not for the hot path)."""
+        from . import _lib
+        if self._hdl is None:
+            return
+        dev = self._buf.device
+        torch.cuda.synchronize(dev)
+        status = int(self._hdl.get_signal_pad(self._hdl.rank, (16,), dtype=torch.int32)[PAD_STATUS_WORD].item())
+        faults = _lib.device_faults(dev.index if dev.index is not None else 0, clear=False)
+        if status or faults:
+            raise RuntimeError(f"ColumnShardedFP8Linear (rank {self.rank}): a peer barrier gave up (status {status}, "
+                               f"fault bits {faults}); the gathered outputs since then are incomplete")
 
     def forward_nccl(self, x):
         shape = x.shape

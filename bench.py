@@ -9,15 +9,16 @@ TFLOP/s (2 M N K summed over the projections), whole job: with N GPUs every rank
 shards of independent requests, no collective; "weak" scaling) and the value is all ranks' FLOPs over the slowest
 rank's device time. One JSON line on rank 0 with, besides the contract keys:
   roofline      the FP8 block GEMM (the dominant kernel): achieved TFLOP/s from CUDA events around its launches in
-                the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200), the sustained
-                figure since the GEMM runs inside a long power-capped step (the burst fraction is reported beside it)
+                the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200): the burst
+                figure, unless the clock samples of the timed region show the power cap active (then the sustained
+                figure, the one measured under that cap); the fraction of the other figure is reported beside it
   e2e           the same metric through the public API (BlockFP8Linear modules) from pinned host memory: the H2D copy
                 of the step's activations and the D2H copy of its four outputs inside the timed region, on their
                 own streams so that the two PCIe directions and the GPU work of neighbouring steps overlap
   cpu_baseline  the reference's CPU maths (oracle/, numpy + BLAS on all host threads) on a bounded sample of rows
   clocks        nvidia-smi samples taken during the timed region
 --impl reference times the reference's CPU implementation of the path (the oracle port) on this box's host cores
-(the reference has no native code and no GPU path of its own for B200 besides Triton), rank 0 only.
+(the reference has no native code, and its only B200 GPU path is a Triton kernel), rank 0 only.
 """
 import argparse
 import json
@@ -71,7 +72,7 @@ def flops_per_row():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 100 ms while running (started before, stopped after the timed
+    """nvidia-smi clock / throttle samples every 20 ms while running (started before, stopped after the timed
     region)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -83,7 +84,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -127,7 +128,7 @@ def cpu_sample(rows, seed=0):
 
 def cpu_step(xs, ws):
     """One step of the reference's CPU path: per projection, act_quant_ops + reference() (both operands dequantised
-    every call, an fp32 matmul), as fp8block.linear runs on CPU tensors (basal/fp8block.py:285-296)."""
+    every call, an fp32 matmul), as fp8block.linear runs on CPU tensors (basal/fp8block.py:74-85)."""
     from oracle import blockquant as obq
     out = []
     for name, n, k in PROJ:
@@ -318,8 +319,11 @@ def run_ours(args, rank, world, local_rank):
 
     gemm_flops = sum(2 * M * n * k for _, n, k in PROJ)
     achieved = gemm_flops / (sum(gemm_ms) * 1e-3) / 1e12
-    peak = 2.0 * pk["bf16_tflops_sustained"]
-    peak_burst = 2.0 * pk["bf16_tflops"]
+    # the denominator follows the clocks sampled in the timed region: the sustained peak was measured under the
+    # power cap, the burst peak at full clock; a region the cap did not touch is held to the burst figure
+    capped = "sw_power_cap" in clocks.get("reasons", [])
+    peak_burst, peak_sust = 2.0 * pk["bf16_tflops"], 2.0 * pk["bf16_tflops_sustained"]
+    peak = peak_sust if capped else peak_burst
     traffic = profiled_traffic()
     if rank == 0:
         cpu = cpu_baseline() if world == 1 else None
@@ -333,9 +337,12 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "basal200 fp8 block GEMM (tcgen05 kind::f8f6f4)",
-                         "peak_source": f"2 x bf16_tflops_sustained of {pk['source']} peaks (FP8 dense = 2 x bf16 "
-                                        "dense; the GEMM is timed inside a long power-capped step)",
+                         "peak_source": (f"2 x {'bf16_tflops_sustained' if capped else 'bf16_tflops'} of "
+                                         f"{pk['source']} peaks (FP8 dense = 2 x bf16 dense; "
+                                         f"{'sw_power_cap active' if capped else 'no power cap'} in the clock "
+                                         "samples of the timed region)"),
                          "frac_of_burst_peak": round(achieved / peak_burst, 4),
+                         "frac_of_sustained_peak": round(achieved / peak_sust, 4),
                          "per_projection_tflops": {name: round(2 * M * n * k / (t * 1e-3) / 1e12, 1)
                                                    for (name, n, k), t in zip(PROJ, gemm_ms)},
                          "o_k4096_tflops": round(o4_tflops, 1)},

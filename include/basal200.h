@@ -35,10 +35,10 @@ enum { BASAL200_BF16 = 0, BASAL200_F16 = 1, BASAL200_F32 = 2 };
 /* ---- FP8-block / INT8-block (128 x 128 weight blocks, 1 x 128 activation groups, fp32 scales) ---- */
 
 /* x [M, K] (x_dtype) -> q [M, K] e4m3 codes, s [M, K/128] fp32. K % 128 == 0. Bit-exact to
- * BlockFormat.act_quant_ops of the FP8 format (basal/blockquant.py:118-123, :137-144; fp8block.py:241-242). */
+ * BlockFormat.act_quant_ops of the FP8 format (basal/blockquant.py:118-123, :137-144; fp8block.py:30-31). */
 int basal200_fp8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, uint8_t* q, float* s, void* stream);
 
-/* The INT8 format (int8block.py:349-350): q int8, round half to even, +-127. */
+/* The INT8 format (int8block.py:43-44): q int8, round half to even, +-127. */
 int basal200_int8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* q, float* s, void* stream);
 
 /* w [N, K] (w_dtype) -> q [N, K] e4m3, s [N/128, K/128] fp32. Bit-exact to BlockFormat.quantize
@@ -46,7 +46,7 @@ int basal200_int8_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, in
 int basal200_fp8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* q, float* s,
                                 void* stream);
 
-/* The INT8 format of the same (int8block.py:349-350). */
+/* The INT8 format of the same (int8block.py:43-44). */
 int basal200_int8_block_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* q, float* s,
                                  void* stream);
 
@@ -69,19 +69,28 @@ int basal200_fp8_block_gemm(const uint8_t* q, const float* s, const uint8_t* w, 
  * "fp8_block_gemm of the shard, then all-gather of the outputs"): the shard's [M, N] result (its weight rows are the
  * linear's rows col_off .. col_off + N - 1) is stored into each of the npeers buffers outs[r] ([M, n_total], c_dtype
  * bf16 or fp16, row-major, peer-mapped device memory of every rank), at columns col_off .. col_off + N - 1, by the
- * GEMM's own stores. The caller synchronises the ranks afterwards. N, col_off multiples of 128; npeers <= 8. */
+ * GEMM's own stores. The caller synchronises the ranks afterwards. N, col_off multiples of 128; npeers <= 8.
+ * barrier_pad: this rank's pad of basal200_peer_barrier (4-byte aligned), or NULL. When the pad's status word says
+ * that a barrier gave up, the GEMM stores nothing at all, so a rank that missed a barrier never writes into a peer's
+ * output while that peer may still be reading it. */
 int basal200_fp8_block_gemm_gather(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
                                    void* const* outs, int npeers, int64_t col_off, int64_t n_total, int c_dtype,
-                                   int64_t M, int64_t N, int64_t K, void* stream);
+                                   int64_t M, int64_t N, int64_t K, const uint32_t* barrier_pad, void* stream);
 
-/* A barrier of the `world` ranks that share peer-mapped signal pads (pads[r]: rank r's pad, at least 9 uint32 words,
+/* Word of a barrier pad that holds its sticky status: 0 while every barrier completed; non-zero once a wait of this
+ * rank gave up, or a peer's did (a rank whose status is set writes it into every peer's pad at each barrier). The
+ * host reads it to raise an error; it stays set until the caller zeroes it with every rank idle. */
+#define BASAL200_PAD_STATUS_WORD 9
+
+/* A barrier of the `world` ranks that share peer-mapped signal pads (pads[r]: rank r's pad, at least 10 uint32 words,
  * zero before the first call, used by nothing else): enqueued on `stream`, it returns (on the device) once every rank
  * has reached the same call, with each rank's stream work before it visible to the others' work after it. A wait
- * for a rank gives up after timeout_ns: the kernel records BASAL200_FAULT_TIMEOUT_PEER and ends (no trap). The call
- * count lives in the pad, so a captured CUDA graph may replay the barrier. world <= 8. */
+ * for a rank gives up after timeout_ns: the kernel records BASAL200_FAULT_TIMEOUT_PEER, sets the pad's status word
+ * (BASAL200_PAD_STATUS_WORD) and ends (no trap). The call count lives in the pad, so a captured CUDA graph may replay
+ * the barrier. world <= 8. */
 int basal200_peer_barrier(uint32_t* const* pads, int world, int rank, int64_t timeout_ns, void* stream);
 
-/* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:349): each slice's product exact in int32. */
+/* basal::int8_block_gemm (basal/blockquant.py:95-96, int8block.py:43): each slice's product exact in int32. */
 int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, const float* ws, const void* bias,
                              void* c, int c_dtype, int64_t M, int64_t N, int64_t K, void* workspace,
                              int64_t workspace_bytes, void* stream);
@@ -90,13 +99,13 @@ int basal200_int8_block_gemm(const int8_t* q, const float* s, const int8_t* w, c
  * then the block GEMM into y [M, N] (y_dtype = x_dtype), + bias; workspace as for basal200_fp8_block_gemm. When the
  * workspace makes the GEMM split and x is bf16 or fp16, the quantiser runs inside the GEMM kernel instead (one launch
  * fewer; q_scratch is then not written, s_scratch is, and every bit of y and s_scratch is the same). Replaces
- * fp8block.linear / BlockFormat.linear (basal/fp8block.py:285-296, basal/blockquant.py:175-183) and the op
- * basal::fp8_block_linear_sm90 (fp8block.py:272-277). */
+ * fp8block.linear / BlockFormat.linear (basal/fp8block.py:74-85, basal/blockquant.py:175-183) and the op
+ * basal::fp8_block_linear_sm90 (fp8block.py:61-71). */
 int basal200_fp8_block_linear(const void* x, int x_dtype, const uint8_t* w, const float* ws, const void* bias,
                               void* y, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch, float* s_scratch,
                               void* workspace, int64_t workspace_bytes, void* stream);
 
-/* int8block.linear (int8block.py:350 = BlockFormat.linear, basal/blockquant.py:175-183). */
+/* int8block.linear (int8block.py:44 = BlockFormat.linear, basal/blockquant.py:175-183). */
 int basal200_int8_block_linear(const void* x, int x_dtype, const int8_t* w, const float* ws, const void* bias,
                                void* y, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                void* workspace, int64_t workspace_bytes, void* stream);
@@ -116,7 +125,7 @@ int basal200_fp8_block_linear_glu(const void* x, int x_dtype, const uint8_t* w, 
                                   int64_t I, int64_t K, int act, uint8_t* q_scratch, float* s_scratch, void* workspace,
                                   int64_t workspace_bytes, void* stream);
 
-/* The INT8 format of the same (int8block.py:349-350). */
+/* The INT8 format of the same (int8block.py:43-44). */
 int basal200_int8_block_linear_glu(const void* x, int x_dtype, const int8_t* w, const float* ws, void* y, int64_t M,
                                    int64_t I, int64_t K, int act, int8_t* q_scratch, float* s_scratch,
                                    void* workspace, int64_t workspace_bytes, void* stream);
@@ -139,7 +148,7 @@ int basal200_fp8_block_linear_residual(const void* x, int x_dtype, const uint8_t
                                        int64_t K, uint8_t* q_scratch, float* s_scratch, void* workspace,
                                        int64_t workspace_bytes, void* stream);
 
-/* The INT8 format of the same (int8block.py:349-350). */
+/* The INT8 format of the same (int8block.py:43-44). */
 int basal200_int8_block_linear_residual(const void* x, int x_dtype, const int8_t* w, const float* ws,
                                         const void* bias, const void* residual, void* y, int64_t M, int64_t N,
                                         int64_t K, int8_t* q_scratch, float* s_scratch, void* workspace,
@@ -157,7 +166,8 @@ int64_t basal200_block_linear_residual_workspace_bytes(int64_t M, int64_t N, int
  * array inside the library (16 MiB + 512 KiB, BASAL200_NOALLOC_MAX_ELEMS values), which every GPU that loads the
  * library holds until the process exits. M * K above that limit returns BASAL200_ERR_LIMIT before any work. The
  * call allocates nothing. Its first call on a device looks up the array's address on that device (with the device
- * current): make that first call before any stream capture. All calls on a device share the array, so calls that
+ * current) and keeps it for the life of the process: make that first call before any stream capture, and do not
+ * call it on a device after cudaDeviceReset (the kept address would then name memory of the destroyed context). All calls on a device share the array, so calls that
  * overlap on the GPU (other streams, other threads) race on it; serialise them. No counterpart in the reference. */
 int basal200_fp8_block_linear_noalloc(const void* x, int x_dtype, const uint8_t* w, const float* ws,
                                       const void* bias, void* y, int64_t M, int64_t N, int64_t K, void* stream);

@@ -7,8 +7,8 @@ Restates basal/blockquant.py (rkinas/basal 2.8.1):
   gemm(q, s, w, ws)        reference(), blockquant.py:54-60: both operands dequantised, one fp32 matmul
   linear(x, w, ws, fmt)    BlockFormat.linear on the CPU, blockquant.py:175-183 (act_quant + gemm + bias)
 
-The formats: FP8 = e4m3 within +-448, saturated then cast (fp8block.py:239-241); INT8 = within +-127 rounded to the
-nearest integer, ties to even (int8block.py:327, :349). Scales are amax clamped to >= 1e-12, then / qmax, in fp32.
+The formats: FP8 = e4m3 within +-448, saturated then cast (fp8block.py:28-30); INT8 = within +-127 rounded to the
+nearest integer, ties to even (int8block.py:21, :43). Scales are amax clamped to >= 1e-12, then / qmax, in fp32.
 All divisions are IEEE fp32 divisions, as torch's CPU kernels do them.
 """
 import numpy as np
@@ -79,7 +79,7 @@ def gemm(q, s, w, ws, fmt):
 
 def linear(x, w, ws, fmt, bias=None):
     """x [M, K] fp32 through a block-scaled weight -> fp32 [M, N] before the cast to x's dtype
-    (blockquant.py:175-183, fp8block.py:285-296 on the CPU)."""
+    (blockquant.py:175-183, fp8block.py:74-85 on the CPU)."""
     q, s = act_quant(x, fmt)
     y = gemm(q, s, w, ws, fmt)
     if bias is not None:

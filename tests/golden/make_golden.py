@@ -5,7 +5,7 @@
 Every array here is an output of the reference's own CPU functions on seeded inputs:
   blockquant.npz  BlockFormat.act_quant_ops / quantize / reference (basal/blockquant.py:54-60, :118-135) for the FP8
                   (fp8block.FORMAT) and INT8 (int8block.FORMAT) formats, and fp8block.linear / int8block.linear on the
-                  CPU (fp8block.py:285-296, blockquant.py:175-183)
+                  CPU (fp8block.py:74-85, blockquant.py:175-183)
   nvfp4.npz       nvfp4._act_ops, swizzle, quantize, NVFP4Linear.of + forward on the CPU (basal/nvfp4.py:49-112,
                   :197-245), the code table of tests/test_nvfp4.py:13-15
   readout.npz     CodeReadout.probs / probs_each (basal/readout.py:81-104), with and without bias and soft cap
@@ -69,7 +69,7 @@ def make_blockquant(bq, fp8block, int8block):
         out[f"{name}_actf_q"], out[f"{name}_actf_s"] = u8(q), s.numpy()
         wq, ws = f.quantize(w)
         out[f"{name}_w_q"], out[f"{name}_w_s"] = u8(wq), ws.numpy()
-    # the GEMM's maths at a small shape (the GPU tests cover tests/test_fp8block.py:211-225 against this oracle): M=37, K=512, N=256
+    # the GEMM's maths at a small shape (the GPU tests cover tests/test_fp8block.py:134-148 against this oracle): M=37, K=512, N=256
     g = torch.Generator().manual_seed(2)
     xa = bf16_exact(torch.randn(37, 512, generator=g))
     wb = bf16_exact(torch.randn(256, 512, generator=g) / 32)

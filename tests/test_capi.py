@@ -60,10 +60,11 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_nvfp4_act_quant(null, 0, null, 4, 96, null, null, null) == 2
     # column-parallel GEMM with gathered outputs: no output buffer; a shard past the full width; fp32 output
     outs = (ctypes.c_void_p * 2)(None, None)
-    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 0, 0, 256, 0, 4, 128, 256, null) == 1
-    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 256, 256, 0, 4, 128, 256, null) == 2
-    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 2, 4, 128, 256, null) == 4
-    assert lib.basal200_fp8_block_gemm_gather(null, null, null, null, outs, 2, 0, 256, 0, 0, 128, 256, null) == 0
+    gather = lib.basal200_fp8_block_gemm_gather
+    assert gather(null, null, null, null, outs, 0, 0, 256, 0, 4, 128, 256, null, null) == 1
+    assert gather(null, null, null, null, outs, 2, 256, 256, 0, 4, 128, 256, null, null) == 2
+    assert gather(null, null, null, null, outs, 2, 0, 256, 2, 4, 128, 256, null, null) == 4
+    assert gather(null, null, null, null, outs, 2, 0, 256, 0, 0, 128, 256, null, null) == 0
     # gated linear: an unknown activation; I not a multiple of 128; fp32 activations; M = 0 is an empty success
     glu = lib.basal200_fp8_block_linear_glu
     assert glu(null, 0, null, null, null, 4, 256, 256, 3, null, null, null, 0, null) == 1
@@ -81,6 +82,14 @@ def test_argument_checks_before_device_work(lib):
     assert lib.basal200_block_linear_residual_workspace_bytes(16, 2048, 2048) == 16 * 2048 * 2 + 16 * 2048 * 16 * 4
     # readout: Kmax beyond 1024
     assert lib.basal200_code_probs(null, 1, 1, null, null, 2000, null, null) == 8
+    # the allocation-free linear: one row past its array's limit is refused before any pointer is looked at or any
+    # device call is made (null pointers here); M = 0 is an empty success
+    noalloc = lib.basal200_fp8_block_linear_noalloc
+    limit = 1 << 24  # BASAL200_NOALLOC_MAX_ELEMS
+    assert noalloc(null, 0, null, null, null, null, limit // 2048 + 1, 256, 2048, null) == 8
+    assert noalloc(null, 0, null, null, null, null, 1, 256, limit + 128, null) == 8
+    assert noalloc(null, 0, null, null, null, null, 0, 256, 2048, null) == 0
+    assert b"limit" in lib.basal200_status_string(8)
 
 
 def test_split_workspace_sizes(lib):

@@ -1,5 +1,5 @@
 """The tcgen05 block GEMM (FP8 kind::f8f6f4, INT8 kind::i8) against the oracle's maths (basal/blockquant.py:54-60),
-the reference's own GPU tests restated (tests/test_fp8block.py:211-225, tests/test_int8block.py:308-321: the maths
+the reference's own GPU tests restated (tests/test_fp8block.py:134-148, tests/test_int8block.py:71-84: the maths
 within 2e-3 (FP8) / 1e-5 (INT8), a row's output bit-identical alone and among other rows), the bf16 output within
 1e-2 relative, the edge cases (M = 0, partial tiles, N % 256 = 128, bias) and the full
 C2 projection shapes through row samples."""
@@ -55,7 +55,7 @@ def test_gemm_equals_the_maths(b2, fmt, M, N, K):
 @pytest.mark.parametrize("fmt", ["fp8", "int8"])
 @pytest.mark.parametrize("M", [1, 37, 128, 1000])
 def test_kernel_ignores_the_other_rows(b2, fmt, M):
-    """tests/test_fp8block.py:211-225: a row's output alone and among other rows, bit for bit."""
+    """tests/test_fp8block.py:134-148: a row's output alone and among other rows, bit for bit."""
     x, q, s, qa, sa = operands(b2, fmt, M, 768, 1024)
     m = mod(b2, fmt)
     alone = m.gemm(qa[-1:], sa[-1:], q, s, torch.bfloat16)

@@ -30,7 +30,7 @@ def test_formats_share_one_core(b2):
 
 
 def test_grid_refuses_partial_output_tiles(b2):
-    """tests/test_fp8block.py:106-115: N not a multiple of 128 is refused; the count is of 128 x 256 tiles here."""
+    """tests/test_fp8block.py:29-38: N not a multiple of 128 is refused; the count is of 128 x 256 tiles here."""
     g = b2.blockquant.grid
     assert g(1, 384) == (2,) and g(129, 384) == (4,) and g(0, 128) == (0,) and g(1, 256) == (1,)
     for n in (200, 64):

@@ -1,7 +1,7 @@
 """The CPU oracle (oracle/) against the golden fixtures the reference itself wrote (tests/golden/make_golden.py):
 codes and scales bit for bit, GEMM / linear / readout outputs to fp32 rounding. Also the reference's own
 known-answer tests for this path (tests/test_nvfp4.py:13-23, tests/test_blockquant.py:55-68,
-tests/test_fp8block.py:93-103, tests/test_int8block.py:14-22) restated on the oracle. No GPU."""
+tests/test_fp8block.py:16-26, tests/test_int8block.py:14-22) restated on the oracle. No GPU."""
 import numpy as np
 import pytest
 
@@ -50,7 +50,7 @@ def test_gemm_and_linear(gb, fmt):
 
 def test_known_answers_block_formats(gb):
     """Every block reaches qmax exactly; FP8 error within |w| 2^-4 + s 2^-9, INT8 within half a step
-    (tests/test_fp8block.py:93-103, tests/test_int8block.py:14-22)."""
+    (tests/test_fp8block.py:16-26, tests/test_int8block.py:14-22)."""
     w = gb["w"]
     for fmt, qmax in (("fp8", 448.0), ("int8", 127.0)):
         q, s = bq.quantize(w, fmt)

@@ -2,8 +2,9 @@
 that plans all device memory up front, a host language without a device allocator of its own, a caller that must not
 let cudaMalloc synchronise the device mid-request): called through the C ABI and compared with the allocating entry
 point basal200_fp8_block_linear on the same inputs, for two calls in a row (the second call finds the first call's
-codes in the library's shared array), plus its size limit. Collected last on purpose: it needs nothing from the other
-test files and runs the same alone in a fresh process."""
+codes in the library's shared array), on the large-M kernel and on the few-rows kernel (M = 16). Its size limit is
+checked without a GPU in test_capi.py (the refusal comes before any device call). Collected last on purpose: it
+needs nothing from the other test files and runs the same alone in a fresh process."""
 import ctypes
 
 import pytest
@@ -11,7 +12,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-BF16, ERR_LIMIT = 0, 8
+BF16 = 0
 MAX_ELEMS = 1 << 24  # BASAL200_NOALLOC_MAX_ELEMS of include/basal200.h
 
 
@@ -56,7 +57,8 @@ def _noalloc(lib, x, w, ws, bias, M, N, K):
 
 def test_noalloc_matches_the_allocating_linear_on_two_calls_in_a_row(lib):
     torch.manual_seed(0)
-    cases = [(1000, 768, 1024, None), (4096, 2048, 4096, torch.randn(2048, device="cuda").bfloat16())]
+    cases = [(1000, 768, 1024, None), (4096, 2048, 4096, torch.randn(2048, device="cuda").bfloat16()),
+             (16, 2048, 2048, None), (16, 1280, 6144, torch.randn(1280, device="cuda").bfloat16())]
     for i, (M, N, K, bias) in enumerate(cases):
         x = torch.randn(M, K, device="cuda").bfloat16()
         w, ws = _weight(N, K, seed=i)
@@ -68,12 +70,12 @@ def test_noalloc_matches_the_allocating_linear_on_two_calls_in_a_row(lib):
         assert torch.equal(got, want)  # the same two kernels on the same inputs: the same bits
 
 
-def test_noalloc_refuses_sizes_beyond_its_array(lib):
+def test_noalloc_runs_at_the_small_end_and_at_its_limit(lib):
+    """One row, and exactly BASAL200_NOALLOC_MAX_ELEMS activation values (M * K at the limit), both within bounds."""
     w, ws = _weight(256, 2048, seed=3)
-    M = MAX_ELEMS // 2048 + 1
-    y = torch.empty(1, 256, dtype=torch.bfloat16, device="cuda")
-    x = torch.empty(1, 2048, dtype=torch.bfloat16, device="cuda")
-    rc = lib.basal200_fp8_block_linear_noalloc(_p(x), BF16, _p(w), _p(ws), None, _p(y), M, 256, 2048, _stream())
-    assert rc == ERR_LIMIT
-    assert b"limit" in lib.basal200_status_string(rc)
-    assert _noalloc(lib, x, w, ws, None, 1, 256, 2048).shape == (1, 256)  # at the limit's small end it still runs
+    x = torch.randn(1, 2048, device="cuda").bfloat16()
+    assert torch.equal(_noalloc(lib, x, w, ws, None, 1, 256, 2048), _allocating(lib, x, w, ws, None, 1, 256, 2048))
+    M = MAX_ELEMS // 2048
+    x = torch.randn(M, 2048, device="cuda").bfloat16()
+    got = _noalloc(lib, x, w, ws, None, M, 256, 2048)
+    assert torch.equal(got, _allocating(lib, x, w, ws, None, M, 256, 2048))
