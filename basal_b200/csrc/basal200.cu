@@ -11,6 +11,7 @@
 #include "nvfp4_gemm.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
+#include "hybrid.cuh"
 
 namespace b200 {
 namespace {
@@ -708,15 +709,16 @@ int glu_rows_launch(const void* t, void* y, int64_t M, int64_t I, int act, cudaS
                     I);
 }
 
+// codes: q / s already hold x's activation codes and scales (the entry points that take codes); x is not read.
 template <bool INT8>
 int block_linear_glu(const void* x, int xt, const void* w, const float* ws, void* y, int64_t M, int64_t I, int64_t K,
-                     int act, void* q, float* s, void* work, int64_t work_bytes, cudaStream_t st) {
+                     int act, void* q, float* s, void* work, int64_t work_bytes, cudaStream_t st, bool codes = false) {
   if (M < 0 || I <= 0 || K <= 0) return BASAL200_ERR_ARG;
   if (act != BASAL200_ACT_SILU && act != BASAL200_ACT_GELU_TANH) return BASAL200_ERR_ARG;
   if (I % 128 || K % 128) return BASAL200_ERR_SHAPE;
   if (xt != BASAL200_BF16 && xt != BASAL200_F16) return BASAL200_ERR_DTYPE;
   if (M == 0) return BASAL200_OK;
-  if (!x || !w || !ws || !y || !q || !s) return BASAL200_ERR_ARG;
+  if ((!x && !codes) || !w || !ws || !y || !q || !s) return BASAL200_ERR_ARG;
   if (!aligned16(w) || !aligned16(y) || !aligned16(q)) return BASAL200_ERR_ALIGN;
   if (M > (int64_t)1 << 30 || I > (int64_t)1 << 29) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
@@ -727,7 +729,9 @@ int block_linear_glu(const void* x, int xt, const void* w, const float* ws, void
     uint8_t* temp = static_cast<uint8_t*>(work);
     uint8_t* split = temp + glu_temp_bytes(M, I);
     const int64_t split_bytes = work_bytes - glu_temp_bytes(M, I);
-    if (INT8)
+    if (codes)
+      rc = block_gemm<INT8>(q, s, w, ws, nullptr, temp, xt, M, 2 * I, K, split, split_bytes, st);
+    else if (INT8)
       rc = basal200_int8_block_linear(x, xt, static_cast<const int8_t*>(w), ws, nullptr, temp, M, 2 * I, K,
                                       static_cast<int8_t*>(q), s, split, split_bytes, st);
     else
@@ -737,7 +741,7 @@ int block_linear_glu(const void* x, int xt, const void* w, const float* ws, void
     return xt == BASAL200_BF16 ? glu_rows_launch<BASAL200_BF16>(temp, y, M, I, act, st)
                                : glu_rows_launch<BASAL200_F16>(temp, y, M, I, act, st);
   }
-  if ((rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
+  if (!codes && (rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
   CUtensorMap ta, tb;
   blockgemm::OutMaps out;
   memset(&out, 0, sizeof(out));
@@ -775,12 +779,12 @@ int64_t res_workspace(int64_t M, int64_t N, int64_t K) {
 template <bool INT8>
 int block_linear_residual(const void* x, int xt, const void* w, const float* ws, const void* bias, const void* res,
                           void* y, int64_t M, int64_t N, int64_t K, void* q, float* s, void* work, int64_t work_bytes,
-                          cudaStream_t st) {
+                          cudaStream_t st, bool codes = false) {
   if (M < 0 || N <= 0 || K <= 0) return BASAL200_ERR_ARG;
   if (N % 128 || K % 128) return BASAL200_ERR_SHAPE;
   if (xt != BASAL200_BF16 && xt != BASAL200_F16) return BASAL200_ERR_DTYPE;
   if (M == 0) return BASAL200_OK;
-  if (!x || !w || !ws || !res || !y || !q || !s) return BASAL200_ERR_ARG;
+  if ((!x && !codes) || !w || !ws || !res || !y || !q || !s) return BASAL200_ERR_ARG;
   if (!aligned16(w) || !aligned16(y) || !aligned16(res) || !aligned16(q) || (bias && !aligned16(bias)))
     return BASAL200_ERR_ALIGN;
   if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return BASAL200_ERR_LIMIT;
@@ -792,7 +796,9 @@ int block_linear_residual(const void* x, int xt, const void* w, const float* ws,
     uint8_t* temp = static_cast<uint8_t*>(work);
     uint8_t* split = temp + res_temp_bytes(M, N);
     const int64_t split_bytes = work_bytes - res_temp_bytes(M, N);
-    if (INT8)
+    if (codes)
+      rc = block_gemm<INT8>(q, s, w, ws, bias, temp, xt, M, N, K, split, split_bytes, st);
+    else if (INT8)
       rc = basal200_int8_block_linear(x, xt, static_cast<const int8_t*>(w), ws, bias, temp, M, N, K,
                                       static_cast<int8_t*>(q), s, split, split_bytes, st);
     else
@@ -806,7 +812,7 @@ int block_linear_residual(const void* x, int xt, const void* w, const float* ws,
     return launch_pdl(blockgemm::add_rows_kernel<BASAL200_F16>, (unsigned)grid, 256, 0, st,
                       static_cast<const void*>(temp), res, y, M * N);
   }
-  if ((rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
+  if (!codes && (rc = act_quant<INT8>(x, xt, M, K, q, s, st))) return rc;
   CUtensorMap ta, tb;
   blockgemm::OutMaps out;
   memset(&out, 0, sizeof(out));
@@ -832,6 +838,96 @@ int block_linear_residual(const void* x, int xt, const void* w, const float* ws,
   if (xt == BASAL200_BF16)
     return block_gemm_launch<INT8, BASAL200_BF16, blockgemm::kActNone, true>(dev, ta, tb, out, p, st);
   return block_gemm_launch<INT8, BASAL200_F16, blockgemm::kActNone, true>(dev, ta, tb, out, p, st);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// The config-5 hybrid decoder's element-wise steps (hybrid.cuh)
+// ------------------------------------------------------------------------------------------------------------
+int rms_quant(const void* x, int xt, const void* w, float eps, int64_t M, int64_t D, void* y, uint8_t* q, float* s,
+              cudaStream_t st) {
+  if (M < 0 || D <= 0 || !(eps >= 0.0f)) return BASAL200_ERR_ARG;
+  if (D % 128) return BASAL200_ERR_SHAPE;
+  if (xt != BASAL200_BF16 && xt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (M == 0) return BASAL200_OK;
+  if (!x || !w || !q || !s) return BASAL200_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(q) || (y && !aligned16(y)) || (reinterpret_cast<uintptr_t>(s) & 3))
+    return BASAL200_ERR_ALIGN;
+  if (D > ((int64_t)1 << 20) || M > ((int64_t)1 << 34)) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t grid = (M + 7) / 8;  // a warp per row, 8 a CTA
+  if (grid > INT32_MAX) return BASAL200_ERR_LIMIT;
+  if (xt == BASAL200_BF16)
+    return launch_pdl(hybrid::rms_quant_kernel<__nv_bfloat16>, (unsigned)grid, 256, 0, st,
+                      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps, M, (int)D,
+                      static_cast<__nv_bfloat16*>(y), q, s);
+  return launch_pdl(hybrid::rms_quant_kernel<__half>, (unsigned)grid, 256, 0, st, static_cast<const __half*>(x),
+                    static_cast<const __half*>(w), eps, M, (int)D, static_cast<__half*>(y), q, s);
+}
+
+int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_rows, const void* conv, int kw,
+             const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk, int Hv, float* q,
+             float* k, float* v, float* beta, float* g, cudaStream_t st) {
+  if (rows < 0 || T < 0 || Hk <= 0 || Hv <= 0 || kw < 1 || kw > 8) return BASAL200_ERR_ARG;
+  if (Hv % Hk) return BASAL200_ERR_SHAPE;
+  if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (rows == 0 || T == 0) return BASAL200_OK;
+  if (!proj || !conv || !A_log || !dt_bias || !q || !k || !v || !beta || !g) return BASAL200_ERR_ARG;
+  if (tail && tail_rows != 1 && tail_rows != rows) return BASAL200_ERR_ARG;
+  const int64_t C = (int64_t)(2 * Hk + Hv) * 128;
+  if (ld < C || b_off < 0 || a_off < 0 || b_off + Hv > ld || a_off + Hv > ld) return BASAL200_ERR_SHAPE;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return BASAL200_ERR_ALIGN;
+  const int64_t items = (int64_t)rows * T * Hk;  // a warp each, 8 a CTA
+  if ((items + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  hybrid::PrepParams p;
+  p.proj = proj;
+  p.ld = ld;
+  p.tail = tail;
+  p.tail_rows = tail_rows;
+  p.conv = conv;
+  p.A_log = A_log;
+  p.dt_bias = dt_bias;
+  p.b_off = b_off;
+  p.a_off = a_off;
+  p.rows = rows;
+  p.T = T;
+  p.Hk = Hk;
+  p.Hv = Hv;
+  p.KW = kw;
+  p.q_scale = 0.08838834764831845f;  // 128^-1/2, rounded to fp32 as torch rounds the Python float
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.beta = beta;
+  p.g = g;
+  const unsigned grid = (unsigned)((items + 7) / 8);
+  if (dt == BASAL200_BF16) return launch_pdl(hybrid::gdn_prep_kernel<__nv_bfloat16>, grid, 256, 0, st, p);
+  return launch_pdl(hybrid::gdn_prep_kernel<__half>, grid, 256, 0, st, p);
+}
+
+int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, int z_off, const void* gw, float eps,
+                   int rows, int T, int Hv, void* y, uint8_t* q, float* s, cudaStream_t st) {
+  if (rows < 0 || T < 0 || Hv <= 0 || Tp < T || !(eps >= 0.0f)) return BASAL200_ERR_ARG;
+  if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (rows == 0 || T == 0) return BASAL200_OK;
+  if (!o || !z || !gw || !q || !s) return BASAL200_ERR_ARG;
+  if (z_off < 0 || z_off + (int64_t)Hv * 128 > ld || (ld % 8) || (z_off % 8)) return BASAL200_ERR_SHAPE;
+  if (!aligned16(o) || !aligned16(z) || !aligned16(gw) || !aligned16(q) || (y && !aligned16(y)) ||
+      (reinterpret_cast<uintptr_t>(s) & 3))
+    return BASAL200_ERR_ALIGN;
+  const int64_t warps = ((int64_t)rows * T * Hv + 1) / 2;  // a half-warp per (token, head)
+  if ((warps + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  if (dt == BASAL200_BF16)
+    return launch_pdl(hybrid::gdn_gate_quant_kernel<__nv_bfloat16>, grid, 256, 0, st, o, Tp,
+                      static_cast<const __nv_bfloat16*>(z), ld, z_off, static_cast<const __nv_bfloat16*>(gw), eps,
+                      rows, T, Hv, static_cast<__nv_bfloat16*>(y), q, s);
+  return launch_pdl(hybrid::gdn_gate_quant_kernel<__half>, grid, 256, 0, st, o, Tp, static_cast<const __half*>(z), ld,
+                    z_off, static_cast<const __half*>(gw), eps, rows, T, Hv, static_cast<__half*>(y), q, s);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -986,6 +1082,38 @@ int basal200_int8_block_linear_glu(const void* x, int x_dtype, const int8_t* w, 
                                    void* workspace, int64_t workspace_bytes, void* stream) {
   return block_linear_glu<true>(x, x_dtype, w, ws, y, M, I, K, act, q_scratch, s_scratch, workspace,
                                 workspace_bytes, as_stream(stream));
+}
+
+int basal200_fp8_block_gemm_glu(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, void* y,
+                                int y_dtype, int64_t M, int64_t I, int64_t K, int act, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  return block_linear_glu<false>(nullptr, y_dtype, w, ws, y, M, I, K, act, const_cast<uint8_t*>(q),
+                                 const_cast<float*>(s), workspace, workspace_bytes, as_stream(stream), true);
+}
+
+int basal200_fp8_block_gemm_residual(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
+                                     const void* bias, const void* residual, void* y, int y_dtype, int64_t M,
+                                     int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream) {
+  return block_linear_residual<false>(nullptr, y_dtype, w, ws, bias, residual, y, M, N, K, const_cast<uint8_t*>(q),
+                                      const_cast<float*>(s), workspace, workspace_bytes, as_stream(stream), true);
+}
+
+int basal200_rms_norm_fp8_quant(const void* x, int x_dtype, const void* w, float eps, int64_t M, int64_t D, void* y,
+                                uint8_t* q, float* s, void* stream) {
+  return rms_quant(x, x_dtype, w, eps, M, D, y, q, s, as_stream(stream));
+}
+
+int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail, int tail_rows, const void* conv,
+                      int kw, const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk,
+                      int Hv, float* q, float* k, float* v, float* beta, float* g, void* stream) {
+  return gdn_prep(proj, dtype, ld, tail, tail_rows, conv, kw, A_log, dt_bias, b_off, a_off, rows, T, Hk, Hv, q, k, v,
+                  beta, g, as_stream(stream));
+}
+
+int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype, int64_t ld, int z_off,
+                                const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
+                                void* stream) {
+  return gdn_gate_quant(o, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing

@@ -1,0 +1,300 @@
+// The config-5 hybrid decoder's element-wise steps around its FP8-block linears, each one kernel that reads the
+// previous step's output once and writes the next GEMM's operand (the maths of the reference's Qwen 3.5 graph forward,
+// basal/gdn_graph.py:122-140, :432-439, with the roundings of its torch ops):
+//
+//   rms_quant_kernel      Qwen3_5RMSNorm (1 + w) of a row, rounded to 16 bits, quantised into 1 x 128 e4m3 groups:
+//                         the A operand (codes, scales) of the next block GEMM, and optionally the normed row itself
+//   gdn_prep_kernel       the Gated DeltaNet's causal depthwise convolution (k taps) + SiLU over the q / k / v
+//                         channels of the merged input projection, rounded to 16 bits, the l2 norms of q and k (q also
+//                         scaled by dk^-1/2), beta = sigmoid(b), g = -e^A_log softplus(a + dt_bias): the recurrence's
+//                         operands, head-major [rows, value heads, T, d] fp32 (key heads repeated for their values)
+//   gdn_gate_quant_kernel the Gated DeltaNet's output: each value head's 128 values rounded to 16 bits, RMS-normed,
+//                         times the norm weight, times SiLU(z), rounded, and quantised as one 1 x 128 group (a head is
+//                         exactly one group of the output projection's input)
+//
+// Every multiply and add that torch rounds on its own is __fmul_rn / __fadd_rn (no contraction into an FMA);
+// exponentials and divisions are expf / __fdiv_rn, as torch's CUDA kernels compute silu, sigmoid and softplus. The
+// sums of squares of the norms are fp32 in this kernel's own order (torch's reduction order is not part of the
+// contract), so a normed value may differ from torch's by one unit in the last place.
+#pragma once
+#include "quant.cuh"
+
+namespace b200 {
+namespace hybrid {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+
+// v rounded to T and back (the value a torch op on T tensors leaves)
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f<T>(from_f<T>(v));
+}
+
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// 8 16-bit values -> fp32
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]) {
+  uint4 w[1];
+  raw_load8(p, w);
+  unpack8(w, p, v);
+}
+
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]) {
+  uint4 u;
+  T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = from_f<T>(v[i]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// RMSNorm + FP8 quantiser: a warp per row of D features (D % 128 == 0). Pass 1 sums the squares (lane l holds the
+// 8-value chunks l, l + 32, ...: 256 consecutive features a warp step, as the quantiser's half-warp groups), pass 2
+// reloads the row (L1 / L2), forms y = RN16(RN(x * r) * RN(1 + w)) with r = rsqrt(mean + eps), and quantises each
+// 128-feature group exactly as act_quant_block_kernel does (half-warp amax, scale = RN(max(amax, 1e-12) / 448),
+// block_codes8), so the codes equal the standalone quantiser's of y.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) rms_quant_kernel(const T* __restrict__ x, const T* __restrict__ w, float eps,
+                                                        int64_t M, int D, T* __restrict__ y,
+                                                        uint8_t* __restrict__ q, float* __restrict__ s) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row < M) {
+    const T* xr = x + row * D;
+    float ss = 0.0f;
+    for (int c = lane * 8; c < D; c += 256) {
+      float v[8];
+      ld8(xr + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    const int groups = D / 128;
+    for (int base = 0; base < D; base += 256) {
+      const int c = base + lane * 8;
+      const bool live = c < D;  // the last step of a D % 256 == 128 row: its upper half-warp has no group
+      float v[8];
+      if (live) {
+        float xv[8], wv[8];
+        ld8(xr + c, xv);
+        ld8(w + c, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = round_to<T>(__fmul_rn(__fmul_rn(xv[i], r), __fadd_rn(1.0f, wv[i])));
+        if (y) st8(y + row * D + c, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+      }
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+      const uint2 codes = block_codes8<false>(v, sc);
+      if (live) {
+        *reinterpret_cast<uint2*>(q + row * D + c) = codes;
+        if ((lane & 15) == 0) s[row * groups + c / 128] = sc;
+      }
+    }
+  }
+  pdl_launch();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Gated DeltaNet input: a warp per (row r, token t, key head h); lane l owns channels 4l .. 4l + 3 of a 128-channel
+// head. proj [rows * T, ld] holds, per token, the convolution's input channels [q (Hk * 128) | k (Hk * 128) | v (Hv *
+// 128)] from column 0, then b at column b_off and a at a_off (one per value head). tail [tr, KW - 1, C] (tr = 1: every
+// row continues the same inputs; tr = rows; null: zeros) holds the KW - 1 inputs before token 0, oldest first.
+// Convolution of channel c at token t: acc = x[t - KW + 1] w[c, 0], then acc = RN(acc + RN(x[t - KW + 1 + j] w[c, j]))
+// for j = 1 .. KW - 1 (torch's order in the unfused form: a product, then a sum, each rounded); y = RN16(silu(acc)).
+// ---------------------------------------------------------------------------------------------------------------
+struct PrepParams {
+  const void* proj;
+  int64_t ld;         // elements between tokens in proj
+  const void* tail;   // [tr, KW - 1, C] or null
+  int tail_rows;      // 1 or rows
+  const void* conv;   // [C, KW] 16-bit
+  const float* A_log; // [Hv]
+  const void* dt_bias;// [Hv] 16-bit
+  int b_off, a_off;   // columns of b and a in proj
+  int rows, T, Hk, Hv, KW;
+  float q_scale;      // dk^-1/2
+  float* q;           // [rows, Hv, T, 128]
+  float* k;
+  float* v;
+  float* beta;        // [rows, Hv, T]
+  float* g;
+};
+
+template <typename T>
+__device__ __forceinline__ float conv_in(const PrepParams& p, int r, int t, int col) {
+  // the convolution input of channel col at token t of row r (t < 0: the tail's, or zero)
+  if (t >= 0) return to_f<T>(static_cast<const T*>(p.proj)[((int64_t)r * p.T + t) * p.ld + col]);
+  if (!p.tail) return 0.0f;
+  const int C = (p.Hk * 2 + p.Hv) * 128;
+  const int tr = p.tail_rows == 1 ? 0 : r;
+  return to_f<T>(static_cast<const T*>(p.tail)[((int64_t)tr * (p.KW - 1) + (p.KW - 1 + t)) * C + col]);
+}
+
+template <typename T>
+__device__ __forceinline__ void conv4(const PrepParams& p, int r, int t, int col0, float (&y)[4]) {
+  const T* cw = static_cast<const T*>(p.conv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int col = col0 + i;
+    float acc = __fmul_rn(conv_in<T>(p, r, t - p.KW + 1, col), to_f<T>(cw[(int64_t)col * p.KW]));
+    for (int j = 1; j < p.KW; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(conv_in<T>(p, r, t - p.KW + 1 + j, col), to_f<T>(cw[(int64_t)col * p.KW + j])));
+    y[i] = round_to<T>(silu_f(acc));
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int64_t items = (int64_t)p.rows * p.T * p.Hk;
+  if (item < items) {
+    const int h = (int)(item % p.Hk);
+    const int t = (int)((item / p.Hk) % p.T);
+    const int r = (int)(item / ((int64_t)p.Hk * p.T));
+    const int c0 = lane * 4;
+    float qv[4], kv[4];
+    conv4<T>(p, r, t, h * 128 + c0, qv);
+    conv4<T>(p, r, t, p.Hk * 128 + h * 128 + c0, kv);
+    float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sq = __fadd_rn(sq, __fmul_rn(qv[i], qv[i]));
+      sk = __fadd_rn(sk, __fmul_rn(kv[i], kv[i]));
+    }
+    const float rq = rsqrtf(__fadd_rn(warp_sum(sq), 1e-6f));
+    const float rk = rsqrtf(__fadd_rn(warp_sum(sk), 1e-6f));
+    float4 qo, ko;
+    qo.x = __fmul_rn(__fmul_rn(qv[0], rq), p.q_scale);
+    qo.y = __fmul_rn(__fmul_rn(qv[1], rq), p.q_scale);
+    qo.z = __fmul_rn(__fmul_rn(qv[2], rq), p.q_scale);
+    qo.w = __fmul_rn(__fmul_rn(qv[3], rq), p.q_scale);
+    ko.x = __fmul_rn(kv[0], rk);
+    ko.y = __fmul_rn(kv[1], rk);
+    ko.z = __fmul_rn(kv[2], rk);
+    ko.w = __fmul_rn(kv[3], rk);
+    const int rep = p.Hv / p.Hk;
+    for (int j = 0; j < rep; ++j) {
+      const int vh = h * rep + j;
+      const int64_t o = (((int64_t)r * p.Hv + vh) * p.T + t) * 128 + c0;
+      *reinterpret_cast<float4*>(p.q + o) = qo;
+      *reinterpret_cast<float4*>(p.k + o) = ko;
+      float vv[4];
+      conv4<T>(p, r, t, 2 * p.Hk * 128 + vh * 128 + c0, vv);
+      *reinterpret_cast<float4*>(p.v + o) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      if (lane == 0) {
+        const T* pr = static_cast<const T*>(p.proj) + ((int64_t)r * p.T + t) * p.ld;
+        const float bb = to_f<T>(pr[p.b_off + vh]);
+        const float aa = to_f<T>(pr[p.a_off + vh]);
+        const int64_t bo = ((int64_t)r * p.Hv + vh) * p.T + t;
+        p.beta[bo] = round_to<T>(sigmoid_f(bb));
+        const float dt = to_f<T>(static_cast<const T*>(p.dt_bias)[vh]);
+        p.g[bo] = __fmul_rn(-expf(p.A_log[vh]), softplus_f(__fadd_rn(aa, dt)));
+      }
+    }
+  }
+  pdl_launch();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Gated DeltaNet output + FP8 quantiser: a half-warp per (token, value head), 8 values a lane. o [rows, Hv, Tp, 128]
+// fp32 (the recurrence's output, Tp >= ntok tokens a row), z in proj (16-bit, row stride ld, column z_off + vh * 128), gw [128]:
+// u = RN16(o); n = RN16(RN(u * rsqrt(mean(u^2) + eps))); n = RN16(RN(gw * n)); out = RN16(RN(n * silu(z)));
+// codes / scale of the 128 values as act_quant_block_kernel's, into q [rows * T, Hv * 128] / s [rows * T, Hv].
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) gdn_gate_quant_kernel(const float* __restrict__ o, int Tp,
+                                                             const T* __restrict__ z, int64_t ld, int z_off,
+                                                             const T* __restrict__ gw, float eps, int rows, int ntok,
+                                                             int Hv, T* __restrict__ y, uint8_t* __restrict__ q,
+                                                             float* __restrict__ s) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 15;
+  const int64_t item = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + (lane >> 4);
+  const int64_t items = (int64_t)rows * ntok * Hv;
+  const bool live = item < items;
+  float v[8];
+  int64_t tok = 0;
+  int vh = 0;
+  if (live) {
+    vh = (int)(item % Hv);
+    tok = item / Hv;  // r * T + t
+    const int t = (int)(tok % ntok), r = (int)(tok / ntok);
+    const float* src = o + (((int64_t)r * Hv + vh) * Tp + t) * 128 + l * 8;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = round_to<T>(v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+#pragma unroll
+  for (int o2 = 8; o2 >= 1; o2 >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o2));
+  const float rr = rsqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), eps));
+  if (live) {
+    float zv[8], wv[8];
+    ld8(z + tok * ld + z_off + vh * 128 + l * 8, zv);
+    ld8(gw + l * 8, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float n = round_to<T>(__fmul_rn(wv[i], round_to<T>(__fmul_rn(v[i], rr))));
+      v[i] = round_to<T>(__fmul_rn(n, silu_f(zv[i])));
+    }
+    if (y) st8(y + tok * (int64_t)Hv * 128 + vh * 128 + l * 8, v);
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o2 = 8; o2 >= 1; o2 >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o2));
+  const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+  const uint2 codes = block_codes8<false>(v, sc);
+  if (live) {
+    *reinterpret_cast<uint2*>(q + tok * (int64_t)Hv * 128 + vh * 128 + l * 8) = codes;
+    if (l == 0) s[tok * Hv + vh] = sc;
+  }
+  pdl_launch();
+}
+
+}  // namespace hybrid
+}  // namespace b200

@@ -125,9 +125,10 @@ def linear(x, w, ws, alpha, inv_g, bias=None):
     """x [..., K] through an NVFP4 weight (codes w [N, K / 2], swizzled scales ws, alpha = the two global scales'
     product, inv_g = 1 / the input's global scale) -> [..., N] in x's dtype."""
     lead, K = x.shape[:-1], x.shape[-1]
-    y = ops.nvfp4_linear(x.reshape(-1, K), w, ws, alpha, inv_g)
-    if bias is not None:
-        y = y + bias.to(y.dtype)
+    if bias is None:
+        y = ops.nvfp4_linear(x.reshape(-1, K), w, ws, alpha, inv_g)
+    else:  # the reference's y + bias.to(y.dtype), with its roundings, inside the GEMM's epilogue
+        y = ops.nvfp4_linear_bias(x.reshape(-1, K), w, ws, alpha, inv_g, bias)
     return y.reshape(*lead, w.shape[0])
 
 

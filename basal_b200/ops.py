@@ -3,6 +3,8 @@
   basal::fp8_block_gemm(q, s, w, ws, dtype)      reference op, basal/blockquant.py:151-159 (FP8 format)
   basal::int8_block_gemm(q, s, w, ws, dtype)     reference op, same, INT8 format (int8block.py:43)
   basal::nvfp4_linear(x, w, ws, alpha, inv_g)    reference op, basal/nvfp4.py:183-194
+  basal::nvfp4_linear_bias(x, w, ws, alpha, inv_g, bias)
+                                                 the same + bias in the epilogue (nvfp4.linear's bias, :211-212)
   basal::fp8_block_linear(x, w, ws, bias)        act_quant + GEMM (+ bias): what fp8block.linear computes
                                                  (fp8block.py:74-85); takes the place of basal::fp8_block_linear_sm90
   basal::int8_block_linear(x, w, ws, bias)       the same for INT8 (BlockFormat.linear, blockquant.py:175-183)
@@ -19,6 +21,13 @@
   basal::nvfp4_gemm(q, s, w, ws, alpha, m, dtype)  nvfp4._mm (nvfp4.py:167-180)
   basal::code_logits(h, head, ids, bias, softcap)  CodeReadout.logits over the option rows (readout.py:71-74)
   basal::code_probs(z, idx, pad)                 CodeReadout.probs_of (readout.py:76-79)
+  basal::fp8_block_gemm_glu(q, s, w, ws, act, dtype), basal::fp8_block_gemm_residual(q, s, w, ws, bias, residual)
+                                                 the gated and residual linears from activation codes
+  basal::rms_norm_fp8_quant(x, w, eps)           a Qwen 3.5 RMSNorm fused with the FP8 quantiser (gdn_graph.py:122-126)
+  basal::gdn_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off)
+                                                 the Gated DeltaNet's convolution, norms and gates (gdn_graph.py:131-140)
+  basal::gdn_gate_fp8_quant(o, proj, z_off, gw, eps, rows, T)
+                                                 its gated output norm fused with the FP8 quantiser (gdn_graph.py:432-438)
 
 Every op is functional (mutates_args=()), allocates its outputs (and scratch) from the caching allocator, enqueues on
 the current stream and never synchronises: Dynamo traces them through their fake kernels and a CUDA graph captures
@@ -296,10 +305,8 @@ def _(q, s, w, ws, alpha, m, dtype):
     return q.new_empty((m, w.shape[0]), dtype=dtype)
 
 
-@torch.library.custom_op("basal::nvfp4_linear", mutates_args=())
-def nvfp4_linear(x: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, inv_g: Tensor) -> Tensor:
-    """x [M, K] -> [M, N] in x's dtype: the quantiser and the GEMM as one op (basal/nvfp4.py:183-189)."""
-    require_cuda(x, w, ws, alpha, inv_g)
+def _nvfp4_linear(x, w, ws, alpha, inv_g, bias):
+    require_cuda(x, w, ws, alpha, inv_g, bias)
     x, w, ws = _c(x), _c(w), _c(ws)
     M, K = x.shape
     N = w.shape[0]
@@ -307,13 +314,34 @@ def nvfp4_linear(x: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, inv_g: Tensor)
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     q = torch.empty((max(Mp, 1), K // 2), dtype=torch.uint8, device=x.device)
     s = torch.empty((max(Mp, 1) * (K // 16),), dtype=torch.uint8, device=x.device)
+    if bias is not None:
+        bias = _c(bias.to(x.dtype))
     call("basal200_nvfp4_linear", x.device, ptr(x), code(x.dtype), ptr(w), ptr(ws), ptr(_c(alpha.float())),
-         ptr(_c(inv_g.float())), None, ptr(y), M, N, K, ptr(q), ptr(s))
+         ptr(_c(inv_g.float())), ptr(bias), ptr(y), M, N, K, ptr(q), ptr(s))
     return y
+
+
+@torch.library.custom_op("basal::nvfp4_linear", mutates_args=())
+def nvfp4_linear(x: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, inv_g: Tensor) -> Tensor:
+    """x [M, K] -> [M, N] in x's dtype: the quantiser and the GEMM as one op (basal/nvfp4.py:183-189)."""
+    return _nvfp4_linear(x, w, ws, alpha, inv_g, None)
 
 
 @nvfp4_linear.register_fake
 def _(x, w, ws, alpha, inv_g):
+    return x.new_empty((x.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("basal::nvfp4_linear_bias", mutates_args=())
+def nvfp4_linear_bias(x: Tensor, w: Tensor, ws: Tensor, alpha: Tensor, inv_g: Tensor, bias: Tensor) -> Tensor:
+    """nvfp4_linear + bias, the bias added in the GEMM's epilogue with torch's roundings (the output cast to x's
+    dtype, the bias cast to it, the sum cast): what basal/nvfp4.py:211-212 computes after the op, in the op, so that
+    a compiled layer rounds it as eager does (Inductor would otherwise fuse the bias cast into the addition)."""
+    return _nvfp4_linear(x, w, ws, alpha, inv_g, bias)
+
+
+@nvfp4_linear_bias.register_fake
+def _(x, w, ws, alpha, inv_g, bias):
     return x.new_empty((x.shape[0], w.shape[0]))
 
 
@@ -377,3 +405,128 @@ def code_probs(z: Tensor, idx: Tensor, pad: Tensor) -> Tensor:
 @code_probs.register_fake
 def _(z, idx, pad):
     return z.new_empty((z.shape[0], idx.shape[1]), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# the config-5 hybrid decoder's steps around its linears
+# ---------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op("basal::fp8_block_gemm_glu", mutates_args=())
+def fp8_block_gemm_glu(q: Tensor, s: Tensor, w: Tensor, ws: Tensor, act: str, dtype: torch.dtype) -> Tensor:
+    """Activation codes (q, s) [M, K] through a merged block-FP8 [gate; up] weight [2I, K] -> act(gate) * up [M, I]
+    in dtype (bf16 / fp16), the gate/up pairing in the GEMM's epilogue."""
+    require_cuda(q, s, w, ws)
+    if act not in _ACT:
+        raise ValueError(f"gated linear: act must be one of {sorted(_ACT)}, not {act!r}")
+    q, s, w, ws = _c(q), _c(s), _c(w), _c(ws)
+    M, K = q.shape
+    if w.shape[0] % 256:
+        raise ValueError(f"gated linear: the merged [gate; up] weight has {w.shape[0]} rows, not a multiple of 256")
+    I = w.shape[0] // 2
+    y = torch.empty((M, I), dtype=dtype, device=q.device)
+    n = int(_lib.lib().basal200_block_linear_glu_workspace_bytes(M, I, K))
+    work = torch.empty(n, dtype=torch.uint8, device=q.device) if n > 0 else None
+    call("basal200_fp8_block_gemm_glu", q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(y), code(dtype), M, I, K,
+         _ACT[act], ptr(work), n)
+    return y
+
+
+@fp8_block_gemm_glu.register_fake
+def _(q, s, w, ws, act, dtype):
+    return q.new_empty((q.shape[0], w.shape[0] // 2), dtype=dtype)
+
+
+@torch.library.custom_op("basal::fp8_block_gemm_residual", mutates_args=())
+def fp8_block_gemm_residual(q: Tensor, s: Tensor, w: Tensor, ws: Tensor, bias: Optional[Tensor],
+                            residual: Tensor) -> Tensor:
+    """residual + (activation codes (q, s) [M, K] through an FP8-block weight, + bias) -> [M, N] in the residual's
+    dtype, the sum in the GEMM's epilogue."""
+    require_cuda(q, s, w, ws, bias, residual)
+    q, s, w, ws, residual = _c(q), _c(s), _c(w), _c(ws), _c(residual)
+    M, K = q.shape
+    N = w.shape[0]
+    if residual.shape != (M, N):
+        raise ValueError(f"residual linear: the residual must be [{M}, {N}], not {list(residual.shape)}")
+    y = torch.empty((M, N), dtype=residual.dtype, device=q.device)
+    if bias is not None:
+        bias = _c(bias.to(residual.dtype))
+    n = int(_lib.lib().basal200_block_linear_residual_workspace_bytes(M, N, K))
+    work = torch.empty(n, dtype=torch.uint8, device=q.device) if n > 0 else None
+    call("basal200_fp8_block_gemm_residual", q.device, ptr(q), ptr(s), ptr(w), ptr(ws), ptr(bias), ptr(residual),
+         ptr(y), code(residual.dtype), M, N, K, ptr(work), n)
+    return y
+
+
+@fp8_block_gemm_residual.register_fake
+def _(q, s, w, ws, bias, residual):
+    return residual.new_empty((q.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("basal::rms_norm_fp8_quant", mutates_args=())
+def rms_norm_fp8_quant(x: Tensor, w: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    """Qwen3_5RMSNorm of the rows of x [M, D] (weight applied as 1 + w) -> the FP8 codes [M, D] and scales
+    [M, D / 128] of the normed rows rounded to x's dtype (the normed rows are not written)."""
+    require_cuda(x, w)
+    x, w = _c(x), _c(w.to(x.dtype))
+    M, D = x.shape
+    q = torch.empty((M, D), dtype=E4M3, device=x.device)
+    s = torch.empty((M, D // 128), dtype=torch.float32, device=x.device)
+    call("basal200_rms_norm_fp8_quant", x.device, ptr(x), code(x.dtype), ptr(w), float(eps), M, D, None, ptr(q),
+         ptr(s))
+    return q, s
+
+
+@rms_norm_fp8_quant.register_fake
+def _(x, w, eps):
+    return x.new_empty(x.shape, dtype=E4M3), x.new_empty((x.shape[0], x.shape[1] // 128), dtype=torch.float32)
+
+
+@torch.library.custom_op("basal::gdn_prep", mutates_args=())
+def gdn_prep(proj: Tensor, tail: Optional[Tensor], conv: Tensor, A_log: Tensor, dt_bias: Tensor, rows: int, T: int,
+             Hk: int, Hv: int, b_off: int, a_off: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """The Gated DeltaNet's convolution (with the inputs before token 0 in tail [1 or rows, kw - 1, C]), SiLU, l2 norms
+    and gates over proj [rows * T, ld] -> q, k, v [rows, Hv, T, 128] fp32, beta, g [rows, Hv, T] fp32."""
+    require_cuda(proj, tail, conv, A_log, dt_bias)
+    if proj.stride(-1) != 1:
+        proj = proj.contiguous()
+    conv = _c(conv.to(proj.dtype))
+    tail = None if tail is None else _c(tail.to(proj.dtype))
+    dev = proj.device
+    q = torch.empty((rows, Hv, T, 128), dtype=torch.float32, device=dev)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    beta = torch.empty((rows, Hv, T), dtype=torch.float32, device=dev)
+    g = torch.empty_like(beta)
+    call("basal200_gdn_prep", dev, ptr(proj), code(proj.dtype), proj.stride(0), ptr(tail),
+         0 if tail is None else tail.shape[0], ptr(conv), conv.shape[1], ptr(_c(A_log.float())),
+         ptr(_c(dt_bias.to(proj.dtype))), b_off, a_off, rows, T, Hk, Hv, ptr(q), ptr(k), ptr(v), ptr(beta), ptr(g))
+    return q, k, v, beta, g
+
+
+@gdn_prep.register_fake
+def _(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off):
+    q = proj.new_empty((rows, Hv, T, 128), dtype=torch.float32)
+    b = proj.new_empty((rows, Hv, T), dtype=torch.float32)
+    return q, q.new_empty(q.shape), q.new_empty(q.shape), b, b.new_empty(b.shape)
+
+
+@torch.library.custom_op("basal::gdn_gate_fp8_quant", mutates_args=())
+def gdn_gate_fp8_quant(o: Tensor, proj: Tensor, z_off: int, gw: Tensor, eps: float, rows: int,
+                       T: int) -> tuple[Tensor, Tensor]:
+    """The recurrence's output o [rows, Hv, Tp, 128] fp32 (Tp >= T) through the gated RMSNorm with z from proj
+    [rows * T, ld] (columns z_off ..) -> the FP8 codes [rows * T, Hv * 128] and per-head scales [rows * T, Hv] of the
+    output projection's input."""
+    require_cuda(o, proj, gw)
+    o = _c(o)
+    if proj.stride(-1) != 1:
+        proj = proj.contiguous()
+    Hv, Tp = o.shape[1], o.shape[2]
+    q = torch.empty((rows * T, Hv * 128), dtype=E4M3, device=o.device)
+    s = torch.empty((rows * T, Hv), dtype=torch.float32, device=o.device)
+    call("basal200_gdn_gate_fp8_quant", o.device, ptr(o), Tp, ptr(proj), code(proj.dtype), proj.stride(0), z_off,
+         ptr(_c(gw.to(proj.dtype))), float(eps), rows, T, Hv, None, ptr(q), ptr(s))
+    return q, s
+
+
+@gdn_gate_fp8_quant.register_fake
+def _(o, proj, z_off, gw, eps, rows, T):
+    Hv = o.shape[1]
+    return o.new_empty((rows * T, Hv * 128), dtype=E4M3), o.new_empty((rows * T, Hv), dtype=torch.float32)

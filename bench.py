@@ -10,8 +10,9 @@ shards of independent requests, no collective; "weak" scaling) and the value is 
 rank's device time. One JSON line on rank 0 with, besides the contract keys:
   roofline      the FP8 block GEMM (the dominant kernel): achieved TFLOP/s from CUDA events around its launches in
                 the timed steps, against 2 x the measured dense bf16 peak (FP8 is twice bf16 on B200): the burst
-                figure, unless the clock samples of the timed region show the power cap active (then the sustained
-                figure, the one measured under that cap); the fraction of the other figure is reported beside it
+                figure, unless the clock samples of the timed region show the power cap holding the median SM clock
+                below its maximum (then the sustained figure, the one measured under that cap); the fraction of the
+                other figure is reported beside it
   e2e           the same metric through the public API (BlockFP8Linear modules) from pinned host memory: the H2D copy
                 of the step's activations and the D2H copy of its four outputs inside the timed region, on their
                 own streams so that the two PCIe directions and the GPU work of neighbouring steps overlap
@@ -321,7 +322,8 @@ def run_ours(args, rank, world, local_rank):
     achieved = gemm_flops / (sum(gemm_ms) * 1e-3) / 1e12
     # the denominator follows the clocks sampled in the timed region: the sustained peak was measured under the
     # power cap, the burst peak at full clock; a region the cap did not touch is held to the burst figure
-    capped = "sw_power_cap" in clocks.get("reasons", [])
+    capped = ("sw_power_cap" in clocks.get("reasons", []) and clocks.get("sm_mhz") is not None
+              and clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"])  # the cap active AND holding the clock down
     peak_burst, peak_sust = 2.0 * pk["bf16_tflops"], 2.0 * pk["bf16_tflops_sustained"]
     peak = peak_sust if capped else peak_burst
     traffic = profiled_traffic()
@@ -339,8 +341,8 @@ def run_ours(args, rank, world, local_rank):
                          "kernel": "basal200 fp8 block GEMM (tcgen05 kind::f8f6f4)",
                          "peak_source": (f"2 x {'bf16_tflops_sustained' if capped else 'bf16_tflops'} of "
                                          f"{pk['source']} peaks (FP8 dense = 2 x bf16 dense; "
-                                         f"{'sw_power_cap active' if capped else 'no power cap'} in the clock "
-                                         "samples of the timed region)"),
+                                         f"{'the power cap held the median SM clock down' if capped else 'median SM clock at its maximum'} "
+                                         "in the clock samples of the timed region)"),
                          "frac_of_burst_peak": round(achieved / peak_burst, 4),
                          "frac_of_sustained_peak": round(achieved / peak_sust, 4),
                          "per_projection_tflops": {name: round(2 * M * n * k / (t * 1e-3) / 1e12, 1)

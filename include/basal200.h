@@ -157,6 +157,52 @@ int basal200_int8_block_linear_residual(const void* x, int x_dtype, const int8_t
 /* Workspace bytes (16-byte aligned) for the few-rows path of the residual linears; 0 for M > 64. Pure. */
 int64_t basal200_block_linear_residual_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
+/* The gated linear of basal200_fp8_block_linear_glu from activation codes and scales already quantised (q [M, K]
+ * e4m3, s [M, K/128] fp32, e.g. by basal200_rms_norm_fp8_quant, which fuses the quantiser into the norm before it):
+ * y [M, I] (y_dtype bf16 or fp16) = act(gate) * up with the same roundings. workspace as for the gated linear. No
+ * counterpart in the reference, whose gated MLP input is the merged linear then act(g) * u (basal/gdn_graph.py:127). */
+int basal200_fp8_block_gemm_glu(const uint8_t* q, const float* s, const uint8_t* w, const float* ws, void* y,
+                                int y_dtype, int64_t M, int64_t I, int64_t K, int act, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* The residual linear of basal200_fp8_block_linear_residual from activation codes and scales already quantised (e.g.
+ * by basal200_gdn_gate_fp8_quant): y [M, N] = residual + (q, s) . w^T (+ bias), y_dtype bf16 or fp16, y may be the
+ * residual. The output projections of basal/gdn_graph.py:128, :439, :466. */
+int basal200_fp8_block_gemm_residual(const uint8_t* q, const float* s, const uint8_t* w, const float* ws,
+                                     const void* bias, const void* residual, void* y, int y_dtype, int64_t M,
+                                     int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---- The config-5 hybrid decoder's steps around its linears (a Qwen 3.5 layer, basal/gdn_graph.py:122-140, :432-439)
+ * ---- */
+
+/* Qwen3_5RMSNorm of each row of x [M, D] (x_dtype bf16 or fp16, weight w [D] of that type applied as 1 + w, fp32
+ * inside, basal/gdn_graph.py:122-126) fused with the FP8 activation quantiser: q [M, D] e4m3 and s [M, D/128] fp32
+ * are the codes of the normed row rounded to x_dtype, bit-exact to basal200_fp8_act_quant of that row; y [M, D] (may
+ * be NULL) receives the normed row. D % 128 == 0. */
+int basal200_rms_norm_fp8_quant(const void* x, int x_dtype, const void* w, float eps, int64_t M, int64_t D, void* y,
+                                uint8_t* q, float* s, void* stream);
+
+/* The Gated DeltaNet's input steps (basal/gdn_graph.py:131-140, :559-576, with transformers' Qwen3_5GatedDeltaNet):
+ * over rows of T tokens (proj [rows * T, ld] of `dtype`, the merged input projection's output: the convolution's
+ * channels [q (Hk heads) | k (Hk) | v (Hv)] of 128 from column 0, b and a (Hv each) at columns b_off and a_off), the
+ * causal depthwise convolution of kw taps (conv [C, kw], C = (2 Hk + Hv) * 128; tail [tail_rows, kw - 1, C] the inputs
+ * before token 0, tail_rows 1 (shared) or rows, or NULL for zeros) and SiLU, rounded to `dtype`; the l2 norms of q and
+ * k (eps 1e-6; q also times 128^-1/2); beta = sigmoid(b) rounded; g = -exp(A_log) * softplus(a + dt_bias) in fp32.
+ * Outputs are head-major fp32: q, k, v [rows, Hv, T, 128] (a key head's q and k repeated for its Hv / Hk value heads),
+ * beta, g [rows, Hv, T]. */
+int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail, int tail_rows, const void* conv,
+                      int kw, const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk,
+                      int Hv, float* q, float* k, float* v, float* beta, float* g, void* stream);
+
+/* The Gated DeltaNet's output steps (basal/gdn_graph.py:432-438, Qwen3_5RMSNormGated) fused with the FP8 quantiser of
+ * the output projection's input: o [rows, Hv, Tp, 128] fp32 (the recurrence's output, Tp >= T), z in a [rows * T, ld]
+ * matrix of `dtype` from column z_off (Hv * 128 values a token), gw [128]: each head's values rounded to `dtype`,
+ * RMS-normed (eps), times gw, times silu(z), rounded -> y [rows * T, Hv * 128] (may be NULL), and quantised with one
+ * scale per head: q [rows * T, Hv * 128] e4m3, s [rows * T, Hv] fp32 (bit-exact to basal200_fp8_act_quant of y). */
+int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype, int64_t ld, int z_off,
+                                const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
+                                void* stream);
+
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)
 

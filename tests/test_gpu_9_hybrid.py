@@ -1,0 +1,275 @@
+"""The config-5 hybrid classifier (basal_b200.hybrid: every linear an FP8-block BlockFP8Linear) and its fused steps.
+
+Kernels, against plain torch statements of the same steps (fp32 inside, the reference's roundings):
+  - basal::rms_norm_fp8_quant: the normed rows within one unit in the last place of torch's Qwen3_5RMSNorm, and its
+    codes / scales equal to basal::fp8_act_quant of its own normed rows, bit for bit;
+  - basal::gdn_prep: convolution + SiLU outputs (v), beta and g equal to the torch statement bit for bit, q and k
+    (l2-normed) within 1e-6;
+  - basal::gdn_gate_fp8_quant: its output within one unit in the last place of the torch statement, its codes equal
+    to the quantiser's of its own output bit for bit;
+  - the gated and residual GEMMs from codes equal the linears that quantise x themselves, bit for bit.
+The model, against the CPU oracle (oracle/hybrid.py, pinned to the reference's Qwen 3.5 graph forward by
+tests/test_oracle_hybrid.py), with the same weights (the GPU quantiser's codes, bit-exact to the oracle's):
+  - C5's layer sizes, layer by layer: each layer fed the oracle's input (prefix pass from position 0, then the suffix
+    pass continuing the oracle's prefix state), its update (output - input) within 1e-2 of the oracle's for the
+    median row and within one e4m3 step (2^-4) for every row;
+  - 8 small layers end to end (prefix 100, suffix 40, 3 requests): identical argmax, probabilities within 1e-3;
+  - the full C5 model: probabilities finite, summing to 1.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import hybrid as ohy
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def hy():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from basal_b200 import hybrid
+    return hybrid
+
+
+def ulps_bf16(a, b):
+    """Largest distance in bf16 units between two bf16 tensors of finite values."""
+    ia = a.contiguous().view(torch.int16).int()
+    ib = b.contiguous().view(torch.int16).int()
+    ia = torch.where(ia < 0, -(ia & 0x7FFF), ia)
+    ib = torch.where(ib < 0, -(ib & 0x7FFF), ib)
+    return int((ia - ib).abs().max())
+
+
+def test_rms_norm_quant_kernel(hy):
+    from basal_b200 import _lib, ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for M, D in ((1, 128), (37, 2560), (300, 384), (4099, 2048)):
+        x = (torch.randn(M, D, device="cuda", generator=g) * 3).to(BF)
+        x[0, :128] = 0  # a zero group among others
+        w = (torch.randn(D, device="cuda", generator=g) * 0.1).to(BF)
+        y = torch.empty_like(x)
+        q = torch.empty(M, D, dtype=torch.uint8, device="cuda")
+        s = torch.empty(M, D // 128, dtype=torch.float32, device="cuda")
+        _lib.call("basal200_rms_norm_fp8_quant", x.device, x.data_ptr(), _lib.BF16, w.data_ptr(), 1e-6, M, D,
+                  y.data_ptr(), q.data_ptr(), s.data_ptr())
+        assert ulps_bf16(y, hy.rms(x, w, 1e-6)) <= 1
+        qa, sa = ops.fp8_act_quant(y)
+        assert torch.equal(q, qa.view(torch.uint8)) and torch.equal(s, sa)
+        q2, s2 = ops.rms_norm_fp8_quant(x, w, 1e-6)
+        assert torch.equal(q2.view(torch.uint8), q) and torch.equal(s2, s)
+
+
+def torch_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off):
+    """The Gated DeltaNet input steps in plain torch (the unfused form: convolution products and sums each rounded,
+    SiLU in fp32, rounded to bf16, l2 norms in fp32)."""
+    C = (2 * Hk + Hv) * 128
+    x = proj[:, :C].view(rows, T, C)
+    xin = torch.cat([tail.expand(rows, -1, -1).to(x.dtype), x], 1)
+    w = conv.float()
+    acc = xin[:, 0:T].float() * w[:, 0]
+    for j in range(1, w.shape[1]):
+        acc = acc + xin[:, j:j + T].float() * w[:, j]
+    y = F.silu(acc).to(x.dtype)
+    q, k, v = y.split((Hk * 128, Hk * 128, Hv * 128), -1)
+    r = Hv // Hk
+    q = q.reshape(rows, T, Hk, 128).repeat_interleave(r, 2).float()
+    k = k.reshape(rows, T, Hk, 128).repeat_interleave(r, 2).float()
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * (1.0 / 128 ** 0.5)
+    k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    bb = proj[:, b_off:b_off + Hv].view(rows, T, Hv)
+    aa = proj[:, a_off:a_off + Hv].view(rows, T, Hv)
+    beta = bb.sigmoid().float()
+    gg = -A_log.float().exp() * F.softplus(aa.float() + dt_bias.float())
+    t = lambda z: z.transpose(1, 2).contiguous()  # noqa: E731
+    return t(q), t(k), t(v.reshape(rows, T, Hv, 128).float()), t(beta), t(gg)
+
+
+@pytest.mark.parametrize("rows, T, Hk, Hv", [(2, 37, 1, 2), (3, 5, 2, 2), (2, 70, 16, 32)])
+def test_gdn_prep_kernel(hy, rows, T, Hk, Hv):
+    from basal_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(T)
+    C = (2 * Hk + Hv) * 128
+    ld = C + Hv * 128 + 2 * Hv + 64
+    proj = torch.randn(rows * T, ld, device="cuda", generator=g).to(BF)
+    conv = (torch.rand(C, 4, device="cuda", generator=g) - 0.5).to(BF)
+    A_log = torch.log(1 + 15 * torch.rand(Hv, device="cuda", generator=g))
+    dt_bias = (1 + 0.1 * torch.randn(Hv, device="cuda", generator=g)).to(BF)
+    b_off, a_off = C + Hv * 128, C + Hv * 128 + Hv
+    for tail in (torch.randn(1, 3, C, device="cuda", generator=g).to(BF), torch.zeros(1, 3, C, device="cuda",
+                                                                                          dtype=BF)):
+        got = ops.gdn_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off)
+        want = torch_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off)
+        for name, a, b in zip("qkvbg", got, want):
+            if name in "qk":
+                assert (a - b).abs().max() <= 1e-6, name
+            else:
+                assert torch.equal(a, b), name
+
+
+def test_gdn_gate_quant_kernel(hy):
+    from basal_b200 import _lib, ops
+    g = torch.Generator(device="cuda").manual_seed(1)
+    rows, T, Tp, Hv, z_off = 3, 37, 64, 4, 256
+    ld = z_off + Hv * 128 + 128
+    o = torch.randn(rows, Hv, Tp, 128, device="cuda", generator=g) * 0.3
+    proj = torch.randn(rows * T, ld, device="cuda", generator=g).to(BF)
+    gw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(BF)
+    y = torch.empty(rows * T, Hv * 128, dtype=BF, device="cuda")
+    q = torch.empty(rows * T, Hv * 128, dtype=torch.uint8, device="cuda")
+    s = torch.empty(rows * T, Hv, dtype=torch.float32, device="cuda")
+    _lib.call("basal200_gdn_gate_fp8_quant", o.device, o.data_ptr(), Tp, proj.data_ptr(), _lib.BF16, ld, z_off,
+              gw.data_ptr(), 1e-6, rows, T, Hv, y.data_ptr(), q.data_ptr(), s.data_ptr())
+    u = o[:, :, :T].transpose(1, 2).to(BF).float()  # [rows, T, Hv, 128]
+    n = (u * torch.rsqrt(u.pow(2).mean(-1, keepdim=True) + 1e-6)).to(BF)
+    n = gw * n
+    z = proj[:, z_off:z_off + Hv * 128].view(rows, T, Hv, 128)
+    want = (n * F.silu(z.float())).to(BF).reshape(rows * T, Hv * 128)
+    assert ulps_bf16(y, want) <= 1
+    qa, sa = ops.fp8_act_quant(y)
+    assert torch.equal(q, qa.view(torch.uint8)) and torch.equal(s, sa)
+    q2, s2 = ops.gdn_gate_fp8_quant(o, proj, z_off, gw, 1e-6, rows, T)
+    assert torch.equal(q2.view(torch.uint8), q) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("M", [16, 300])
+def test_gemms_from_codes_equal_the_linears(hy, M):
+    import basal_b200 as b2
+    from basal_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(M)
+    K, I, N = 512, 256, 384
+    x = torch.randn(M, K, device="cuda", generator=g).to(BF)
+    wg, sg = b2.fp8block.quantize(torch.randn(2 * I, K, device="cuda", generator=g) * 0.02)
+    wr, sr = b2.fp8block.quantize(torch.randn(N, K, device="cuda", generator=g) * 0.02)
+    res = torch.randn(M, N, device="cuda", generator=g).to(BF)
+    q, s = ops.fp8_act_quant(x)
+    assert torch.equal(ops.fp8_block_gemm_glu(q, s, wg, sg, "silu", BF), b2.fp8block.linear_glu(x, wg, sg, "silu"))
+    assert torch.equal(ops.fp8_block_gemm_residual(q, s, wr, sr, None, res),
+                       b2.fp8block.FORMAT.linear_residual(x, wr, sr, None, res))
+
+
+def export(model, ids, option_ids):
+    """The model's weights in oracle/hybrid.py's layout, with the embedding rows of `ids` only (ids remapped)."""
+    c = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
+    used = np.unique(np.concatenate([np.asarray(i).ravel() for i in ids]))
+    remap = {int(t): j for j, t in enumerate(used)}
+    W = {"embed": c(model.embed[torch.as_tensor(used, device=model.device)]),
+         "head": c(model.head.weight[torch.as_tensor(option_ids, device=model.device)]),
+         "final_norm": c(model.final_norm), "layers": []}
+    for L in model.layers:
+        d = {}
+        for k, v in L.items():
+            if k == "kind":
+                d[k] = v
+            elif hasattr(v, "weight_scale"):
+                d[k] = (v.weight.view(torch.uint8).cpu().numpy(), v.weight_scale.cpu().numpy())
+            else:
+                d[k] = c(v)
+        W["layers"].append(d)
+    return W, lambda a: np.vectorize(remap.get)(np.asarray(a))
+
+
+def _update_err(gpu_out, h_in, o_out):
+    """(median, largest) per-row relative difference of the layer's update (output - input), GPU against oracle."""
+    du = gpu_out.float().cpu().numpy().reshape(o_out.shape) - h_in
+    do = o_out - h_in
+    e = np.linalg.norm(du - do, axis=-1) / np.maximum(np.linalg.norm(do, axis=-1), 1e-30)
+    return float(np.median(e)), float(e.max())
+
+
+def test_c5_layers_one_by_one_against_the_oracle(hy):
+    cfg = hy.HybridConfig(layers=4)
+    model = hy.HybridClassifier(cfg, seed=1)
+    g = torch.Generator().manual_seed(2)
+    P, S = 70, 37
+    pre = torch.randint(0, cfg.vocab, (P,), generator=g)
+    suf = torch.randint(0, cfg.vocab, (S,), generator=g)
+    W, remap = export(model, [pre, suf], [0])
+    dev = torch.device("cuda")
+    cuda = lambda a, dt=BF: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)  # noqa: E731
+    errs = []
+    ost = {"length": P, "kv": [], "states": []}
+    for pas, ids, pos in (("prefix", pre, np.arange(P)), ("suffix", suf, np.arange(P, P + S))):
+        h = W["embed"][remap(ids.numpy())]
+        T = len(pos)
+        cos, sin = hy.rope_tables(cfg, torch.as_tensor(pos, device=dev)[None], BF)
+        ia = ig = 0
+        for i, L in enumerate(model.layers):
+            OL = W["layers"][i]
+            hin = cuda(h)[None]
+            if L["kind"] == hy.LINEAR:
+                if pas == "prefix":
+                    s0 = np.zeros((cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim), np.float32)
+                    c0 = np.zeros((cfg.conv - 1, cfg.conv_dim), np.float32)
+                else:
+                    s0, c0 = ost["states"][ig]
+                gout, _, _ = model._gdn(L, hin, cuda(s0, torch.float32)[None], cuda(c0)[None])
+                oout, so, to = ohy.gdn(OL, cfg, h, s0, c0, ohy.bf16)
+                if pas == "prefix":
+                    ost["states"].append((so, to))
+                ig += 1
+            else:
+                pk, pv = (None, None) if pas == "prefix" else ost["kv"][ia]
+                gout, _, _ = model._attention(L, hin, cos, sin, None if pk is None else cuda(pk)[None],
+                                              None if pv is None else cuda(pv)[None])
+                oout, ko, vo = ohy.attention(OL, cfg, h, pos, pk, pv, ohy.bf16)
+                if pas == "prefix":
+                    ost["kv"].append((ko, vo))
+                ia += 1
+            errs.append((pas, i, L["kind"], _update_err(gout, h, oout)))
+            gm = model._mlp(L, cuda(oout)[None])
+            om = ohy.mlp(OL, oout, cfg.eps, ohy.bf16)
+            errs.append((pas, i, "mlp", _update_err(gm, oout, om)))
+            h = om
+    # Each layer quantises its activations to e4m3 twice or more (its input, its output projection's input): where
+    # an fp32 sum in another order (GPU against numpy) moves a value across an e4m3 rounding boundary, that value
+    # moves by one e4m3 step (2^-4 relative). Such flips are rare, so a row's update agrees to about 1e-2; a wrong
+    # formula, head layout or state would be off by O(1).
+    print("\n".join(f"{p} layer {i} {k}: median {a:.2e}, max {m:.2e}" for p, i, k, (a, m) in errs))
+    assert max(a for *_, (a, m) in errs) <= 1e-2, errs
+    assert max(m for *_, (a, m) in errs) <= 2 ** -4, errs
+    from basal_b200 import _lib
+    assert _lib.device_faults(0) == 0
+
+
+def test_small_hybrid_end_to_end_against_the_oracle(hy):
+    cfg = hy.HybridConfig(layers=8, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, vocab=2048,
+                          lin_k_heads=1, lin_v_heads=2)
+    model = hy.HybridClassifier(cfg, seed=0)
+    g = torch.Generator().manual_seed(1)
+    P, S, B = 100, 40, 3
+    pre = torch.randint(0, cfg.vocab, (P,), generator=g)
+    suf = torch.randint(0, cfg.vocab, (B, S), generator=g)
+    options = torch.randperm(cfg.vocab, generator=g)[:8].tolist()
+    from basal_b200.readout import CodeReadout
+    ro = CodeReadout(model.head)
+    rows, idx, pad = ro.rows([options] * B)
+    st = model.prefix(pre)
+    probs = model.decide(suf.cuda(), st, ro, rows, idx, pad).cpu().numpy()
+    W, remap = export(model, [pre, suf], options)
+    _, ost = ohy.prefix(W, cfg, remap(pre.numpy()))
+    for r in range(B):
+        _, p = ohy.decide(W, cfg, ost, remap(suf[r].numpy()), np.arange(8))
+        assert np.argmax(p) == np.argmax(probs[r]), (r, p, probs[r])
+        assert np.abs(p - probs[r]).max() <= 1e-3, (r, np.abs(p - probs[r]).max())
+
+
+def test_full_c5_decisions(hy):
+    model = hy.HybridClassifier(hy.C5, seed=2)
+    g = torch.Generator().manual_seed(3)
+    pre = torch.randint(0, hy.C5.vocab, (256,), generator=g)
+    suf = torch.randint(0, hy.C5.vocab, (8, 64), generator=g).cuda()
+    from basal_b200.readout import CodeReadout
+    ro = CodeReadout(model.head)
+    options = torch.randperm(hy.C5.vocab, generator=g)[:8].tolist()
+    rows, idx, pad = ro.rows([options] * 8)
+    st = model.prefix(pre)
+    p = model.decide(suf, st, ro, rows, idx, pad)
+    assert torch.isfinite(p).all()
+    assert torch.allclose(p.sum(-1), torch.ones(8, device="cuda"), atol=1e-5)
+    assert model.flops_per_token() == 2 * sum(m.in_features * m.out_features for _, m in model.linears())
+    from basal_b200 import _lib
+    assert _lib.device_faults(0) == 0
