@@ -12,6 +12,7 @@
 #include "quant.cuh"
 #include "readout.cuh"
 #include "hybrid.cuh"
+#include "gdn_chunk.cuh"
 
 namespace b200 {
 namespace {
@@ -41,10 +42,10 @@ int current_device(int* dev) {
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
 enum SmemSlot {
   kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50,
-  kSlotRes = 58
+  kSlotRes = 58, kSlotGdn = 62
 };
 // kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7,
-// kSlotRes .. + 3 (bits of a 64-bit mask)
+// kSlotRes .. + 3, kSlotGdn (bits of a 64-bit mask)
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
@@ -930,6 +931,46 @@ int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, in
                     z_off, static_cast<const __half*>(gw), eps, rows, T, Hv, static_cast<__half*>(y), q, s);
 }
 
+int gdn_chunk(const float* q, const float* k, const float* v, const float* g, const float* beta, const float* s0,
+              int s0_rows, float* o, float* s_out, int rows, int H, int T, cudaStream_t st) {
+  if (rows < 0 || H <= 0 || T < 0) return BASAL200_ERR_ARG;
+  if (rows == 0) return BASAL200_OK;
+  if (T > 0 && (!q || !k || !v || !g || !beta || !o)) return BASAL200_ERR_ARG;  // no tokens: nothing of them is read
+  if (s0 && s0_rows != 1 && s0_rows != rows) return BASAL200_ERR_ARG;
+  if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))) || (s0 && !aligned16(s0)) ||
+      (s_out && !aligned16(s_out)))
+    return BASAL200_ERR_ALIGN;
+  if ((int64_t)rows * H * 2 > INT32_MAX || (int64_t)rows * H * T * 128 > ((int64_t)1 << 40)) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  if (T == 0) {  // no tokens: the state passes through unchanged
+    if (!s_out) return BASAL200_OK;
+    if (!s0) return cudaMemsetAsync(s_out, 0, (size_t)rows * H * 128 * 128 * 4, st) == cudaSuccess
+                        ? BASAL200_OK : BASAL200_ERR_LAUNCH;
+    for (int r = 0; r < rows; ++r)
+      if (cudaMemcpyAsync(s_out + (int64_t)r * H * 128 * 128, s0 + (int64_t)(s0_rows == 1 ? 0 : r) * H * 128 * 128,
+                          (size_t)H * 128 * 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return BASAL200_ERR_LAUNCH;
+    return BASAL200_OK;
+  }
+  constexpr size_t smem = sizeof(gdnchunk::Smem);
+  if ((rc = set_smem(dev, kSlotGdn, gdnchunk::gdn_chunk_kernel, smem))) return rc;
+  gdnchunk::Params p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.g = g;
+  p.beta = beta;
+  p.s0 = s0;
+  p.s0_rows = s0_rows;
+  p.o = o;
+  p.s_out = s_out;
+  p.rows = rows;
+  p.H = H;
+  p.T = T;
+  return launch_pdl(gdnchunk::gdn_chunk_kernel, (unsigned)(rows * H * 2), gdnchunk::NT, smem, st, p);
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // Allocation-free FP8-block linear: the activation codes and scales live in one file-scope device array instead of
 // caller scratch. The array is part of the loaded module, so every GPU that loads the library holds its
@@ -1114,6 +1155,12 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream) {
   return gdn_gate_quant(o, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
+}
+
+int basal200_gdn_chunk_rule(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                            const float* s0, int s0_rows, float* o, float* s_out, int rows, int H, int T,
+                            void* stream) {
+  return gdn_chunk(q, k, v, g, beta, s0, s0_rows, o, s_out, rows, H, T, as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing

@@ -17,8 +17,8 @@ blockquant.fuse does for the reference: the Gated DeltaNet's q/k/v/z/b/a, the at
 input basal::fp8_block_linear_glu (SwiGLU in the GEMM's epilogue) and the output projections
 basal::fp8_block_linear_residual (the residual add in the GEMM's epilogue). The norms, the convolution, the gates and
 the rotary embedding follow the reference's roundings (bf16 between operations, fp32 inside the norms); the
-recurrence runs in fp32 (chunks of 64 tokens); the attention over the prefix and the rows' own tokens is torch's
-scaled_dot_product_attention. Everything runs on the GPU.
+recurrence runs in fp32 over chunks of 64 tokens (basal::gdn_chunk_rule); the attention over the prefix and the rows'
+own tokens is torch's scaled_dot_product_attention. Everything runs on the GPU.
 """
 import dataclasses
 import math
@@ -50,7 +50,6 @@ class HybridConfig:
     eps: float = 1e-6
     rotary_frac: float = 0.25    # partial rotary: the first 32 of 128 dimensions of a head
     rope_theta: float = 10000.0
-    chunk: int = 64              # tokens per chunk of the recurrence
 
     @property
     def kinds(self):
@@ -108,49 +107,6 @@ def rope_tables(cfg, pos, dtype):
     f = pos.float()[..., None] * inv
     emb = torch.cat([f, f], -1)
     return emb.cos().to(dtype), emb.sin().to(dtype)
-
-
-def l2norm(x, eps=1e-6):
-    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
-
-
-def chunk_delta_rule(q, k, v, g, beta, s0, chunk):
-    """The gated delta rule over chunks (fp32): q, k [b, H, T, dk] (l2-normed, q scaled), v [b, H, T, dv], g, beta
-    [b, H, T], s0 [b or 1, H, dk, dv] -> (o [b, H, Tp, dv], final state [b, H, dk, dv]); Tp = T rounded up to whole
-    chunks (the rows past T are the padding's, not outputs).
-
-    Per token t (the definition): S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T,
-    o_t = S_t^T q_t. Within a chunk with cumulative log-decays G, the rows' updates solve a unit lower-triangular
-    system (I + A) with A_ij = beta_i (k_i . k_j) e^{G_i - G_j} for j < i; across chunks the state carries."""
-    b, H, T, dk = k.shape
-    dv = v.shape[-1]
-    pad = -T % chunk
-    if pad:
-        q, k, v = (F.pad(t, (0, 0, 0, pad)) for t in (q, k, v))
-        g, beta = F.pad(g, (0, pad)), F.pad(beta, (0, pad))
-    n = (T + pad) // chunk
-    q, k, v = (t.reshape(b, H, n, chunk, -1) for t in (q, k, v))
-    G = g.reshape(b, H, n, chunk).cumsum(-1)
-    beta = beta.reshape(b, H, n, chunk)
-    low = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
-    both = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(0)
-    diff = (G[..., :, None] - G[..., None, :]).masked_fill(~both, 0.0).exp().masked_fill(~both, 0.0)
-    kk = k @ k.transpose(-1, -2)
-    A = (beta[..., None] * kk * diff).masked_fill(~low, 0.0)
-    eye = torch.eye(chunk, dtype=q.dtype, device=q.device)
-    Tinv = torch.linalg.solve_triangular(A + eye, eye.expand_as(A), upper=False, unitriangular=True)
-    U = Tinv @ (beta[..., None] * v)
-    W = Tinv @ (beta[..., None] * G.exp()[..., None] * k)
-    qk = (q @ k.transpose(-1, -2)) * diff
-    qg = q * G.exp()[..., None]
-    kd = k * (G[..., -1:] - G).exp()[..., None]
-    S = s0.expand(b, H, dk, dv).contiguous()
-    out = torch.empty(b, H, n, chunk, dv, dtype=q.dtype, device=q.device)
-    for c in range(n):
-        vn = U[:, :, c] - W[:, :, c] @ S
-        out[:, :, c] = qg[:, :, c] @ S + qk[:, :, c] @ vn
-        S = G[:, :, c, -1, None, None].exp() * S + kd[:, :, c].transpose(-1, -2) @ vn
-    return out.reshape(b, H, n * chunk, dv), S
 
 
 @dataclasses.dataclass
@@ -235,7 +191,7 @@ class HybridClassifier:
         b_off, a_off = C + cfg.value_dim, C + cfg.value_dim + cfg.lin_v_heads
         q, k, v, beta, g = ops.gdn_prep(proj, tail0, L["conv"], L["A_log"], L["dt_bias"], b, T, cfg.lin_k_heads,
                                         cfg.lin_v_heads, b_off, a_off)
-        o, s = chunk_delta_rule(q, k, v, g, beta, s0, cfg.chunk)
+        o, s = ops.gdn_chunk_rule(q, k, v, g, beta, s0)
         qo, so = ops.gdn_gate_fp8_quant(o, proj, z_off, L["gnorm"], cfg.eps, b, T)
         out = L["out"]
         h = ops.fp8_block_gemm_residual(qo, so, out.weight, out.weight_scale, None, h2).view(b, T, D)

@@ -28,6 +28,7 @@
                                                  the Gated DeltaNet's convolution, norms and gates (gdn_graph.py:131-140)
   basal::gdn_gate_fp8_quant(o, proj, z_off, gw, eps, rows, T)
                                                  its gated output norm fused with the FP8 quantiser (gdn_graph.py:432-438)
+  basal::gdn_chunk_rule(q, k, v, g, beta, s0)   its gated delta rule over chunks of 64 tokens (gdn_graph.py:81-87)
 
 Every op is functional (mutates_args=()), allocates its outputs (and scratch) from the caching allocator, enqueues on
 the current stream and never synchronises: Dynamo traces them through their fake kernels and a CUDA graph captures
@@ -530,3 +531,26 @@ def gdn_gate_fp8_quant(o: Tensor, proj: Tensor, z_off: int, gw: Tensor, eps: flo
 def _(o, proj, z_off, gw, eps, rows, T):
     Hv = o.shape[1]
     return o.new_empty((rows * T, Hv * 128), dtype=E4M3), o.new_empty((rows * T, Hv), dtype=torch.float32)
+
+
+@torch.library.custom_op("basal::gdn_chunk_rule", mutates_args=())
+def gdn_chunk_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor,
+                   s0: Optional[Tensor]) -> tuple[Tensor, Tensor]:
+    """The gated delta rule (fp32) over q, k, v [rows, H, T, 128], g, beta [rows, H, T] from the state s0 [1 or rows, H,
+    128, 128] (None: zeros) -> (o [rows, H, T, 128], the final state [rows, H, 128, 128])."""
+    require_cuda(q, k, v, g, beta, s0)
+    q, k, v, g, beta = (_c(t.float()) for t in (q, k, v, g, beta))
+    rows, H, T, _ = q.shape
+    o = torch.empty_like(v)
+    s = torch.empty((rows, H, 128, 128), dtype=torch.float32, device=q.device)
+    if s0 is not None:
+        s0 = _c(s0.float())
+    call("basal200_gdn_chunk_rule", q.device, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(s0),
+         0 if s0 is None else s0.shape[0], ptr(o), ptr(s), rows, H, T)
+    return o, s
+
+
+@gdn_chunk_rule.register_fake
+def _(q, k, v, g, beta, s0):
+    rows, H = q.shape[0], q.shape[1]
+    return v.new_empty(v.shape), v.new_empty((rows, H, 128, 128))

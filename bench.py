@@ -18,6 +18,12 @@ rank's device time. One JSON line on rank 0 with, besides the contract keys:
                 own streams so that the two PCIe directions and the GPU work of neighbouring steps overlap
   cpu_baseline  the reference's CPU maths (oracle/, numpy + BLAS on all host threads) on a bounded sample of rows
   clocks        nvidia-smi samples taken during the timed region
+  decisions     the metric's second half: a random-init 32-layer Gated DeltaNet / attention hybrid
+                (hidden 2560, every linear FP8-block, basal_b200.hybrid) answering 4096 decision requests, each a
+                shared 1024-token prefix + 256 random suffix tokens, read out over 8 options; the requests are
+                row-sharded across the ranks (strong scaling: 4096 in all), each GPU computes the prefix once;
+                decisions/s = 4096 / the slowest rank's time, with the suffix ids copied in from pinned host memory and
+                the probabilities copied back inside the timed region
 --impl reference times the reference's CPU implementation of the path (the oracle port) on this box's host cores
 (the reference has no native code, and its only B200 GPU path is a Triton kernel), rank 0 only.
 """
@@ -318,6 +324,10 @@ def run_ours(args, rank, world, local_rank):
     o4_tflops = 2 * M * HIDDEN * 4096 / (e0.elapsed_time(e1) / 20 * 1e-3) / 1e12
     del x4, q4, s4, o4, lin4
 
+    del xs, mods, hx, hy, dx
+    torch.cuda.empty_cache()
+    decisions = run_decisions(rank, world, local_rank) if not args.no_decisions else None
+
     gemm_flops = sum(2 * M * n * k for _, n, k in PROJ)
     achieved = gemm_flops / (sum(gemm_ms) * 1e-3) / 1e12
     # the denominator follows the clocks sampled in the timed region: the sustained peak was measured under the
@@ -357,6 +367,10 @@ def run_ours(args, rank, world, local_rank):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if decisions is not None:
+            if world == 1:
+                decisions["cpu_baseline"] = c5_cpu_baseline()
+            line["decisions"] = decisions
         print(json.dumps(line), flush=True)
 
 
@@ -575,6 +589,122 @@ def run_sweep(fmts):
     print(json.dumps({"faults": b2._lib.device_faults(0), "hbm_peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}))
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# decisions/s
+# ------------------------------------------------------------------------------------------------------------------
+C5_REQUESTS, C5_PREFIX, C5_SUFFIX, C5_OPTIONS, C5_MICRO = 4096, 1024, 256, 8, 128
+
+
+def c5_inputs(vocab):
+    """The seeded prefix ids, every request's suffix ids [4096, 256] (host) and the 8 option ids."""
+    import torch
+    g = torch.Generator().manual_seed(5)
+    prefix = torch.randint(0, vocab, (C5_PREFIX,), generator=g)
+    options = torch.randperm(vocab, generator=g)[:C5_OPTIONS].tolist()
+    suffix = torch.randint(0, vocab, (C5_REQUESTS, C5_SUFFIX), generator=torch.Generator().manual_seed(6))
+    return prefix, suffix, options
+
+
+def run_decisions(rank, world, local_rank):
+    """Decisions/s of C5 over `world` ranks (each its row shard of the 4096 requests); returns a dict on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from basal_b200 import hybrid, readout, shard
+    dev = torch.device("cuda", local_rank)
+    model = hybrid.HybridClassifier(hybrid.C5, device=dev, seed=0)  # the same weights on every rank
+    prefix, suffix, options = c5_inputs(hybrid.C5.vocab)
+    lo, hi = shard.shard_range(C5_REQUESTS, world, rank)
+    mine = suffix[lo:hi].pin_memory()
+    out = torch.empty(hi - lo, C5_OPTIONS, dtype=torch.float32).pin_memory()
+    ro = readout.CodeReadout(model.head)
+    rows, idx, pad = ro.rows([options] * C5_MICRO)
+    ids = torch.empty(C5_MICRO, C5_SUFFIX, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def job(n_requests):
+        st = model.prefix(prefix.to(dev, non_blocking=True))
+        for a in range(0, n_requests, C5_MICRO):
+            b = min(a + C5_MICRO, n_requests)
+            ids[: b - a].copy_(mine[a:b], non_blocking=True)
+            r, i, p = (rows, idx, pad) if b - a == C5_MICRO else ro.rows([options] * (b - a))
+            out[a:b].copy_(model.decide(ids[: b - a], st, ro, r, i, p), non_blocking=True)
+
+    job(min(C5_MICRO, hi - lo))  # warm-up: the prefix and one micro-batch
+    torch.cuda.synchronize(dev)
+    shard.check_peers(tag="decisions")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    job(hi - lo)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = shard.max_over_ranks(e0.elapsed_time(e1))
+    if world > 1:
+        dist.barrier()
+    tokens = world * C5_PREFIX + C5_REQUESTS * C5_SUFFIX
+    ok = bool(torch.isfinite(out).all()) and float((out.sum(-1) - 1).abs().max()) < 1e-4
+    if rank != 0:
+        return None
+    return {"value": round(C5_REQUESTS / (ms * 1e-3), 1), "unit": "decisions/s", "n_gpus": world,
+            "ms": round(ms, 1), "requests": C5_REQUESTS, "prefix_tokens": C5_PREFIX, "suffix_tokens": C5_SUFFIX,
+            "options": C5_OPTIONS, "micro_batch": C5_MICRO, "scaling": "strong (4096 requests in all)",
+            "linear_tflops": round(model.flops_per_token() * tokens / (ms * 1e-3) / 1e12, 1),
+            "probabilities_ok": ok,
+            "h2d_bytes": int(C5_REQUESTS * C5_SUFFIX * 8 + world * C5_PREFIX * 8),
+            "d2h_bytes": int(C5_REQUESTS * C5_OPTIONS * 4),
+            "model": "random-init 32-layer hybrid, 24 Gated DeltaNet + 8 attention layers, hidden 2560, SwiGLU 9728, "
+                     "vocab 151936, every linear FP8-block (GPT-2 scaled init)",
+            "timed": "the prefix on every GPU, then the rank's requests in micro-batches of 128 (suffix ids copied in "
+                     "from pinned host memory, probabilities copied out), CUDA events, max over ranks"}
+
+
+def c5_cpu_baseline():
+    """The oracle (numpy, all host threads) on one request of the C5 layer sizes, on one 3 : 1 period of layers
+    (4 of 32), a 64-token prefix and 32 suffix tokens; per-token time x 8 periods x 256 tokens = seconds a decision."""
+    import numpy as np
+    from oracle import hybrid as ohy
+
+    class Cfg:  # C5's sizes (basal_b200.hybrid.C5), 4 layers
+        layers, hidden, heads, kv_heads, head_dim, inter, vocab = 4, 2560, 16, 4, 128, 9728, 151936
+        lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim, conv, eps, rotary_dims, rope_theta = 16, 32, 128, 128, 4, \
+            1e-6, 32, 10000.0
+        key_dim, value_dim = 2048, 4096
+        conv_dim = 8192
+        in_sizes = (8192, 4096, 32, 32, 64)
+        qkv_sizes = (4096, 512, 512)
+        kinds = ["linear_attention"] * 3 + ["full_attention"]
+    cfg = Cfg()
+    rng = np.random.default_rng(0)
+    n = lambda *sh, std=0.02: (rng.standard_normal(sh, dtype=np.float32) * np.float32(std))  # noqa: E731
+
+    def q(a):  # random finite e4m3 codes (sign | 0x00..0x7e) and 128 x 128 block scales of a weight's shape
+        codes = rng.integers(0, 0x7F, a.shape, dtype=np.uint8) | (rng.integers(0, 2, a.shape, dtype=np.uint8) << 7)
+        return codes, np.full((a.shape[0] // 128, a.shape[1] // 128), 0.02 / 448 * 3, np.float32)
+    D = cfg.hidden
+    W = {"embed": n(512, D, std=1.0), "head": n(8, D), "final_norm": n(D), "layers": []}
+    for kind in cfg.kinds:
+        L = dict(kind=kind, nw=n(D), mlp_nw=n(D), gate_up=q(n(2 * cfg.inter, D)), down=q(n(D, cfg.inter)))
+        if kind == "linear_attention":
+            L.update(w_in=q(n(sum(cfg.in_sizes), D)), conv=n(cfg.conv_dim, 4, std=0.3), A_log=np.zeros(32, np.float32),
+                     dt_bias=np.ones(32, np.float32), gnorm=np.ones(128, np.float32), out=q(n(D, cfg.value_dim)))
+        else:
+            L.update(w_qkv=q(n(sum(cfg.qkv_sizes), D)), q_norm=n(128), k_norm=n(128), o=q(n(D, 2048)))
+        W["layers"].append(L)
+    _, st = ohy.prefix(W, cfg, rng.integers(0, 512, 64))
+    sfx = rng.integers(0, 512, 32)
+    t0 = time.perf_counter()
+    ohy.decide(W, cfg, st, sfx, np.arange(8))
+    dt = time.perf_counter() - t0
+    sec = dt / 32 * (32 / 4) * C5_SUFFIX
+    return {"value": round(1.0 / sec, 4), "unit": "decisions/s", "cores": blas_threads(), "kind": "port",
+            "sample": f"1 request: 32 suffix tokens through 4 of the 32 layers in {dt:.1f} s (after a 64-token prefix), "
+                      "scaled to 32 layers and 256 tokens; the FP8 weights dequantised on every call, as the "
+                      "reference's CPU linear does (basal/blockquant.py:54-60)"}
+
+
 # C5's projections (hidden 2560; 16 query and 4 key/value heads of 128; SwiGLU 9728), as (name, N, K)
 C5_PROJ = (("qkv", 3072, 2560), ("o", 2560, 2048), ("gate_up", 19456, 2560), ("down", 2560, 9728))
 
@@ -660,6 +790,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--case", choices=sorted(CASES), help="run one small profiling case instead of the benchmark")
+    ap.add_argument("--no-decisions", action="store_true", help="skip the C5 decisions/s measurement")
+    ap.add_argument("--decisions-only", action="store_true", help="only the C5 decisions/s measurement (one line)")
     ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout, "
                     "glu,res) instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
     args = ap.parse_args()
@@ -700,6 +832,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.decisions_only:
+            import torch
+            torch.cuda.set_device(local_rank)
+            d = run_decisions(rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps({"metric": "decisions/s (BASELINE config 5)", **d}), flush=True)
+            return
         run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -203,6 +203,16 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream);
 
+/* The gated delta rule of the Gated DeltaNet layers (transformers' torch_chunk_gated_delta_rule / fla's
+ * chunk_gated_delta_rule, called by basal/gdn_graph.py:81-87, :492-493), fp32: per row r and value head h, from the
+ * state s0 [s0_rows, H, 128, 128] (s0_rows 1: shared by every row; NULL: zeros), over T tokens of q, k, v
+ * [rows, H, T, 128] (q, k l2-normed, q scaled as basal200_gdn_prep leaves them), g, beta [rows, H, T]:
+ * S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T, o_t = S_t^T q_t -> o [rows, H, T, 128], and
+ * the final state into s_out [rows, H, 128, 128] (may be NULL). Computed over chunks of 64 tokens. */
+int basal200_gdn_chunk_rule(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                            const float* s0, int s0_rows, float* o, float* s_out, int rows, int H, int T,
+                            void* stream);
+
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)
 

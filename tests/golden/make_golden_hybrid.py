@@ -22,7 +22,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 SIZES = dict(layers=4, hidden=32, heads=2, kv_heads=1, head_dim=16, inter=64, vocab=64, lin_k_heads=2,
              lin_v_heads=4, lin_k_dim=8, lin_v_dim=8, conv=4, full_every=4, eps=1e-6, rotary_frac=0.5,
-             rope_theta=10000.0, chunk=64)
+             rope_theta=10000.0)
 P, S = 70, 37   # a prefix past one chunk of 64, a suffix of a partial chunk
 
 

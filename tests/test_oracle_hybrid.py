@@ -11,8 +11,49 @@ import numpy as np
 import pytest
 import torch
 
+import torch.nn.functional as F
+
 from conftest import GOLDEN, golden
 from oracle import hybrid as ohy
+
+
+def l2norm(x, eps=1e-6):
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
+
+
+def chunk_delta_rule(q, k, v, g, beta, s0, chunk):
+    """The gated delta rule over chunks in plain torch (fp32; the chunked form the CUDA kernel basal::gdn_chunk_rule
+    computes): q, k [b, H, T, dk], v [b, H, T, dv], g, beta [b, H, T], s0 [b or 1, H, dk, dv] -> (o [b, H, Tp, dv],
+    the final state), Tp = T rounded up to whole chunks. Within a chunk with cumulative gates G, the rows' updates
+    solve the unit lower-triangular system (I + A), A_ij = beta_i (k_i . k_j) e^{G_i - G_j} for j < i."""
+    b, H, T, dk = k.shape
+    dv = v.shape[-1]
+    pad = -T % chunk
+    if pad:
+        q, k, v = (F.pad(t, (0, 0, 0, pad)) for t in (q, k, v))
+        g, beta = F.pad(g, (0, pad)), F.pad(beta, (0, pad))
+    n = (T + pad) // chunk
+    q, k, v = (t.reshape(b, H, n, chunk, -1) for t in (q, k, v))
+    G = g.reshape(b, H, n, chunk).cumsum(-1)
+    beta = beta.reshape(b, H, n, chunk)
+    low = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
+    both = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(0)
+    diff = (G[..., :, None] - G[..., None, :]).masked_fill(~both, 0.0).exp().masked_fill(~both, 0.0)
+    A = (beta[..., None] * (k @ k.transpose(-1, -2)) * diff).masked_fill(~low, 0.0)
+    eye = torch.eye(chunk, dtype=q.dtype, device=q.device)
+    Tinv = torch.linalg.solve_triangular(A + eye, eye.expand_as(A), upper=False, unitriangular=True)
+    U = Tinv @ (beta[..., None] * v)
+    W = Tinv @ (beta[..., None] * G.exp()[..., None] * k)
+    qk = (q @ k.transpose(-1, -2)) * diff
+    qg = q * G.exp()[..., None]
+    kd = k * (G[..., -1:] - G).exp()[..., None]
+    S = s0.expand(b, H, dk, dv).contiguous()
+    out = torch.empty(b, H, n, chunk, dv, dtype=q.dtype, device=q.device)
+    for c in range(n):
+        vn = U[:, :, c] - W[:, :, c] @ S
+        out[:, :, c] = qg[:, :, c] @ S + qk[:, :, c] @ vn
+        S = G[:, :, c, -1, None, None].exp() * S + kd[:, :, c].transpose(-1, -2) @ vn
+    return out.reshape(b, H, n * chunk, dv), S
 
 
 def sizes():
@@ -57,10 +98,8 @@ def test_bf16_rounding_equals_torch():
 
 @pytest.mark.parametrize("T, chunk", [(150, 64), (64, 64), (5, 64), (130, 32)])
 def test_chunked_delta_rule_equals_the_per_token_definition(T, chunk):
-    """basal_b200.hybrid.chunk_delta_rule (the chunked form the GPU runs, in torch) against oracle.hybrid.delta_rule
-    (the per-token definition), from a non-zero initial state, with ragged last chunks. Plain torch on CPU tensors:
-    the function is the same code the model runs on the GPU."""
-    from basal_b200.hybrid import chunk_delta_rule, l2norm
+    """The chunked form (chunk_delta_rule above, the algorithm of the CUDA kernel basal::gdn_chunk_rule) against
+    oracle.hybrid.delta_rule (the per-token definition), from a non-zero initial state, with ragged last chunks."""
     g = torch.Generator().manual_seed(T)
     b, H, dk, dv = 2, 3, 16, 8
     q = l2norm(torch.randn(b, H, T, dk, generator=g)) * dk ** -0.5
