@@ -456,28 +456,7 @@ def run_sweep(fmts):
     flush = torch.ones(64 << 20, device=dev)
     reps = 4
 
-    def graph_us(fn, n=15):
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            fn()
-        torch.cuda.current_stream().wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(n):
-            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1) * 1e3)
-        del g
-        return statistics.median(ts)
+    graph_us = graph_timer(torch, flush)
 
     base = graph_us(lambda: flush.sum())
     gen = torch.Generator(device=dev).manual_seed(0)
@@ -705,6 +684,130 @@ def c5_cpu_baseline():
                       "reference's CPU linear does (basal/blockquant.py:54-60)"}
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# the reference's own GPU paths on this box (its package installed unmodified under baseline/_ref)
+# ------------------------------------------------------------------------------------------------------------------
+def graph_timer(torch, flush):
+    """us of fn() captured in a CUDA graph after a read of `flush` (L2 holds no operand), minus the read alone; median
+    of n replays."""
+    def graph_us(fn, n=15):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        del g
+        return statistics.median(ts)
+    return graph_us
+
+
+def run_ref_sweep(fmts):
+    """The reference's GPU paths (basal 2.8.1 from baseline/_ref, through its own public functions) on the inputs
+    run_sweep draws (the same seeds and draw order, so the same operands): FP8 / INT8 the Triton block GEMM
+    (blockquant.py:63-106, what runs on B200: fp8block.sm90() is false off Hopper) and the linear (its
+    torch.compile'd act_quant + that GEMM); NVFP4 cuBLAS through F.scaled_mm (nvfp4._mm) and the linear (its Triton
+    quantiser + cuBLAS); "c2": C2's projection set. Run in a process of its own: the reference registers the same
+    basal:: op names as basal_b200. One JSON line per point, "impl": "reference"."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "basal")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref holds no reference install"}))
+        return
+    sys.path.insert(0, ref)
+    import torch
+
+    from basal import fp8block, int8block, nvfp4
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    flush = torch.ones(64 << 20, device=dev)
+    graph_us = graph_timer(torch, flush)
+    base = graph_us(lambda: flush.sum())
+    reps = 4
+    gen = torch.Generator(device=dev).manual_seed(0)
+    if "c2" in fmts:
+        run_ref_c2(fp8block, graph_us, base, flush, dev)
+    for fmt in [f for f in fmts if f in ("fp8", "int8", "nvfp4")]:
+        mod = {"fp8": fp8block, "int8": int8block}.get(fmt)
+        for N, K in ((2048, 2048), (12288, 2048), (2048, 6144)):
+            ws = [torch.randn(N, K, device=dev, generator=gen) * 0.02 for _ in range(reps)]
+            if fmt == "nvfp4":
+                lins = []
+                for w in ws:
+                    lin = torch.nn.Linear(K, N, bias=False, device=dev)
+                    with torch.no_grad():
+                        lin.weight.copy_(w)
+                    lins.append(lin)
+            else:
+                qw = [mod.quantize(w) for w in ws]
+            del ws
+            for M in (16, 128, 1024, 8192):
+                x = torch.randn(M, K, device=dev, generator=gen)
+                if fmt == "nvfp4":
+                    x = torch.where(torch.rand(M, K, device=dev, generator=gen) < 0.01, x * 20, x).bfloat16()
+                    fs = [nvfp4.NVFP4Linear.of(lin, float(x.abs().max())) for lin in lins]
+                    qa, sa = nvfp4.act_quant(x, fs[0].inv_g)
+                    gemm = [lambda f=f: nvfp4._mm(qa, sa, f.weight, f.weight_scale, f.alpha, M, torch.bfloat16)
+                            for f in fs]
+                    linear = [lambda f=f: f(x) for f in fs]
+                else:
+                    x = x.bfloat16()
+                    qa, sa = mod.act_quant(x)
+                    gemm = [lambda q=q, s=s: mod.gemm(qa, sa, q, s, torch.bfloat16) for q, s in qw]
+                    linear = [lambda q=q, s=s: mod.linear(x, q, s) for q, s in qw]
+
+                def body(fns):
+                    flush.sum()
+                    for fn in fns:
+                        fn()
+                tg = (graph_us(lambda: body(gemm)) - base) / reps
+                tl = (graph_us(lambda: body(linear)) - base) / reps
+                print(json.dumps({"impl": "reference", "format": fmt, "M": M, "N": N, "K": K, "gemm_us": round(tg, 2),
+                                  "gemm_tflops": round(2 * M * N * K / tg / 1e6, 1), "linear_us": round(tl, 2),
+                                  "kernel": "cuBLAS block-scaled FP4 (F.scaled_mm)" if fmt == "nvfp4" else
+                                  "Triton block GEMM"}), flush=True)
+    print(json.dumps({"impl": "reference", "peak_source": pk["source"], "torch": torch.__version__}))
+
+
+def run_ref_c2(fp8block, graph_us, base, flush, dev):
+    """C2's projection set through the reference's FP8 linear (its act_quant + Triton block GEMM), one step captured
+    in a CUDA graph after an L2-clean read: TFLOP/s beside this build's bench value."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    M = int(torch.randint(128, 2049, (64,), generator=g).sum())  # C2's packed rows (shard.varlen_lengths, seed 0)
+    gen = torch.Generator(device=dev).manual_seed(1000)
+    xs = {HIDDEN: torch.randn(M, HIDDEN, device=dev, generator=gen).bfloat16(),
+          INTER: torch.randn(M, INTER, device=dev, generator=gen).bfloat16()}
+    ws = {name: fp8block.quantize(torch.randn(n, k, device=dev, generator=gen) * 0.02) for name, n, k in PROJ}
+
+    def step():
+        flush.sum()
+        for name, n, k in PROJ:
+            fp8block.linear(xs[k], *ws[name])
+    t = graph_us(step, n=5) - base
+    gemm_t = {}
+    for name, n, k in PROJ:
+        qa, sa = fp8block.act_quant(xs[k])
+        gemm_t[name] = graph_us(lambda: (flush.sum(), fp8block.gemm(qa, sa, *ws[name], torch.bfloat16)), n=5) - base
+    print(json.dumps({"impl": "reference", "workload": "C2", "rows": M, "step_us": round(t, 1),
+                      "tflops": round(M * flops_per_row() / t / 1e6, 1),
+                      "gemm_tflops": {name: round(2 * M * n * k / gemm_t[name] / 1e6, 1) for name, n, k in PROJ},
+                      "path": "fp8block.linear: torch.compile'd act_quant + the Triton block GEMM"}), flush=True)
+
+
 # C5's projections (hidden 2560; 16 query and 4 key/value heads of 128; SwiGLU 9728), as (name, N, K)
 C5_PROJ = (("qkv", 3072, 2560), ("o", 2560, 2048), ("gate_up", 19456, 2560), ("down", 2560, 9728))
 
@@ -809,6 +912,9 @@ def main():
             run_sweep_tp(rank, world, local_rank)
         finally:
             dist.destroy_process_group()
+        return
+    if args.sweep and args.sweep.startswith("ref"):  # ref,fp8,int8,nvfp4,c2: the reference's GPU paths
+        run_ref_sweep(args.sweep.split(",")[1:])
         return
     if args.sweep:
         run_sweep(args.sweep.split(","))
