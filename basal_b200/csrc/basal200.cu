@@ -869,15 +869,17 @@ int rms_quant(const void* x, int xt, const void* w, float eps, int64_t M, int64_
 int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_rows, const void* conv, int kw,
              const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk, int Hv, float* q,
              float* k, float* v, float* beta, float* g, cudaStream_t st) {
-  if (rows < 0 || T < 0 || Hk <= 0 || Hv <= 0 || kw < 1 || kw > 8) return BASAL200_ERR_ARG;
-  if (Hv % Hk) return BASAL200_ERR_SHAPE;
+  if (rows < 0 || T < 0 || Hk <= 0 || Hv <= 0 || kw < 1) return BASAL200_ERR_ARG;
+  if (Hv % Hk || kw != 4) return BASAL200_ERR_SHAPE;  // the kernel's convolution has 4 taps (Qwen 3.5's)
   if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
   if (rows == 0 || T == 0) return BASAL200_OK;
   if (!proj || !conv || !A_log || !dt_bias || !q || !k || !v || !beta || !g) return BASAL200_ERR_ARG;
   if (tail && tail_rows != 1 && tail_rows != rows) return BASAL200_ERR_ARG;
   const int64_t C = (int64_t)(2 * Hk + Hv) * 128;
   if (ld < C || b_off < 0 || a_off < 0 || b_off + Hv > ld || a_off + Hv > ld) return BASAL200_ERR_SHAPE;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return BASAL200_ERR_ALIGN;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(conv) || (ld % 4) ||
+      (reinterpret_cast<uintptr_t>(proj) & 7) || (tail && (reinterpret_cast<uintptr_t>(tail) & 7)))
+    return BASAL200_ERR_ALIGN;  // 8-byte loads of 4 channels, 16-byte loads of 4 channels' weights
   const int64_t items = (int64_t)rows * T * Hk;  // a warp each, 8 a CTA
   if ((items + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
@@ -896,7 +898,6 @@ int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_ro
   p.T = T;
   p.Hk = Hk;
   p.Hv = Hv;
-  p.KW = kw;
   p.q_scale = 0.08838834764831845f;  // 128^-1/2, rounded to fp32 as torch rounds the Python float
   p.q = q;
   p.k = k;

@@ -1,6 +1,6 @@
 // The gated delta rule of the Gated DeltaNet layers (the recurrence of transformers' torch_chunk_gated_delta_rule /
 // fla's chunk_gated_delta_rule, which the reference's Qwen 3.5 graph forward calls, basal/gdn_graph.py:81-87,
-// :492-493), over chunks of 64 tokens, in fp32.
+// :492-493), over chunks of 64 tokens, with fp32 accuracy.
 //
 // Per value head, with l2-normed keys k_t, scaled queries q_t, values v_t, gates g_t <= 0 and beta_t in (0, 1), the
 // state S [dk = 128, dv = 128] follows S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T and the
@@ -9,12 +9,14 @@
 //   U = T (beta V),  W = T (beta e^G K),  V' = U - W S,
 //   O = e^G (Q S) + (Q K^T (.) e^{G_i - G_j}, j <= i) V',  S <- e^{G_last} S + (e^{G_last - G} K)^T V'.
 //
-// A CTA owns one (row, value head) and one half of the value dimension (64 of S's 128 columns): the products that do
-// not involve V (A, T, W, Q K^T) are computed by both halves. 256 threads; every product is a register-tiled fp32 FMA
-// loop over shared memory with the left operand stored transposed ([k][rows]: a thread's rows are one float4) and the
-// right one row-major ([k][cols]: a thread's columns are one or two float4), so every shared-memory read is a
-// contiguous vector. T is found by 16 x 16 blocks: the diagonal blocks by forward substitution (a warp each), the
-// off-diagonal ones by T_IJ = -T_II sum_{M = J .. I - 1} A_IM T_MJ, one block distance at a time.
+// A CTA owns one (row, value head) and one half of the value dimension (64 of S's 128 columns); the products that do
+// not involve V (A, T, W, Q K^T) are computed by both halves. 256 threads = 8 warps. Every product runs on the tensor
+// cores as mma.sync m16n8k8 with TF32 operands split in two (x = hi + lo, both TF32; each product is hi*hi + hi*lo +
+// lo*hi with an fp32 accumulator, which keeps fp32 accuracy). Operands sit in shared memory in their natural
+// row-major layouts, each row padded so that the fragment loads of a warp hit 32 different banks (leading dimensions
+// of 4 mod 32 words for matrices read along rows, 8 mod 32 for matrices read down columns). T is found by 16 x 16
+// blocks: the diagonal blocks by forward substitution (a warp each), the off-diagonal ones by
+// T_IJ = -T_II sum_{M = J .. I - 1} A_IM T_MJ, one block distance at a time.
 #pragma once
 #include "common.cuh"
 
@@ -25,7 +27,10 @@ constexpr int CH = 64;    // tokens a chunk
 constexpr int DK = 128;   // key dim
 constexpr int DV = 128;   // value dim
 constexpr int DH = 64;    // value columns a CTA owns
-constexpr int NT = 256;   // threads
+constexpr int NT = 256;   // threads (8 warps)
+constexpr int LK = DK + 4;   // row stride of Q, K, W (read along rows and, for K, down columns)
+constexpr int LH = DH + 8;   // row stride of S and V (read down columns)
+constexpr int LC = CH + 4;   // row stride of A, T, P (read along rows)
 
 struct Params {
   const float* q;      // [rows, H, T, 128] (l2-normed, scaled)
@@ -41,107 +46,128 @@ struct Params {
 };
 
 struct Smem {
-  float S[DK * DH];    // the state's columns of this CTA, [kk][c]
-  float K[CH * DK];    // keys, row-major [i][kk]
-  float KT[DK * CH];   // keys transposed [kk][i]; after the products with K^T: W transposed [kk][i]
-  float QT[DK * CH];   // queries transposed [kk][i]
-  float V[CH * DH];    // beta V, then V' = U - W S ([i][c])
-  float A[CH * CH];    // A row-major [i][j]
-  float Tm[CH * CH];   // T row-major, then transposed [j][i]
-  float PT[CH * CH];   // (Q K^T (.) decay, causal) transposed [j][i]
+  float S[DK * LH];    // the state's columns of this CTA, [kk][c]
+  float K[CH * LK];    // keys [i][kk]
+  float Q[CH * LK];    // queries [i][kk]
+  float W[CH * LK];    // T (beta e^G K) [i][kk]
+  float V[CH * LH];    // beta V, then V' = U - W S [i][c]
+  float A[CH * LC];    // A [i][j]
+  float Tm[CH * LC];   // T [i][j]
+  float P[CH * LC];    // (Q K^T (.) decay, causal) [i][j]; scratch of the inverse before
   float G[CH];         // cumulative gates
   float B[CH];         // beta
+  float EB[CH];        // beta_i e^{G_i}
+  float ED[CH];        // e^{G_last - G_i}
 };
 
-// acc[RT][CT] += sum_k AT[k][r0 + i] * B[k][c0 + j] (fp32 FMAs, k ascending); RT, CT multiples of 4.
-template <int RT, int CT, int KN, int LDA, int LDB>
-__device__ __forceinline__ void mm(const float* __restrict__ AT, const float* __restrict__ Bm, int r0, int c0,
-                                   float (&acc)[RT][CT]) {
-#pragma unroll 4
-  for (int k = 0; k < KN; ++k) {
-    float a[RT], b[CT];
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  uint32_t h, l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  const float r = x - __uint_as_float(h);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+  hi = h;
+  lo = l;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// acc[j] (the 16 x 8 tile at rows r0.., columns n0 + 8 j..) += sum_{k < KN} A(r, k) B(k, n) for j < NJ, one warp:
+// fa(r, k) and fb(k, n) read the operands (from shared memory, scaled as the caller needs). Fragment layouts of
+// m16n8k8 (g = lane / 4, t = lane % 4): A (g | g + 8, t | t + 4), B (k = t | t + 4, n = g), C (g | g + 8, 2t, 2t + 1).
+template <int NJ, int KN, typename FA, typename FB>
+__device__ __forceinline__ void warp_mm(float (&acc)[NJ][4], int r0, int n0, FA fa, FB fb, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < KN; k0 += 8) {
+    uint32_t ah[4], al[4];
+    split_tf32(fa(r0 + g, k0 + t), ah[0], al[0]);
+    split_tf32(fa(r0 + g + 8, k0 + t), ah[1], al[1]);
+    split_tf32(fa(r0 + g, k0 + t + 4), ah[2], al[2]);
+    split_tf32(fa(r0 + g + 8, k0 + t + 4), ah[3], al[3]);
+    uint32_t bh[NJ][2], bl[NJ][2];
 #pragma unroll
-    for (int i = 0; i < RT; i += 4) *reinterpret_cast<float4*>(&a[i]) = *reinterpret_cast<const float4*>(AT + k * LDA + r0 + i);
+    for (int j = 0; j < NJ; ++j) {
+      split_tf32(fb(k0 + t, n0 + 8 * j + g), bh[j][0], bl[j][0]);
+      split_tf32(fb(k0 + t + 4, n0 + 8 * j + g), bh[j][1], bl[j][1]);
+    }
+    // the three partial products as three passes over the column tiles: consecutive MMAs use different
+    // accumulators (small terms first, as the sum is formed per accumulator in the same order either way)
 #pragma unroll
-    for (int j = 0; j < CT; j += 4) *reinterpret_cast<float4*>(&b[j]) = *reinterpret_cast<const float4*>(Bm + k * LDB + c0 + j);
+    for (int j = 0; j < NJ; ++j) mma_tf32(acc[j], al, bh[j][0], bh[j][1]);
 #pragma unroll
-    for (int i = 0; i < RT; ++i)
+    for (int j = 0; j < NJ; ++j) mma_tf32(acc[j], ah, bl[j][0], bl[j][1]);
 #pragma unroll
-      for (int j = 0; j < CT; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    for (int j = 0; j < NJ; ++j) mma_tf32(acc[j], ah, bh[j][0], bh[j][1]);
   }
 }
 
-template <int RT, int CT>
-__device__ __forceinline__ void zero(float (&acc)[RT][CT]) {
+template <int NJ>
+__device__ __forceinline__ void zero(float (&acc)[NJ][4]) {
 #pragma unroll
-  for (int i = 0; i < RT; ++i)
-#pragma unroll
-    for (int j = 0; j < CT; ++j) acc[i][j] = 0.0f;
+  for (int j = 0; j < NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 }
 
-// T = (I + A)^-1 for the strictly lower A [64][64] (row-major in sh.A) -> sh.Tm row-major.
+// T = (I + A)^-1 for the strictly lower A [64][64] (sh.A) -> sh.Tm; sh.P is scratch.
 __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
+  float* T = sh.Tm;
+  const float* A = sh.A;
   // diagonal 16 x 16 blocks: warp b, lane j < 16 owns column j of block b; rows in order
   if (warp < 4) {
     const int b0 = warp * 16;
-    float* T = sh.Tm;
-    const float* A = sh.A;
     if (lane < 16)
-      for (int i = 0; i < 16; ++i) T[(b0 + i) * CH + b0 + lane] = (i == lane) ? 1.0f : 0.0f;
+      for (int i = 0; i < 16; ++i) T[(b0 + i) * LC + b0 + lane] = (i == lane) ? 1.0f : 0.0f;
     __syncwarp();
     for (int i = 1; i < 16; ++i) {
       float acc = 0.0f;
       if (lane < i) {
-        for (int m = lane; m < i; ++m) acc = fmaf(A[(b0 + i) * CH + b0 + m], T[(b0 + m) * CH + b0 + lane], acc);
+        for (int m = lane; m < i; ++m) acc = fmaf(A[(b0 + i) * LC + b0 + m], T[(b0 + m) * LC + b0 + lane], acc);
       }
       __syncwarp();
-      if (lane < i) T[(b0 + i) * CH + b0 + lane] = -acc;
+      if (lane < i) T[(b0 + i) * LC + b0 + lane] = -acc;
       __syncwarp();
     }
   }
-  // the blocks above the diagonal are zero
-  for (int e = tid; e < CH * CH; e += NT) {
+  for (int e = tid; e < CH * CH; e += NT) {  // the blocks above the diagonal are zero
     const int i = e / CH, j = e % CH;
-    if ((j >> 4) > (i >> 4)) sh.Tm[e] = 0.0f;
+    if ((j >> 4) > (i >> 4)) T[i * LC + j] = 0.0f;
   }
   __syncthreads();
-  // off-diagonal blocks, distance d = I - J: a warp per block, lane owns 8 of its 256 entries (row lane / 2, columns
-  // (lane % 2) * 8 ..)
+  // off-diagonal blocks, distance d = I - J: a warp per block, lane owns row lane / 2, columns (lane % 2) * 8 ..
   for (int d = 1; d < 4; ++d) {
     float x[8];
-    const int blk = warp;  // block J = blk, I = blk + d
+    const int blk = warp;
     const bool on = blk + d < 4;
     const int I0 = (blk + d) * 16, J0 = blk * 16;
     const int r = lane >> 1, cb = (lane & 1) * 8;
     if (on) {
 #pragma unroll
       for (int c = 0; c < 8; ++c) x[c] = 0.0f;
-      // X = sum_{M = J .. I - 1} A_IM T_MJ
-      for (int m = J0; m < I0; ++m) {
-        const float a = sh.A[(I0 + r) * CH + m];
+      for (int m = J0; m < I0; ++m) {  // X = sum_{M = J .. I - 1} A_IM T_MJ
+        const float a = A[(I0 + r) * LC + m];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) x[c] = fmaf(a, sh.Tm[m * CH + J0 + cb + c], x[c]);
+        for (int c = 0; c < 8; ++c) x[c] = fmaf(a, T[m * LC + J0 + cb + c], x[c]);
       }
-    }
-    __syncthreads();  // every warp has read the blocks it needs before any block of distance d is written
-    // T_IJ = -T_II X: stage X in the (I, J) block of PT (free until the products with Q K^T)
-    if (on) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) sh.PT[(I0 + r) * CH + J0 + cb + c] = x[c];
+      for (int c = 0; c < 8; ++c) sh.P[(I0 + r) * LC + J0 + cb + c] = x[c];
     }
     __syncthreads();
-    if (on) {
+    if (on) {  // T_IJ = -T_II X
       float y[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) y[c] = 0.0f;
       for (int m = 0; m < 16; ++m) {
-        const float t = sh.Tm[(I0 + r) * CH + I0 + m];
+        const float tt = T[(I0 + r) * LC + I0 + m];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) y[c] = fmaf(t, sh.PT[(I0 + m) * CH + J0 + cb + c], y[c]);
+        for (int c = 0; c < 8; ++c) y[c] = fmaf(tt, sh.P[(I0 + m) * LC + J0 + cb + c], y[c]);
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) sh.Tm[(I0 + r) * CH + J0 + cb + c] = -y[c];
+      for (int c = 0; c < 8; ++c) T[(I0 + r) * LC + J0 + cb + c] = -y[c];
     }
     __syncthreads();
   }
@@ -150,47 +176,38 @@ __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
 __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sh = *reinterpret_cast<Smem*>(smem_raw);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
   const int half = blockIdx.x & 1;
   const int rh = blockIdx.x >> 1;  // r * H + h
   const int r = rh / p.H, h = rh % p.H;
   const int64_t base = (int64_t)rh * p.T;  // token row of (r, h, t = 0) in q / k / v / o, and in g / beta
   pdl_wait();
-  // the initial state's columns of this half
-  for (int e = tid * 4; e < DK * DH; e += NT * 4) {
+  for (int e = tid * 4; e < DK * DH; e += NT * 4) {  // the initial state's columns of this half
     const int kk = e / DH, c = e % DH;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.s0) {
       const int sr = p.s0_rows == 1 ? 0 : r;
       s = *reinterpret_cast<const float4*>(p.s0 + (((int64_t)sr * p.H + h) * DK + kk) * DV + half * DH + c);
     }
-    *reinterpret_cast<float4*>(&sh.S[e]) = s;
+    *reinterpret_cast<float4*>(&sh.S[kk * LH + c]) = s;
   }
-  const int rb = tid >> 4, cb = tid & 15;
+  // the 16-row tile and the 8-column tiles of this warp: 64 x 64 products (2 warps a row tile, 4 column tiles each),
+  // 64 x 128 (8 column tiles each), 128 x 64 (a row tile each, 8 column tiles)
+  const int rt = (warp >> 1) * 16, nq = (warp & 1) * 32, nw = (warp & 1) * 64;
+  const int rs = warp * 16, ns = 0;
   for (int t0 = 0; t0 < p.T; t0 += CH) {
     const int n = min(CH, p.T - t0);
-    // ---- chunk loads: K row-major (float4 along kk), K and Q transposed (a lane per token), beta V, G, beta ----
+    // ---- chunk loads: K and Q row-major, beta, G ----
     for (int e = tid; e < CH * DK / 4; e += NT) {
       const int i = e / (DK / 4), f = e % (DK / 4);
-      float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < n) val = __ldg(reinterpret_cast<const float4*>(p.k + (base + t0 + i) * DK) + f);
-      *reinterpret_cast<float4*>(&sh.K[i * DK + 4 * f]) = val;
-    }
-    for (int e = tid; e < CH * DK / 4; e += NT) {
-      const int i = e % CH, f = e / CH;
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
       if (i < n) {
         kv = __ldg(reinterpret_cast<const float4*>(p.k + (base + t0 + i) * DK) + f);
         qv = __ldg(reinterpret_cast<const float4*>(p.q + (base + t0 + i) * DK) + f);
       }
-      sh.KT[(4 * f + 0) * CH + i] = kv.x;
-      sh.KT[(4 * f + 1) * CH + i] = kv.y;
-      sh.KT[(4 * f + 2) * CH + i] = kv.z;
-      sh.KT[(4 * f + 3) * CH + i] = kv.w;
-      sh.QT[(4 * f + 0) * CH + i] = qv.x;
-      sh.QT[(4 * f + 1) * CH + i] = qv.y;
-      sh.QT[(4 * f + 2) * CH + i] = qv.z;
-      sh.QT[(4 * f + 3) * CH + i] = qv.w;
+      *reinterpret_cast<float4*>(&sh.K[i * LK + 4 * f]) = kv;
+      *reinterpret_cast<float4*>(&sh.Q[i * LK + 4 * f]) = qv;
     }
     if (tid < CH) {
       sh.B[tid] = tid < n ? __ldg(p.beta + base + t0 + tid) : 0.0f;
@@ -215,97 +232,73 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
         val.z *= bt;
         val.w *= bt;
       }
-      *reinterpret_cast<float4*>(&sh.V[i * DH + 4 * f]) = val;
+      *reinterpret_cast<float4*>(&sh.V[i * LH + 4 * f]) = val;
     }
     __syncthreads();
-    // ---- A = beta_i (k_i . k_j) e^{G_i - G_j} (j < i); P = (q_i . k_j) e^{G_i - G_j} (j <= i), stored transposed ----
+    if (tid < CH) {  // read after the inverse's barriers
+      sh.EB[tid] = sh.B[tid] * expf(sh.G[tid]);
+      sh.ED[tid] = expf(sh.G[CH - 1] - sh.G[tid]);
+    }
+    // ---- A_ij = beta_i (k_i . k_j) e^{G_i - G_j} for j < i ----
     {
-      float kk[4][4], qk[4][4];
+      float kk[4][4];
       zero(kk);
-      zero(qk);
-      mm<4, 4, DK, CH, CH>(sh.KT, sh.KT, rb * 4, cb * 4, kk);
-      mm<4, 4, DK, CH, CH>(sh.QT, sh.KT, rb * 4, cb * 4, qk);
+      warp_mm<4, DK>(kk, rt, nq, [&](int i, int c) { return sh.K[i * LK + c]; },
+                     [&](int c, int j) { return sh.K[j * LK + c]; }, lane);
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int i = rb * 4 + a;
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int j = cb * 4 + b;
-          const float dec = j <= i ? expf(sh.G[i] - sh.G[j]) : 0.0f;
-          sh.A[i * CH + j] = j < i ? sh.B[i] * kk[a][b] * dec : 0.0f;
-          sh.PT[j * CH + i] = qk[a][b] * dec;
+        for (int e = 0; e < 4; ++e) {
+          const int i = rt + g8 + (e >> 1) * 8, jj = nq + 8 * j + 2 * t4 + (e & 1);
+          sh.A[i * LC + jj] = jj < i ? sh.B[i] * kk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
         }
-      }
     }
     __syncthreads();
-    // ---- T = (I + A)^-1 (uses PT's blocks below the diagonal as scratch, so P is stored again after) ----
+    unit_lower_inverse(sh, tid);  // ends with a barrier
+    // ---- P = (q_i . k_j) e^{G_i - G_j} for j <= i (into P, the inverse's scratch until now) ----
     {
-      float save[4][4];
+      float qk[4][4];
+      zero(qk);
+      warp_mm<4, DK>(qk, rt, nq, [&](int i, int c) { return sh.Q[i * LK + c]; },
+                     [&](int c, int j) { return sh.K[j * LK + c]; }, lane);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) save[a][b] = sh.PT[(rb * 4 + a) * CH + cb * 4 + b];
-      __syncthreads();
-      unit_lower_inverse(sh, tid);
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) sh.PT[(rb * 4 + a) * CH + cb * 4 + b] = save[a][b];
-      // T transposed in place (each thread its 4 x 4 block's entries, through registers)
-      float t[4][4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) t[a][b] = sh.Tm[(rb * 4 + a) * CH + cb * 4 + b];
-      __syncthreads();
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) sh.Tm[(cb * 4 + b) * CH + rb * 4 + a] = t[a][b];
+        for (int e = 0; e < 4; ++e) {
+          const int i = rt + g8 + (e >> 1) * 8, jj = nq + 8 * j + 2 * t4 + (e & 1);
+          sh.P[i * LC + jj] = jj <= i ? qk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
+        }
     }
-    __syncthreads();
-    // ---- U = T (beta V) [64 x 64] and W = T (beta e^G K) [64 x 128] (W stored transposed over KT) ----
+    // ---- U = T (beta V) [64 x 64] (kept) and W = T (beta e^G K) [64 x 128] (into W) ----
     float u[4][4];
     zero(u);
-    mm<4, 4, CH, CH, DH>(sh.Tm, sh.V, rb * 4, cb * 4, u);
+    warp_mm<4, CH>(u, rt, nq, [&](int i, int k) { return sh.Tm[i * LC + k]; },
+                   [&](int k, int c) { return sh.V[k * LH + c]; }, lane);
     {
-      float w[4][8];
+      float w[8][4];
       zero(w);
-#pragma unroll 2
-      for (int k = 0; k < CH; ++k) {
-        const float sc = sh.B[k] * expf(sh.G[k]);
-        float a[4], b[8];
-        *reinterpret_cast<float4*>(&a[0]) = *reinterpret_cast<const float4*>(sh.Tm + k * CH + rb * 4);
-        *reinterpret_cast<float4*>(&b[0]) = *reinterpret_cast<const float4*>(sh.K + k * DK + cb * 8);
-        *reinterpret_cast<float4*>(&b[4]) = *reinterpret_cast<const float4*>(sh.K + k * DK + cb * 8 + 4);
+      warp_mm<8, CH>(w, rt, nw, [&](int i, int k) { return sh.Tm[i * LC + k]; },
+                     [&](int k, int c) { return sh.K[k * LK + c] * sh.EB[k]; }, lane);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] *= sc;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[i][j] = fmaf(a[i], b[j], w[i][j]);
+      for (int j = 0; j < 8; ++j) {
+        const int c = nw + 8 * j + 2 * t4;
+        *reinterpret_cast<float2*>(&sh.W[(rt + g8) * LK + c]) = make_float2(w[j][0], w[j][1]);
+        *reinterpret_cast<float2*>(&sh.W[(rt + g8 + 8) * LK + c]) = make_float2(w[j][2], w[j][3]);
       }
-      __syncthreads();  // KT's last readers (the products above) are done
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sh.KT[(cb * 8 + j) * CH + rb * 4 + i] = w[i][j];
     }
-    __syncthreads();
+    __syncthreads();  // W and P are complete; every read of beta V is done
     // ---- V' = U - W S [64 x 64] (into V) ----
     {
       float ws[4][4];
       zero(ws);
-      mm<4, 4, DK, CH, DH>(sh.KT, sh.S, rb * 4, cb * 4, ws);
-      __syncthreads();  // every thread has read beta V
+      warp_mm<4, DK>(ws, rt, nq, [&](int i, int k) { return sh.W[i * LK + k]; },
+                     [&](int k, int c) { return sh.S[k * LH + c]; }, lane);
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        float4 vv;
-        vv.x = u[a][0] - ws[a][0];
-        vv.y = u[a][1] - ws[a][1];
-        vv.z = u[a][2] - ws[a][2];
-        vv.w = u[a][3] - ws[a][3];
-        *reinterpret_cast<float4*>(&sh.V[(rb * 4 + a) * DH + cb * 4]) = vv;
+      for (int j = 0; j < 4; ++j) {
+        const int c = nq + 8 * j + 2 * t4;
+        *reinterpret_cast<float2*>(&sh.V[(rt + g8) * LH + c]) = make_float2(u[j][0] - ws[j][0], u[j][1] - ws[j][1]);
+        *reinterpret_cast<float2*>(&sh.V[(rt + g8 + 8) * LH + c]) =
+            make_float2(u[j][2] - ws[j][2], u[j][3] - ws[j][3]);
       }
     }
     __syncthreads();
@@ -314,19 +307,21 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
       float o[4][4], pv[4][4];
       zero(o);
       zero(pv);
-      mm<4, 4, DK, CH, DH>(sh.QT, sh.S, rb * 4, cb * 4, o);
-      mm<4, 4, CH, CH, DH>(sh.PT, sh.V, rb * 4, cb * 4, pv);
+      warp_mm<4, DK>(o, rt, nq, [&](int i, int k) { return sh.Q[i * LK + k]; },
+                     [&](int k, int c) { return sh.S[k * LH + c]; }, lane);
+      warp_mm<4, CH>(pv, rt, nq, [&](int i, int k) { return sh.P[i * LC + k]; },
+                     [&](int k, int c) { return sh.V[k * LH + c]; }, lane);
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int i = rb * 4 + a;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = rt + g8 + hh * 8;
         if (i < n) {
           const float eg = expf(sh.G[i]);
-          float4 ov;
-          ov.x = fmaf(eg, o[a][0], pv[a][0]);
-          ov.y = fmaf(eg, o[a][1], pv[a][1]);
-          ov.z = fmaf(eg, o[a][2], pv[a][2]);
-          ov.w = fmaf(eg, o[a][3], pv[a][3]);
-          *reinterpret_cast<float4*>(p.o + (base + t0 + i) * DV + half * DH + cb * 4) = ov;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = nq + 8 * j + 2 * t4;
+            *reinterpret_cast<float2*>(p.o + (base + t0 + i) * DV + half * DH + c) =
+                make_float2(fmaf(eg, o[j][2 * hh], pv[j][2 * hh]), fmaf(eg, o[j][2 * hh + 1], pv[j][2 * hh + 1]));
+          }
         }
       }
     }
@@ -335,31 +330,21 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
       const float gl = sh.G[CH - 1];
       float sn[8][4];
       zero(sn);
-#pragma unroll 2
-      for (int k = 0; k < CH; ++k) {
-        const float sc = expf(gl - sh.G[k]);
-        float a[8], b[4];
-        *reinterpret_cast<float4*>(&a[0]) = *reinterpret_cast<const float4*>(sh.K + k * DK + rb * 8);
-        *reinterpret_cast<float4*>(&a[4]) = *reinterpret_cast<const float4*>(sh.K + k * DK + rb * 8 + 4);
-        *reinterpret_cast<float4*>(&b[0]) = *reinterpret_cast<const float4*>(sh.V + k * DH + cb * 4);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] *= sc;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) sn[i][j] = fmaf(a[i], b[j], sn[i][j]);
-      }
+      warp_mm<8, CH>(sn, rs, ns, [&](int kk, int i) { return sh.K[i * LK + kk] * sh.ED[i]; },
+                     [&](int i, int c) { return sh.V[i * LH + c]; }, lane);
       const float egl = expf(gl);
       float old[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) old[i][j] = sh.S[(rb * 8 + i) * DH + cb * 4 + j];
-      __syncthreads();  // every thread has read S (Q S, W S) and its entries of it
+        for (int e = 0; e < 4; ++e)
+          old[j][e] = sh.S[(rs + g8 + (e >> 1) * 8) * LH + ns + 8 * j + 2 * t4 + (e & 1)];
+      __syncthreads();  // every thread has read S (W S, Q S) and its own entries of it
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) sh.S[(rb * 8 + i) * DH + cb * 4 + j] = fmaf(egl, old[i][j], sn[i][j]);
+        for (int e = 0; e < 4; ++e)
+          sh.S[(rs + g8 + (e >> 1) * 8) * LH + ns + 8 * j + 2 * t4 + (e & 1)] = fmaf(egl, old[j][e], sn[j][e]);
     }
     __syncthreads();
   }
@@ -367,7 +352,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
     for (int e = tid * 4; e < DK * DH; e += NT * 4) {
       const int kk = e / DH, c = e % DH;
       *reinterpret_cast<float4*>(p.s_out + ((int64_t)rh * DK + kk) * DV + half * DH + c) =
-          *reinterpret_cast<const float4*>(&sh.S[e]);
+          *reinterpret_cast<const float4*>(&sh.S[kk * LH + c]);
     }
   }
   pdl_launch();

@@ -124,21 +124,22 @@ __global__ void __launch_bounds__(256) rms_quant_kernel(const T* __restrict__ x,
 // ---------------------------------------------------------------------------------------------------------------
 // Gated DeltaNet input: a warp per (row r, token t, key head h); lane l owns channels 4l .. 4l + 3 of a 128-channel
 // head. proj [rows * T, ld] holds, per token, the convolution's input channels [q (Hk * 128) | k (Hk * 128) | v (Hv *
-// 128)] from column 0, then b at column b_off and a at a_off (one per value head). tail [tr, KW - 1, C] (tr = 1: every
-// row continues the same inputs; tr = rows; null: zeros) holds the KW - 1 inputs before token 0, oldest first.
-// Convolution of channel c at token t: acc = x[t - KW + 1] w[c, 0], then acc = RN(acc + RN(x[t - KW + 1 + j] w[c, j]))
-// for j = 1 .. KW - 1 (torch's order in the unfused form: a product, then a sum, each rounded); y = RN16(silu(acc)).
+// 128)] from column 0, then b at column b_off and a at a_off (one per value head). tail [tr, 3, C] (tr = 1: every
+// row continues the same inputs; tr = rows; null: zeros) holds the 3 inputs before token 0, oldest first (4 taps).
+// Convolution of channel c at token t: acc = x[t - 3] w[c, 0], then acc = RN(acc + RN(x[t - 3 + j] w[c, j])) for
+// j = 1 .. 3 (torch's order in the unfused form: a product, then a sum, each rounded); y = RN16(silu(acc)). A lane
+// reads its 4 channels of a tap as one 8-byte load and their 16 weights as two 16-byte loads.
 // ---------------------------------------------------------------------------------------------------------------
 struct PrepParams {
   const void* proj;
   int64_t ld;         // elements between tokens in proj
-  const void* tail;   // [tr, KW - 1, C] or null
+  const void* tail;   // [tr, 3, C] or null
   int tail_rows;      // 1 or rows
-  const void* conv;   // [C, KW] 16-bit
+  const void* conv;   // [C, 4] 16-bit
   const float* A_log; // [Hv]
   const void* dt_bias;// [Hv] 16-bit
   int b_off, a_off;   // columns of b and a in proj
-  int rows, T, Hk, Hv, KW;
+  int rows, T, Hk, Hv;
   float q_scale;      // dk^-1/2
   float* q;           // [rows, Hv, T, 128]
   float* k;
@@ -147,27 +148,44 @@ struct PrepParams {
   float* g;
 };
 
+// 4 consecutive 16-bit values (8 bytes) -> fp32
 template <typename T>
-__device__ __forceinline__ float conv_in(const PrepParams& p, int r, int t, int col) {
-  // the convolution input of channel col at token t of row r (t < 0: the tail's, or zero)
-  if (t >= 0) return to_f<T>(static_cast<const T*>(p.proj)[((int64_t)r * p.T + t) * p.ld + col]);
-  if (!p.tail) return 0.0f;
-  const int C = (p.Hk * 2 + p.Hv) * 128;
-  const int tr = p.tail_rows == 1 ? 0 : r;
-  return to_f<T>(static_cast<const T*>(p.tail)[((int64_t)tr * (p.KW - 1) + (p.KW - 1 + t)) * C + col]);
+__device__ __forceinline__ void ld4(const T* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = to_f<T>(h[i]);
 }
 
+// The convolution (KW = 4 taps) + SiLU of channels col .. col + 3 at one token, from the token's 4 input rows src[j]
+// (null: zeros before the first input): acc = x_0 w_0, then acc = RN(acc + RN(x_j w_j)); y = RN16(silu(acc)).
 template <typename T>
-__device__ __forceinline__ void conv4(const PrepParams& p, int r, int t, int col0, float (&y)[4]) {
-  const T* cw = static_cast<const T*>(p.conv);
+__device__ __forceinline__ void conv4(const T* const (&src)[4], const T* conv, int col, float (&y)[4]) {
+  float w[16];  // channel i, tap j at w[4 i + j]: the 4 channels' weights are 32 contiguous bytes
+  {
+    const uint4 a = *reinterpret_cast<const uint4*>(conv + (int64_t)col * 4);
+    const uint4 b = *reinterpret_cast<const uint4*>(conv + (int64_t)col * 4 + 8);
+    const T* ha = reinterpret_cast<const T*>(&a);
+    const T* hb = reinterpret_cast<const T*>(&b);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int col = col0 + i;
-    float acc = __fmul_rn(conv_in<T>(p, r, t - p.KW + 1, col), to_f<T>(cw[(int64_t)col * p.KW]));
-    for (int j = 1; j < p.KW; ++j)
-      acc = __fadd_rn(acc, __fmul_rn(conv_in<T>(p, r, t - p.KW + 1 + j, col), to_f<T>(cw[(int64_t)col * p.KW + j])));
-    y[i] = round_to<T>(silu_f(acc));
+    for (int i = 0; i < 8; ++i) {
+      w[i] = to_f<T>(ha[i]);
+      w[8 + i] = to_f<T>(hb[i]);
+    }
   }
+  float acc[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (src[j]) ld4(src[j] + col, x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float prod = __fmul_rn(x[i], w[4 * i + j]);
+      acc[i] = j == 0 ? prod : __fadd_rn(acc[i], prod);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) y[i] = round_to<T>(silu_f(acc[i]));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -186,10 +204,23 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
     const int h = (int)(item % p.Hk);
     const int t = (int)((item / p.Hk) % p.T);
     const int r = (int)(item / ((int64_t)p.Hk * p.T));
+    const int C = (p.Hk * 2 + p.Hv) * 128;
+    const T* proj = static_cast<const T*>(p.proj);
+    const T* tail = static_cast<const T*>(p.tail);
+    const T* conv = static_cast<const T*>(p.conv);
+    const T* src[4];  // the convolution's inputs at tokens t - 3 .. t (the tail's before token 0, or zeros)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int tt = t - 3 + j;
+      if (tt >= 0)
+        src[j] = proj + ((int64_t)r * p.T + tt) * p.ld;
+      else
+        src[j] = tail ? tail + ((int64_t)(p.tail_rows == 1 ? 0 : r) * 3 + 3 + tt) * C : nullptr;
+    }
     const int c0 = lane * 4;
     float qv[4], kv[4];
-    conv4<T>(p, r, t, h * 128 + c0, qv);
-    conv4<T>(p, r, t, p.Hk * 128 + h * 128 + c0, kv);
+    conv4<T>(src, conv, h * 128 + c0, qv);
+    conv4<T>(src, conv, p.Hk * 128 + h * 128 + c0, kv);
     float sq = 0.0f, sk = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -214,10 +245,10 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
       *reinterpret_cast<float4*>(p.q + o) = qo;
       *reinterpret_cast<float4*>(p.k + o) = ko;
       float vv[4];
-      conv4<T>(p, r, t, 2 * p.Hk * 128 + vh * 128 + c0, vv);
+      conv4<T>(src, conv, 2 * p.Hk * 128 + vh * 128 + c0, vv);
       *reinterpret_cast<float4*>(p.v + o) = make_float4(vv[0], vv[1], vv[2], vv[3]);
       if (lane == 0) {
-        const T* pr = static_cast<const T*>(p.proj) + ((int64_t)r * p.T + t) * p.ld;
+        const T* pr = src[3];
         const float bb = to_f<T>(pr[p.b_off + vh]);
         const float aa = to_f<T>(pr[p.a_off + vh]);
         const int64_t bo = ((int64_t)r * p.Hv + vh) * p.T + t;

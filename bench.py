@@ -385,6 +385,11 @@ CASES = {
     "nvfp4_gemm": ("nvfp4", 65536, 5120, 2048),
     "nvfp4_act_quant": ("nvfp4", 8192, 0, 6144),
     "readout": ("readout", 256, 255, 2048),  # C4's readout: R prompts, k option ids (N), D features (K)
+    # the C5 hybrid's steps at one micro-batch of 32 requests x 256 tokens (M = 8192 rows): (kind, rows, T, D)
+    "rms_quant": ("c5", 32, 256, 2560),
+    "gdn_prep": ("c5", 32, 256, 2560),
+    "gdn_chunk": ("c5", 32, 256, 2560),
+    "gdn_gate": ("c5", 32, 256, 2560),
 }
 
 
@@ -395,6 +400,9 @@ def run_case(name):
     fmt, M, N, K = CASES[name]
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
+    if fmt == "c5":
+        run_c5_case(b2, name, M, N, K, dev, g)
+        return
     x = torch.randn(M, K, device=dev, generator=g).bfloat16()
     if fmt == "readout":
         head = torch.nn.Linear(K, 151936, bias=False, device=dev, dtype=torch.bfloat16)
@@ -428,6 +436,43 @@ def run_case(name):
                 mod.gemm(qa, sa, q, s, torch.bfloat16)
     torch.cuda.synchronize()
     print(json.dumps({"case": name, "M": M, "N": N, "K": K, "faults": b2._lib.device_faults(0)}))
+
+
+def run_c5_case(b2, name, rows, T, D, dev, g):
+    """One C5 step on its own (C5's sizes: 16 key / 32 value heads of 128, convolution 4) over rows x T tokens: 2
+    untimed launches, then 3 of the kernel under study; inputs drawn as the model makes them."""
+    import torch
+    from basal_b200 import hybrid
+    cfg = hybrid.C5
+    M = rows * T
+    if name == "rms_quant":
+        x = torch.randn(M, D, device=dev, generator=g).bfloat16()
+        w = (torch.randn(D, device=dev, generator=g) * 0.02).bfloat16()
+        for _ in range(5):
+            b2.ops.rms_norm_fp8_quant(x, w, cfg.eps)
+    else:
+        ld = sum(cfg.in_sizes)
+        proj = torch.randn(M, ld, device=dev, generator=g).bfloat16()
+        conv = (torch.rand(cfg.conv_dim, cfg.conv, device=dev, generator=g) - 0.5).bfloat16()
+        A_log = torch.log(1 + 15 * torch.rand(cfg.lin_v_heads, device=dev, generator=g))
+        dt_bias = torch.ones(cfg.lin_v_heads, device=dev).bfloat16()
+        tail = torch.randn(1, cfg.conv - 1, cfg.conv_dim, device=dev, generator=g).bfloat16()
+        b_off = cfg.conv_dim + cfg.value_dim
+        args = (proj, tail, conv, A_log, dt_bias, rows, T, cfg.lin_k_heads, cfg.lin_v_heads, b_off,
+                b_off + cfg.lin_v_heads)
+        q, k, v, beta, gg = b2.ops.gdn_prep(*args)
+        s0 = torch.randn(1, cfg.lin_v_heads, 128, 128, device=dev, generator=g) * 0.05
+        o, _ = b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0)
+        for _ in range(5):
+            if name == "gdn_prep":
+                b2.ops.gdn_prep(*args)
+            elif name == "gdn_chunk":
+                b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0)
+            else:
+                b2.ops.gdn_gate_fp8_quant(o, proj, cfg.conv_dim, torch.ones(128, device=dev).bfloat16(), cfg.eps,
+                                          rows, T)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "rows": rows, "T": T, "D": D, "faults": b2._lib.device_faults(0)}))
 
 
 def unsplit_gemm(b2, fmt, qa, sa, q, s):
