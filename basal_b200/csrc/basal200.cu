@@ -22,7 +22,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int checked = 0;  // 1: sm_100, -1: another architecture
   int sms = 0;
-  uint64_t smem_set = 0;  // kernels whose dynamic shared memory limit was raised on this device
+  uint64_t smem_set[2] = {0, 0};  // kernels whose dynamic shared memory limit was raised on this device
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -42,19 +42,21 @@ int current_device(int* dev) {
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
 enum SmemSlot {
   kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50,
-  kSlotRes = 58, kSlotGdn = 62
+  kSlotRes = 58, kSlotGdn = 62, kSlotLogitsTc = 64
 };
 // kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7,
-// kSlotRes .. + 3, kSlotGdn (bits of a 64-bit mask)
+// kSlotRes .. + 3, kSlotGdn, kSlotLogitsTc .. + 11 (bits of a 128-bit mask)
+
+bool smem_is_set(int dev, int slot) { return (g_dev[dev].smem_set[slot >> 6] >> (slot & 63)) & 1; }
 
 // Raises the dynamic shared-memory limit of `kernel` once per device (bit `slot` of the device's mask).
 template <typename K>
 int set_smem(int dev, int slot, K kernel, size_t bytes) {
   DeviceInfo& d = g_dev[dev];
-  if (d.smem_set & (1ull << slot)) return BASAL200_OK;
+  if (smem_is_set(dev, slot)) return BASAL200_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
     return BASAL200_ERR_LAUNCH;
-  d.smem_set |= 1ull << slot;
+  d.smem_set[slot >> 6] |= 1ull << (slot & 63);
   return BASAL200_OK;
 }
 
@@ -292,7 +294,7 @@ int block_gemm_launch(int dev, const CUtensorMap& ta, const CUtensorMap& tb, con
                        : ACT == blockgemm::kActNone
                              ? kSlotBlock + (INT8 ? 3 : 0) + OUT
                              : kSlotGlu + (INT8 ? 4 : 0) + (OUT == BASAL200_F16 ? 2 : 0) + ACT - 1;
-  if (!(g_dev[dev].smem_set & (1ull << slot))) {
+  if (!smem_is_set(dev, slot)) {
     const int rc = check_launch_regs(kern, (int)blockgemm::LAUNCH_REGS);
     if (rc) return rc;
   }
@@ -614,9 +616,47 @@ constexpr int type_index() {
   return std::is_same<T, float>::value ? 0 : (std::is_same<T, __nv_bfloat16>::value ? 1 : 2);
 }
 
+// The tensor-core kernel: a cluster of 8 CTAs (one per feature slice) on each tile of 128 prompts x BN codes.
+template <typename T, typename TB, int BN>
+int logits_tc_launch(int dev, const T* h, int64_t R, int64_t D, int64_t ldh, const T* head, int64_t V, int64_t ldw,
+                     const int64_t* ids, int64_t U, const TB* bias, float softcap, float* z, cudaStream_t st) {
+  auto kern = readout::code_logits_tc_kernel<T, TB, BN>;
+  constexpr size_t smem = readout::tc_smem_bytes<BN>();
+  const int slot = kSlotLogitsTc + (std::is_same<T, __half>::value ? 6 : 0) + type_index<TB>() * 2 + (BN == 32);
+  int rc = set_smem(dev, slot, kern, smem);
+  if (rc) return rc;
+  const int64_t gx = (R + readout::TM - 1) / readout::TM, gy = (U + BN - 1) / BN;
+  if (gx > INT32_MAX || gy > 65535) return BASAL200_ERR_LIMIT;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = readout::TSPLIT;
+  cfg.gridDim = dim3((unsigned)gx, (unsigned)gy, readout::TSPLIT);
+  cfg.blockDim = readout::TTHREADS;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, kern, h, R, D, ldh, head, V, ldw, ids, U, bias, softcap, z) != cudaSuccess)
+    return launched();
+  return launched();
+}
+
 template <typename TH, typename TW, typename TB>
 int logits_launch(int dev, const TH* h, int64_t R, int64_t D, int64_t ldh, const TW* head, int64_t V, int64_t ldw,
                   const int64_t* ids, int64_t U, const TB* bias, float softcap, float* z, cudaStream_t st) {
+  if constexpr (std::is_same<TH, TW>::value && sizeof(TH) == 2) {
+    // one 16-bit type, 16-byte aligned rows, D % 8 == 0: the tensor cores, whatever R and U (so a logit's bits never
+    // depend on them)
+    if (D % 8 == 0 && aligned16(h) && aligned16(head) && ldh % 8 == 0 && ldw % 8 == 0) {
+      if (U <= 16) return logits_tc_launch<TH, TB, 16>(dev, h, R, D, ldh, head, V, ldw, ids, U, bias, softcap, z, st);
+      return logits_tc_launch<TH, TB, 32>(dev, h, R, D, ldh, head, V, ldw, ids, U, bias, softcap, z, st);
+    }
+  }
   if constexpr (sizeof(TH) == 2 && sizeof(TW) == 2) {
     // many codes, whole 256-feature chunks, 16-byte aligned rows: the staged kernel (the same bits)
     if (U > 8 && D % readout::CHUNK == 0 && aligned16(h) && aligned16(head) && (ldh * 2) % 16 == 0 &&

@@ -274,7 +274,7 @@ class HybridClassifier:
     @torch.no_grad()
     def decide(self, ids, st, readout, rows, idx, pad):
         """Option probabilities [B, k] of the rows' last tokens: the readout of readout.rows(...) = rows, idx, pad."""
-        return readout.probs_of(readout.logits(self.suffix_hidden(ids, st), rows), idx, pad)
+        return readout.device_probs(self.suffix_hidden(ids, st), rows, idx, pad)
 
     def linears(self):
         """Every FP8-block linear of the model, with its name."""

@@ -9,7 +9,8 @@ whatever prompts are read with it (probs and probs_each agree exactly).
                                    any, is read by id from the head inside the kernel as well
   logits(h, rows) -> fp32 [n, k]   basal::code_logits, soft cap applied once
   probs_of(z, idx, pad)            basal::code_probs: gather, -inf padding, softmax
-  probs(h, lids), probs_each(h, lids)   one copy to the host
+  device_probs(h, rows, idx, pad)  probs_of(logits(h, rows), idx, pad): the device part of probs
+  probs(h, lids), probs_each(h, lids)   device_probs, then one copy to the host
 """
 import torch
 
@@ -76,9 +77,13 @@ class CodeReadout:
         """Code logits [n, k] -> each prompt's probabilities over its codes [n, K] (padding 0), as a tensor."""
         return ops.code_probs(z, idx, pad)
 
+    def device_probs(self, h, rows, idx, pad):
+        """probs_of(logits(h, rows), idx, pad): the probabilities [n, K] as a device tensor."""
+        return self.probs_of(self.logits(h, rows), idx, pad)
+
     def probs(self, h, lids):
         rows, idx, pad = self.rows(lids)
-        p = self.probs_of(self.logits(h, rows), idx, pad).tolist()  # one device sync
+        p = self.device_probs(h, rows, idx, pad).tolist()  # one device sync
         return [row[: len(ids)] for row, ids in zip(p, lids)]
 
     def probs_each(self, h, lids):

@@ -411,7 +411,7 @@ def run_case(name):
         ro = b2.readout.CodeReadout(head)
         rows, idx, pad = ro.rows([torch.randperm(151936, device=dev, generator=g)[:N].tolist()] * M)
         for _ in range(5):
-            ro.probs_of(ro.logits(x, rows), idx, pad)
+            ro.device_probs(x, rows, idx, pad)
     elif N == 0 and fmt == "nvfp4":
         inv_g = torch.tensor([0.5], device=dev)
         for _ in range(5):
@@ -539,7 +539,8 @@ def run_sweep(fmts):
         fmts = [f for f in fmts if f != "res"]
     if "readout" in fmts:
         # C4's readout: h [256, 2048] bf16 ~ N(0, 1) at the answer positions, a 151,936-row bf16 head ~ N(0, 0.02),
-        # one code set of k ids shared by all rows; the device part (code_logits + code_probs) per call
+        # one code set of k ids shared by all rows; the device part of CodeReadout.probs per call (basal::code_logits +
+        # basal::code_probs)
         R, D, V = 256, 2048, 151936
         head = torch.nn.Linear(D, V, bias=False, device=dev, dtype=torch.bfloat16)
         with torch.no_grad():
@@ -550,7 +551,7 @@ def run_sweep(fmts):
             for k in (2, 8, 64, 255):
                 ids = torch.randperm(V, device=dev, generator=gen)[:k].tolist()
                 rows, idx, pad = ro.rows([ids] * R)
-                t = (graph_us(lambda: (flush.sum(), ro.probs_of(ro.logits(h, rows), idx, pad))) - base)
+                t = graph_us(lambda: (flush.sum(), ro.device_probs(h, rows, idx, pad))) - base
                 byts = 2 * R * D + 2 * k * D + 4 * R * k * 2 + 8 * k
                 print(json.dumps({"sweep": "C4 readout", "R": R, "D": D, "k": k, "softcap": softcap,
                                   "us": round(t, 2), "gbs": round(byts / t / 1e3, 1),

@@ -266,9 +266,12 @@ int basal200_code_logits(const void* h, int h_dtype, int64_t R, int64_t D, int64
                          int bias_dtype, float softcap, float* z, void* stream);
 
 /* p [R, Kmax] fp32 = softmax over j of z[r, idx[r, j]] with -inf where pad[r, j] != 0 (the padding gets 0).
- * Replaces CodeReadout.probs_of (basal/readout.py:76-79). Kmax <= 1024. */
+ * Replaces CodeReadout.probs_of (basal/readout.py:76-79). Kmax <= 1024. The kernel may start while the library
+ * kernel ahead of it in the stream (code_logits) runs, and reads idx and pad before it waits for that kernel: they
+ * must not be outputs of the library kernel directly ahead (z may be). */
 int basal200_code_probs(const float* z, int64_t R, int64_t U, const int64_t* idx, const uint8_t* pad, int64_t Kmax,
                         float* p, void* stream);
+
 
 /* ---- Diagnostics ---- */
 

@@ -103,3 +103,89 @@ def test_code_tile_widths_agree_bit_for_bit(b2, D, hdt):
     got = b2.ops.code_logits(h.cuda(), head.weight, torch.tensor(pool).cuda(), head.bias, 30.0).cpu().numpy()
     assert np.abs(got - ref).max() <= 1e-5
     assert b2._lib.device_faults(0) == 0
+
+
+# ---- the tensor-core path: h and head of one 16-bit type, 16-byte aligned rows, D % 8 == 0 ----
+
+def _head(D, V, seed, dt=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn(V, D, generator=g) / D ** 0.5).to(dt)
+    bias = (torch.randn(V, generator=g) * 0.1).to(dt)
+    return g, w, bias
+
+
+@pytest.mark.parametrize("D", [8, 24, 200, 2048, 8192])
+@pytest.mark.parametrize("R, U", [(1, 1), (130, 17), (300, 40)])
+def test_tensor_core_shapes(b2, D, R, U):
+    """Slices shorter than a swizzle row or empty (D = 8, 24, 200), one round (2048), four rounds a slice (8192);
+    ragged prompt tiles (R = 130, 300) and code tiles (U = 17, 40): within 1e-5 of the oracle's fp32 logits."""
+    g, w, bias = _head(D, 3000, D * 7 + R + U)
+    h = torch.randn(R, D, generator=g).bfloat16()
+    ids = torch.randperm(3000, generator=g)[:U]
+    z = b2.ops.code_logits(h.cuda(), w.cuda(), ids.cuda(), bias.cuda(), 0.0).cpu().numpy()
+    ref = oro.logits(h.float().numpy(), (w[ids].float().numpy(), bias[ids].float().numpy()), None)
+    assert np.abs(z - ref).max() <= 1e-5
+    assert b2._lib.device_faults(0) == 0
+
+
+@pytest.mark.parametrize("cap", [None, 30.0])
+def test_tensor_core_fp16(b2, cap):
+    """fp16 h and head (the MMA's f16 operands): the C4 readout shape, within 1e-5 of the oracle."""
+    g, w, bias = _head(2048, 20000, 11, torch.float16)
+    h = torch.randn(256, 2048, generator=g).half()
+    ids = torch.randperm(20000, generator=g)[:64]
+    z = b2.ops.code_logits(h.cuda(), w.cuda(), ids.cuda(), None, cap or 0.0).cpu().numpy()
+    ref = oro.logits(h.float().numpy(), (w[ids].float().numpy(), None), cap)
+    assert np.abs(z - ref).max() <= 1e-5
+
+
+def test_tensor_core_positions_bit_for_bit(b2):
+    """A prompt's logit for a code is the same bits at any row of any prompt tile (rows 0, 127, 128, 299 of 300) and
+    at any column of a 16- or 32-code tile (among 5 codes or 40), with a bf16 bias and the soft cap."""
+    D, V = 2560, 4000
+    g, w, bias = _head(D, V, 5)
+    h = torch.randn(300, D, generator=g).bfloat16()
+    pool = torch.randperm(V, generator=g)[:40]
+    wc, bc = w.cuda(), bias.cuda()
+    target_row, target_code = 7, int(pool[3])
+    seen = []
+    for pos in (0, 127, 128, 299):
+        perm = list(range(300))
+        perm[pos], perm[target_row] = perm[target_row], perm[pos]
+        hp = h[perm].cuda()
+        for ids in (pool[:5].tolist(), pool.tolist(), [int(pool[9]), target_code] + pool[20:23].tolist()):
+            z = b2.ops.code_logits(hp, wc, torch.tensor(ids).cuda(), bc, 30.0)
+            seen.append(z[pos, ids.index(target_code)].item())
+    assert len(set(seen)) == 1, seen
+    ref = oro.logits(h[target_row:target_row + 1].float().numpy(),
+                     (w[[target_code]].float().numpy(), bias[[target_code]].float().numpy()), 30.0)
+    assert abs(seen[0] - float(ref[0, 0])) <= 1e-5
+
+
+def test_tensor_core_bad_id(b2):
+    """An id outside [0, V) gives NaN logits in its column and the BAD_ID fault bit; the other columns are the bits
+    they have without it."""
+    D, V = 512, 1000
+    g, w, bias = _head(D, V, 3)
+    h = torch.randn(40, D, generator=g).bfloat16().cuda()
+    wc = w.cuda()
+    b2._lib.device_faults(0)
+    good = b2.ops.code_logits(h, wc, torch.tensor([5, 17]).cuda(), None, 0.0)
+    z = b2.ops.code_logits(h, wc, torch.tensor([5, -1, V + 3, 17]).cuda(), None, 0.0)
+    assert b2._lib.device_faults(0) == 16  # BASAL200_FAULT_BAD_ID
+    assert torch.isnan(z[:, 1]).all() and torch.isnan(z[:, 2]).all()
+    assert torch.equal(z[:, 0], good[:, 0]) and torch.equal(z[:, 3], good[:, 1])
+
+
+def test_tensor_core_c5_readout(b2):
+    """C5's readout shape: 4096 prompts, 8 options, D = 2560 (32 prompt tiles x 1 code tile x 8 slices)."""
+    D, V = 2560, 151936
+    g = torch.Generator().manual_seed(21)
+    w = (torch.randn(V, D, generator=g) * 0.02).bfloat16()
+    h = torch.randn(4096, D, generator=g).bfloat16()
+    ids = torch.randperm(V, generator=g)[:8]
+    z = b2.ops.code_logits(h.cuda(), w.cuda(), ids.cuda(), None, 0.0).cpu().numpy()
+    ref = oro.logits(h.float().numpy(), (w[ids].float().numpy(), None), None)
+    assert np.abs(z - ref).max() <= 1e-5
+    assert b2._lib.device_faults(0) == 0
+
