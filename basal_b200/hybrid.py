@@ -93,11 +93,18 @@ def rms(x, w, eps):
     return (h * (1.0 + w.float())).to(x.dtype)
 
 
-def rope(x, cos, sin, r):
-    """The first r dims of each head [b, heads, T, d] rotated by the half-split rule (basal/gdn_graph.py:446-451)."""
-    xr = x[..., :r]
-    rot = torch.cat([-xr[..., r // 2:], xr[..., : r // 2]], -1)
-    return torch.cat([xr * cos[:, None] + rot * sin[:, None], x[..., r:]], -1)
+def rope(x, cos, sin, r, out=None):
+    """The first r dims of each head [b, heads, T, d] rotated by the half-split rule (basal/gdn_graph.py:446-451):
+    x1 cos - x2 sin, x2 cos + x1 sin for the halves x1, x2 of those dims, each product and sum rounded to x's dtype as
+    the reference's (x cos + rotate_half(x) sin) rounds them. Written into out (a new tensor when None)."""
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device) if out is None else out
+    h = r // 2
+    c, s = cos[:, None], sin[:, None]
+    x1, x2 = x[..., :h], x[..., h:r]
+    out[..., :h] = x1 * c[..., :h] - x2 * s[..., :h]
+    out[..., h:r] = x2 * c[..., h:] + x1 * s[..., h:]
+    out[..., r:] = x[..., r:]
+    return out
 
 
 def rope_tables(cfg, pos, dtype):
@@ -116,6 +123,21 @@ class PrefixState:
     length: int
     kv: list
     states: list
+    buffers: dict = dataclasses.field(default_factory=dict)
+
+    def kv_buffers(self, i, b, T):
+        """Key and value buffers [b, kv heads, P + T, d] of attention layer i whose first P positions hold the prefix's
+        keys and values (copied once, kept for later rows): the rows' own T positions are written into them."""
+        kb, vb = self.buffers.get((i, T), (None, None))
+        if kb is None or kb.shape[0] < b:
+            pk, pv = self.kv[i]
+            P = self.length
+            kb = pk.new_empty(b, pk.shape[1], P + T, pk.shape[3])
+            vb = pv.new_empty(b, pv.shape[1], P + T, pv.shape[3])
+            kb[:, :, :P].copy_(pk.expand(b, -1, -1, -1))
+            vb[:, :, :P].copy_(pv.expand(b, -1, -1, -1))
+            self.buffers[(i, T)] = kb, vb
+        return kb[:b], vb[:b]
 
 
 class HybridClassifier:
@@ -200,9 +222,11 @@ class HybridClassifier:
         tail = qkv[:, T - n:] if T >= n else torch.cat([tail0.expand(b, -1, -1), qkv], 1)[:, -n:]
         return h, s, tail.contiguous()
 
-    def _attention(self, L, h, cos, sin, pk, pv):
+    def _attention(self, L, h, cos, sin, pk, pv, bufs=None):
         """h + attention(rms(h)) over the prefix keys / values pk, pv [1, kv heads, P, d] (or none) and the rows'
-        own tokens, causally (basal/gdn_graph.py:452-466, :578-604) -> (h, the rows' keys, values)."""
+        own tokens, causally (basal/gdn_graph.py:452-466, :578-604) -> (h, the rows' keys, values). bufs: key and
+        value buffers [b, kv heads, P + T, d] that hold the prefix's (PrefixState.kv_buffers); the rows' keys and
+        values are written after it instead of concatenated."""
         cfg = self.cfg
         b, T, _ = h.shape
         H, Hk, d = cfg.heads, cfg.kv_heads, cfg.head_dim
@@ -211,15 +235,22 @@ class HybridClassifier:
         qg, k, v = ops.fp8_block_gemm(q8, s8, w.weight, w.weight_scale, h.dtype).view(b, T, -1).split(cfg.qkv_sizes,
                                                                                                         -1)
         q, gate = torch.chunk(qg.view(b, T, H, 2 * d), 2, dim=-1)
+        P = 0 if pk is None else pk.shape[2]
         q = rope(rms(q, L["q_norm"], cfg.eps).transpose(1, 2), cos, sin, cfg.rotary_dims)
-        k = rope(rms(k.view(b, T, Hk, d), L["k_norm"], cfg.eps).transpose(1, 2), cos, sin, cfg.rotary_dims)
+        kn = rms(k.view(b, T, Hk, d), L["k_norm"], cfg.eps).transpose(1, 2)
         v = v.view(b, T, Hk, d).transpose(1, 2)
         G = H // Hk
-        P = 0 if pk is None else pk.shape[2]
-        if P:
+        if P and bufs is not None:
+            kk, vv = bufs
+            k = rope(kn, cos, sin, cfg.rotary_dims, out=kk[:, :, P:])
+            vv[:, :, P:].copy_(v)
+            v = vv[:, :, P:]
+        elif P:
+            k = rope(kn, cos, sin, cfg.rotary_dims)
             kk = torch.cat([pk.expand(b, -1, -1, -1), k], 2)
             vv = torch.cat([pv.expand(b, -1, -1, -1), v], 2)
         else:
+            k = rope(kn, cos, sin, cfg.rotary_dims)
             kk, vv = k, v
         own = torch.ones(T, T, dtype=torch.bool, device=h.device).tril()
         allow = torch.cat([torch.ones(T, P, dtype=torch.bool, device=h.device), own], 1)
@@ -247,7 +278,8 @@ class HybridClassifier:
                 ig += 1
             else:
                 pk, pv = (None, None) if st is None else st.kv[ia]
-                h, k, v = self._attention(L, h, cos, sin, pk, pv)
+                bufs = None if st is None else st.kv_buffers(ia, h.shape[0], h.shape[1])
+                h, k, v = self._attention(L, h, cos, sin, pk, pv, bufs)
                 kv.append((k, v))
                 ia += 1
             h = self._mlp(L, h)

@@ -339,3 +339,22 @@ def test_gdn_chunk_rule_repeated_keys(hy):
     s0 = torch.randn(1, H, 128, 128, device="cuda")
     o0, S0 = ops.gdn_chunk_rule(q[:, :, :0], k[:, :, :0], v[:, :, :0], gl[:, :, :0], beta[:, :, :0], s0)
     assert o0.shape == (1, H, 0, 128) and torch.equal(S0, s0)
+
+
+def test_attention_into_prefix_buffers_equals_concatenation(hy):
+    """The rows' keys and values written after the prefix's in cached buffers (PrefixState.kv_buffers, reused by a
+    second call with fewer rows) give the attention layer's output bit for bit as concatenating them per call."""
+    cfg = hy.HybridConfig(layers=4)
+    model = hy.HybridClassifier(cfg, seed=4)
+    g = torch.Generator().manual_seed(6)
+    P, T = 70, 37
+    st = model.prefix(torch.randint(0, cfg.vocab, (P,), generator=g))
+    L = next(L for L in model.layers if L["kind"] != hy.LINEAR)
+    for b in (5, 3):
+        h = torch.randn(b, T, cfg.hidden, generator=g).bfloat16().cuda()
+        pos = torch.arange(P, P + T, device="cuda")[None].expand(b, T)
+        cos, sin = hy.rope_tables(cfg, pos, torch.bfloat16)
+        pk, pv = st.kv[0]
+        want, wk, wv = model._attention(L, h, cos, sin, pk, pv)
+        got, gk, gv = model._attention(L, h, cos, sin, pk, pv, st.kv_buffers(0, b, T))
+        assert torch.equal(got, want) and torch.equal(gk, wk) and torch.equal(gv, wv)
