@@ -1009,7 +1009,7 @@ int gdn_chunk(const float* q, const float* k, const float* v, const float* g, co
   p.rows = rows;
   p.H = H;
   p.T = T;
-  return launch_pdl(gdnchunk::gdn_chunk_kernel, (unsigned)(rows * H * 2), gdnchunk::NT, smem, st, p);
+  return launch_pdl(gdnchunk::gdn_chunk_kernel, (unsigned)(rows * H), gdnchunk::NT, smem, st, p);
 }
 
 // ------------------------------------------------------------------------------------------------------------

@@ -9,28 +9,30 @@
 //   U = T (beta V),  W = T (beta e^G K),  V' = U - W S,
 //   O = e^G (Q S) + (Q K^T (.) e^{G_i - G_j}, j <= i) V',  S <- e^{G_last} S + (e^{G_last - G} K)^T V'.
 //
-// A CTA owns one (row, value head) and one half of the value dimension (64 of S's 128 columns); the products that do
-// not involve V (A, T, W, Q K^T) are computed by both halves. 256 threads = 8 warps. Every product runs on the tensor
-// cores as mma.sync m16n8k8 with TF32 operands split in two (x = hi + lo, both TF32; each product is hi*hi + hi*lo +
-// lo*hi with an fp32 accumulator, which keeps fp32 accuracy). Operands sit in shared memory in their natural
-// row-major layouts, each row padded so that the fragment loads of a warp hit 32 different banks (leading dimensions
-// of 4 mod 32 words for matrices read along rows, 8 mod 32 for matrices read down columns). T is found by 16 x 16
-// blocks: the diagonal blocks by forward substitution (a warp each), the off-diagonal ones by
-// T_IJ = -T_II sum_{M = J .. I - 1} A_IM T_MJ, one block distance at a time.
+// A CTA of 512 threads (16 warps) owns one (row, value head): its state S [128 x 128] never leaves shared memory, and
+// every product of a chunk is spread over the 16 warps (16 x 16, 16 x 32 or 16 x 64 output tiles a warp). Every
+// product runs on the tensor cores as mma.sync m16n8k8 with TF32 operands split in two (x = hi + lo, both TF32; each
+// product is hi*hi + hi*lo + lo*hi with an fp32 accumulator, which keeps fp32 accuracy). Operands sit in shared
+// memory in their natural row-major layouts, each row padded so that the fragment loads of a warp hit 32 different
+// banks (leading dimensions of 4 mod 32 words for matrices read along rows, 8 mod 32 for matrices read down columns).
+// Buffers are reused within a chunk: P = Q K^T takes A's place once T is found, W takes Q's once Q S and P are done
+// (Q S and U stay in registers until they are used). T is found by 16 x 16 blocks: the diagonal blocks by forward
+// substitution (a warp each), the off-diagonal ones by T_IJ = -T_II sum_{M = J .. I - 1} A_IM T_MJ, one block
+// distance at a time.
 #pragma once
 #include "common.cuh"
 
 namespace b200 {
 namespace gdnchunk {
 
-constexpr int CH = 64;    // tokens a chunk
-constexpr int DK = 128;   // key dim
-constexpr int DV = 128;   // value dim
-constexpr int DH = 64;    // value columns a CTA owns
-constexpr int NT = 256;   // threads (8 warps)
-constexpr int LK = DK + 4;   // row stride of Q, K, W (read along rows and, for K, down columns)
-constexpr int LH = DH + 8;   // row stride of S and V (read down columns)
-constexpr int LC = CH + 4;   // row stride of A, T, P (read along rows)
+constexpr int CH = 64;     // tokens a chunk
+constexpr int DK = 128;    // key dim
+constexpr int DV = 128;    // value dim
+constexpr int NT = 512;    // threads (16 warps)
+constexpr int LK = DK + 4;  // row stride of Q, K, W (read along rows and, for K, down columns)
+constexpr int LV = DV + 8;  // row stride of S and V (read down columns)
+constexpr int LC = CH + 4;  // row stride of A, T, P (read along rows)
+constexpr int LX = 17;      // row stride of the inverse's 16 x 16 scratch blocks
 
 struct Params {
   const float* q;      // [rows, H, T, 128] (l2-normed, scaled)
@@ -46,18 +48,17 @@ struct Params {
 };
 
 struct Smem {
-  float S[DK * LH];    // the state's columns of this CTA, [kk][c]
-  float K[CH * LK];    // keys [i][kk]
-  float Q[CH * LK];    // queries [i][kk]
-  float W[CH * LK];    // T (beta e^G K) [i][kk]
-  float V[CH * LH];    // beta V, then V' = U - W S [i][c]
-  float A[CH * LC];    // A [i][j]
-  float Tm[CH * LC];   // T [i][j]
-  float P[CH * LC];    // (Q K^T (.) decay, causal) [i][j]; scratch of the inverse before
-  float G[CH];         // cumulative gates
-  float B[CH];         // beta
-  float EB[CH];        // beta_i e^{G_i}
-  float ED[CH];        // e^{G_last - G_i}
+  float S[DK * LV];      // the state [kk][c]
+  float K[CH * LK];      // keys [i][kk]
+  float QW[CH * LK];     // queries [i][kk]; then W = T (beta e^G K) [i][kk]
+  float V[CH * LV];      // beta V, then V' = U - W S [i][c]
+  float AP[CH * LC];     // A [i][j]; then P = (Q K^T (.) decay, causal) [i][j]
+  float Tm[CH * LC];     // T [i][j]
+  float X[4][16 * LX];   // the inverse's off-diagonal blocks X = sum A_IM T_MJ, one a warp
+  float G[CH];           // cumulative gates
+  float B[CH];           // beta
+  float EB[CH];          // beta_i e^{G_i}
+  float ED[CH];          // e^{G_last - G_i}
 };
 
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
@@ -82,7 +83,7 @@ __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], 
 template <int NJ, int KN, typename FA, typename FB>
 __device__ __forceinline__ void warp_mm(float (&acc)[NJ][4], int r0, int n0, FA fa, FB fb, int lane) {
   const int g = lane >> 2, t = lane & 3;
-#pragma unroll 2
+#pragma unroll 4  // 8.51 -> 8.27 ms at C5's micro-batch; a full unroll: 12.1 ms
   for (int k0 = 0; k0 < KN; k0 += 8) {
     uint32_t ah[4], al[4];
     split_tf32(fa(r0 + g, k0 + t), ah[0], al[0]);
@@ -112,11 +113,11 @@ __device__ __forceinline__ void zero(float (&acc)[NJ][4]) {
   for (int j = 0; j < NJ; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 }
 
-// T = (I + A)^-1 for the strictly lower A [64][64] (sh.A) -> sh.Tm; sh.P is scratch.
+// T = (I + A)^-1 for the strictly lower A [64][64] (sh.AP) -> sh.Tm; sh.X is scratch.
 __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   float* T = sh.Tm;
-  const float* A = sh.A;
+  const float* A = sh.AP;
   // diagonal 16 x 16 blocks: warp b, lane j < 16 owns column j of block b; rows in order
   if (warp < 4) {
     const int b0 = warp * 16;
@@ -138,14 +139,14 @@ __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
     if ((j >> 4) > (i >> 4)) T[i * LC + j] = 0.0f;
   }
   __syncthreads();
-  // off-diagonal blocks, distance d = I - J: a warp per block, lane owns row lane / 2, columns (lane % 2) * 8 ..
+  // off-diagonal blocks, distance d = I - J: warp J a block, lane owns row lane / 2, columns (lane % 2) * 8 ..
   for (int d = 1; d < 4; ++d) {
-    float x[8];
     const int blk = warp;
     const bool on = blk + d < 4;
     const int I0 = (blk + d) * 16, J0 = blk * 16;
     const int r = lane >> 1, cb = (lane & 1) * 8;
     if (on) {
+      float x[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) x[c] = 0.0f;
       for (int m = J0; m < I0; ++m) {  // X = sum_{M = J .. I - 1} A_IM T_MJ
@@ -154,7 +155,7 @@ __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
         for (int c = 0; c < 8; ++c) x[c] = fmaf(a, T[m * LC + J0 + cb + c], x[c]);
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) sh.P[(I0 + r) * LC + J0 + cb + c] = x[c];
+      for (int c = 0; c < 8; ++c) sh.X[blk][r * LX + cb + c] = x[c];
     }
     __syncthreads();
     if (on) {  // T_IJ = -T_II X
@@ -164,7 +165,7 @@ __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
       for (int m = 0; m < 16; ++m) {
         const float tt = T[(I0 + r) * LC + I0 + m];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) y[c] = fmaf(tt, sh.P[(I0 + m) * LC + J0 + cb + c], y[c]);
+        for (int c = 0; c < 8; ++c) y[c] = fmaf(tt, sh.X[blk][m * LX + cb + c], y[c]);
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c) T[(I0 + r) * LC + J0 + cb + c] = -y[c];
@@ -173,29 +174,41 @@ __device__ __forceinline__ void unit_lower_inverse(Smem& sh, int tid) {
   }
 }
 
+// Stores a warp's m16n8 accumulator tiles acc[j] (rows r0 + g, r0 + g + 8; columns n0 + 8 j + 2 t, + 1) into a
+// row-major shared matrix of stride ld.
+template <int NJ>
+__device__ __forceinline__ void store_tiles(float* m, int ld, const float (&acc)[NJ][4], int r0, int n0, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int c = n0 + 8 * j + 2 * t;
+    *reinterpret_cast<float2*>(&m[(r0 + g) * ld + c]) = make_float2(acc[j][0], acc[j][1]);
+    *reinterpret_cast<float2*>(&m[(r0 + g + 8) * ld + c]) = make_float2(acc[j][2], acc[j][3]);
+  }
+}
+
 __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sh = *reinterpret_cast<Smem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
-  const int half = blockIdx.x & 1;
-  const int rh = blockIdx.x >> 1;  // r * H + h
+  const int rh = blockIdx.x;  // r * H + h
   const int r = rh / p.H, h = rh % p.H;
   const int64_t base = (int64_t)rh * p.T;  // token row of (r, h, t = 0) in q / k / v / o, and in g / beta
   pdl_wait();
-  for (int e = tid * 4; e < DK * DH; e += NT * 4) {  // the initial state's columns of this half
-    const int kk = e / DH, c = e % DH;
+  for (int e = tid * 4; e < DK * DV; e += NT * 4) {  // the initial state
+    const int kk = e / DV, c = e % DV;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.s0) {
       const int sr = p.s0_rows == 1 ? 0 : r;
-      s = *reinterpret_cast<const float4*>(p.s0 + (((int64_t)sr * p.H + h) * DK + kk) * DV + half * DH + c);
+      s = *reinterpret_cast<const float4*>(p.s0 + (((int64_t)sr * p.H + h) * DK + kk) * DV + c);
     }
-    *reinterpret_cast<float4*>(&sh.S[kk * LH + c]) = s;
+    *reinterpret_cast<float4*>(&sh.S[kk * LV + c]) = s;
   }
-  // the 16-row tile and the 8-column tiles of this warp: 64 x 64 products (2 warps a row tile, 4 column tiles each),
-  // 64 x 128 (8 column tiles each), 128 x 64 (a row tile each, 8 column tiles)
-  const int rt = (warp >> 1) * 16, nq = (warp & 1) * 32, nw = (warp & 1) * 64;
-  const int rs = warp * 16, ns = 0;
+  // this warp's tiles: 64 x 64 products 16 rows x 16 columns (NJ = 2), 64 x 128 products 16 x 32 (NJ = 4), the
+  // 128 x 128 state update 16 x 64 (NJ = 8)
+  const int rt = (warp >> 2) * 16, n16 = (warp & 3) * 16, n32 = (warp & 3) * 32;
+  const int rs = (warp >> 1) * 16, n64 = (warp & 1) * 64;
   for (int t0 = 0; t0 < p.T; t0 += CH) {
     const int n = min(CH, p.T - t0);
     // ---- chunk loads: K and Q row-major, beta, G ----
@@ -207,7 +220,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
         qv = __ldg(reinterpret_cast<const float4*>(p.q + (base + t0 + i) * DK) + f);
       }
       *reinterpret_cast<float4*>(&sh.K[i * LK + 4 * f]) = kv;
-      *reinterpret_cast<float4*>(&sh.Q[i * LK + 4 * f]) = qv;
+      *reinterpret_cast<float4*>(&sh.QW[i * LK + 4 * f]) = qv;
     }
     if (tid < CH) {
       sh.B[tid] = tid < n ? __ldg(p.beta + base + t0 + tid) : 0.0f;
@@ -221,18 +234,18 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
         sh.G[i] = acc;
       }
     }
-    for (int e = tid; e < CH * DH / 4; e += NT) {  // beta V
-      const int i = e / (DH / 4), f = e % (DH / 4);
+    for (int e = tid; e < CH * DV / 4; e += NT) {  // beta V
+      const int i = e / (DV / 4), f = e % (DV / 4);
       float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < n) {
-        val = __ldg(reinterpret_cast<const float4*>(p.v + (base + t0 + i) * DV + half * DH) + f);
+        val = __ldg(reinterpret_cast<const float4*>(p.v + (base + t0 + i) * DV) + f);
         const float bt = sh.B[i];
         val.x *= bt;
         val.y *= bt;
         val.z *= bt;
         val.w *= bt;
       }
-      *reinterpret_cast<float4*>(&sh.V[i * LH + 4 * f]) = val;
+      *reinterpret_cast<float4*>(&sh.V[i * LV + 4 * f]) = val;
     }
     __syncthreads();
     if (tid < CH) {  // read after the inverse's barriers
@@ -241,76 +254,71 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
     }
     // ---- A_ij = beta_i (k_i . k_j) e^{G_i - G_j} for j < i ----
     {
-      float kk[4][4];
+      float kk[2][4];
       zero(kk);
-      warp_mm<4, DK>(kk, rt, nq, [&](int i, int c) { return sh.K[i * LK + c]; },
+      warp_mm<2, DK>(kk, rt, n16, [&](int i, int c) { return sh.K[i * LK + c]; },
                      [&](int c, int j) { return sh.K[j * LK + c]; }, lane);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int i = rt + g8 + (e >> 1) * 8, jj = nq + 8 * j + 2 * t4 + (e & 1);
-          sh.A[i * LC + jj] = jj < i ? sh.B[i] * kk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
+          const int i = rt + g8 + (e >> 1) * 8, jj = n16 + 8 * j + 2 * t4 + (e & 1);
+          sh.AP[i * LC + jj] = jj < i ? sh.B[i] * kk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
         }
     }
     __syncthreads();
-    unit_lower_inverse(sh, tid);  // ends with a barrier
-    // ---- P = (q_i . k_j) e^{G_i - G_j} for j <= i (into P, the inverse's scratch until now) ----
+    unit_lower_inverse(sh, tid);  // ends with a barrier; A is not read again
+    // ---- P = (q_i . k_j) e^{G_i - G_j} for j <= i (into A's place) ----
     {
-      float qk[4][4];
+      float qk[2][4];
       zero(qk);
-      warp_mm<4, DK>(qk, rt, nq, [&](int i, int c) { return sh.Q[i * LK + c]; },
+      warp_mm<2, DK>(qk, rt, n16, [&](int i, int c) { return sh.QW[i * LK + c]; },
                      [&](int c, int j) { return sh.K[j * LK + c]; }, lane);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int i = rt + g8 + (e >> 1) * 8, jj = nq + 8 * j + 2 * t4 + (e & 1);
-          sh.P[i * LC + jj] = jj <= i ? qk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
+          const int i = rt + g8 + (e >> 1) * 8, jj = n16 + 8 * j + 2 * t4 + (e & 1);
+          sh.AP[i * LC + jj] = jj <= i ? qk[j][e] * expf(sh.G[i] - sh.G[jj]) : 0.0f;
         }
     }
-    // ---- U = T (beta V) [64 x 64] (kept) and W = T (beta e^G K) [64 x 128] (into W) ----
-    float u[4][4];
+    // ---- Q S and U = T (beta V) [64 x 128], kept in registers ----
+    float qs[4][4], u[4][4];
+    zero(qs);
     zero(u);
-    warp_mm<4, CH>(u, rt, nq, [&](int i, int k) { return sh.Tm[i * LC + k]; },
-                   [&](int k, int c) { return sh.V[k * LH + c]; }, lane);
+    warp_mm<4, DK>(qs, rt, n32, [&](int i, int k) { return sh.QW[i * LK + k]; },
+                   [&](int k, int c) { return sh.S[k * LV + c]; }, lane);
+    warp_mm<4, CH>(u, rt, n32, [&](int i, int k) { return sh.Tm[i * LC + k]; },
+                   [&](int k, int c) { return sh.V[k * LV + c]; }, lane);
+    __syncthreads();  // every read of Q is done (P, Q S)
+    // ---- W = T (beta e^G K) [64 x 128] (into Q's place) ----
     {
-      float w[8][4];
+      float w[4][4];
       zero(w);
-      warp_mm<8, CH>(w, rt, nw, [&](int i, int k) { return sh.Tm[i * LC + k]; },
+      warp_mm<4, CH>(w, rt, n32, [&](int i, int k) { return sh.Tm[i * LC + k]; },
                      [&](int k, int c) { return sh.K[k * LK + c] * sh.EB[k]; }, lane);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = nw + 8 * j + 2 * t4;
-        *reinterpret_cast<float2*>(&sh.W[(rt + g8) * LK + c]) = make_float2(w[j][0], w[j][1]);
-        *reinterpret_cast<float2*>(&sh.W[(rt + g8 + 8) * LK + c]) = make_float2(w[j][2], w[j][3]);
-      }
+      store_tiles(sh.QW, LK, w, rt, n32, lane);
     }
-    __syncthreads();  // W and P are complete; every read of beta V is done
-    // ---- V' = U - W S [64 x 64] (into V) ----
+    __syncthreads();  // W and P are complete; every read of beta V is done (U)
+    // ---- V' = U - W S [64 x 128] (into V) ----
     {
       float ws[4][4];
       zero(ws);
-      warp_mm<4, DK>(ws, rt, nq, [&](int i, int k) { return sh.W[i * LK + k]; },
-                     [&](int k, int c) { return sh.S[k * LH + c]; }, lane);
+      warp_mm<4, DK>(ws, rt, n32, [&](int i, int k) { return sh.QW[i * LK + k]; },
+                     [&](int k, int c) { return sh.S[k * LV + c]; }, lane);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = nq + 8 * j + 2 * t4;
-        *reinterpret_cast<float2*>(&sh.V[(rt + g8) * LH + c]) = make_float2(u[j][0] - ws[j][0], u[j][1] - ws[j][1]);
-        *reinterpret_cast<float2*>(&sh.V[(rt + g8 + 8) * LH + c]) =
-            make_float2(u[j][2] - ws[j][2], u[j][3] - ws[j][3]);
-      }
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) u[j][e] -= ws[j][e];
+      store_tiles(sh.V, LV, u, rt, n32, lane);
     }
     __syncthreads();
     // ---- O = e^G (Q S) + P V' ----
     {
-      float o[4][4], pv[4][4];
-      zero(o);
+      float pv[4][4];
       zero(pv);
-      warp_mm<4, DK>(o, rt, nq, [&](int i, int k) { return sh.Q[i * LK + k]; },
-                     [&](int k, int c) { return sh.S[k * LH + c]; }, lane);
-      warp_mm<4, CH>(pv, rt, nq, [&](int i, int k) { return sh.P[i * LC + k]; },
-                     [&](int k, int c) { return sh.V[k * LH + c]; }, lane);
+      warp_mm<4, CH>(pv, rt, n32, [&](int i, int k) { return sh.AP[i * LC + k]; },
+                     [&](int k, int c) { return sh.V[k * LV + c]; }, lane);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int i = rt + g8 + hh * 8;
@@ -318,41 +326,40 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
           const float eg = expf(sh.G[i]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int c = nq + 8 * j + 2 * t4;
-            *reinterpret_cast<float2*>(p.o + (base + t0 + i) * DV + half * DH + c) =
-                make_float2(fmaf(eg, o[j][2 * hh], pv[j][2 * hh]), fmaf(eg, o[j][2 * hh + 1], pv[j][2 * hh + 1]));
+            const int c = n32 + 8 * j + 2 * t4;
+            *reinterpret_cast<float2*>(p.o + (base + t0 + i) * DV + c) =
+                make_float2(fmaf(eg, qs[j][2 * hh], pv[j][2 * hh]), fmaf(eg, qs[j][2 * hh + 1], pv[j][2 * hh + 1]));
           }
         }
       }
     }
-    // ---- S <- e^{G_last} S + (e^{G_last - G} K)^T V' [128 x 64] ----
+    // ---- S <- e^{G_last} S + (e^{G_last - G} K)^T V' [128 x 128] ----
     {
       const float gl = sh.G[CH - 1];
       float sn[8][4];
       zero(sn);
-      warp_mm<8, CH>(sn, rs, ns, [&](int kk, int i) { return sh.K[i * LK + kk] * sh.ED[i]; },
-                     [&](int i, int c) { return sh.V[i * LH + c]; }, lane);
+      warp_mm<8, CH>(sn, rs, n64, [&](int kk, int i) { return sh.K[i * LK + kk] * sh.ED[i]; },
+                     [&](int i, int c) { return sh.V[i * LV + c]; }, lane);
       const float egl = expf(gl);
       float old[8][4];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          old[j][e] = sh.S[(rs + g8 + (e >> 1) * 8) * LH + ns + 8 * j + 2 * t4 + (e & 1)];
+        for (int e = 0; e < 4; ++e) old[j][e] = sh.S[(rs + g8 + (e >> 1) * 8) * LV + n64 + 8 * j + 2 * t4 + (e & 1)];
       __syncthreads();  // every thread has read S (W S, Q S) and its own entries of it
 #pragma unroll
       for (int j = 0; j < 8; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          sh.S[(rs + g8 + (e >> 1) * 8) * LH + ns + 8 * j + 2 * t4 + (e & 1)] = fmaf(egl, old[j][e], sn[j][e]);
+          sh.S[(rs + g8 + (e >> 1) * 8) * LV + n64 + 8 * j + 2 * t4 + (e & 1)] = fmaf(egl, old[j][e], sn[j][e]);
     }
     __syncthreads();
   }
   if (p.s_out) {
-    for (int e = tid * 4; e < DK * DH; e += NT * 4) {
-      const int kk = e / DH, c = e % DH;
-      *reinterpret_cast<float4*>(p.s_out + ((int64_t)rh * DK + kk) * DV + half * DH + c) =
-          *reinterpret_cast<const float4*>(&sh.S[kk * LH + c]);
+    for (int e = tid * 4; e < DK * DV; e += NT * 4) {
+      const int kk = e / DV, c = e % DV;
+      *reinterpret_cast<float4*>(p.s_out + ((int64_t)rh * DK + kk) * DV + c) =
+          *reinterpret_cast<const float4*>(&sh.S[kk * LV + c]);
     }
   }
   pdl_launch();
