@@ -61,13 +61,15 @@ struct Smem {
   float ED[CH];          // e^{G_last - G_i}
 };
 
+// x rounded to TF32 (10 mantissa bits), to nearest with ties away from zero, as cvt.rna.tf32.f32 rounds a finite
+// value: half a unit of the 13th bit added to the magnitude bits, the 13 bits then cleared (integer operations,
+// which issue at full rate).
+__device__ __forceinline__ uint32_t rna_tf32(uint32_t b) { return (b + 0x1000u) & 0xFFFFE000u; }
+
+// x = hi + lo, both TF32 (x - hi is exact in fp32).
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  uint32_t h, l;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-  const float r = x - __uint_as_float(h);
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
-  hi = h;
-  lo = l;
+  hi = rna_tf32(__float_as_uint(x));
+  lo = rna_tf32(__float_as_uint(x - __uint_as_float(hi)));
 }
 
 __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
