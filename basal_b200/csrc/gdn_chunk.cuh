@@ -61,6 +61,10 @@ struct Smem {
   float ED[CH];          // e^{G_last - G_i}
 };
 
+__device__ __forceinline__ void prefetch_l2(const void* a) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(a)));
+}
+
 // x rounded to TF32 (10 mantissa bits), to nearest with ties away from zero, as cvt.rna.tf32.f32 rounds a finite
 // value: half a unit of the 13th bit added to the magnitude bits, the 13 bits then cleared (integer operations,
 // which issue at full rate).
@@ -227,6 +231,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
     if (tid < CH) {
       sh.B[tid] = tid < n ? __ldg(p.beta + base + t0 + tid) : 0.0f;
       sh.G[tid] = tid < n ? __ldg(p.g + base + t0 + tid) : 0.0f;
+    }
+    {  // ask L2 for the next chunk's keys, queries and values (128-byte lines), so its loads do not wait for DRAM
+      const int n2 = min(CH, p.T - t0 - CH);
+      for (int e = tid; e < 3 * n2 * (DK * 4 / 128); e += NT) {
+        const int m = e / (n2 * 4), rem = e % (n2 * 4);
+        const float* src = m == 0 ? p.k : (m == 1 ? p.q : p.v);
+        prefetch_l2(src + (base + t0 + CH + rem / 4) * DK + (rem % 4) * 32);
+      }
     }
     __syncthreads();
     if (tid == 0) {  // cumulative gates, in token order
