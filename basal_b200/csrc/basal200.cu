@@ -42,10 +42,10 @@ int current_device(int* dev) {
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
 enum SmemSlot {
   kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50,
-  kSlotRes = 58, kSlotGdn = 62, kSlotLogitsTc = 64
+  kSlotRes = 58, kSlotGdn = 62, kSlotLogitsTc = 64, kSlotGdnV = 76
 };
 // kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7,
-// kSlotRes .. + 3, kSlotGdn, kSlotLogitsTc .. + 11 (bits of a 128-bit mask)
+// kSlotRes .. + 3, kSlotGdn, kSlotLogitsTc .. + 11, kSlotGdnV .. + 1 (bits of a 128-bit mask)
 
 bool smem_is_set(int dev, int slot) { return (g_dev[dev].smem_set[slot >> 6] >> (slot & 63)) & 1; }
 
@@ -908,7 +908,7 @@ int rms_quant(const void* x, int xt, const void* w, float eps, int64_t M, int64_
 
 int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_rows, const void* conv, int kw,
              const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk, int Hv, float* q,
-             float* k, float* v, float* beta, float* g, cudaStream_t st) {
+             float* k, void* v, float* beta, float* g, cudaStream_t st) {
   if (rows < 0 || T < 0 || Hk <= 0 || Hv <= 0 || kw < 1) return BASAL200_ERR_ARG;
   if (Hv % Hk || kw != 4) return BASAL200_ERR_SHAPE;  // the kernel's convolution has 4 taps (Qwen 3.5's)
   if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
@@ -917,7 +917,7 @@ int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_ro
   if (tail && tail_rows != 1 && tail_rows != rows) return BASAL200_ERR_ARG;
   const int64_t C = (int64_t)(2 * Hk + Hv) * 128;
   if (ld < C || b_off < 0 || a_off < 0 || b_off + Hv > ld || a_off + Hv > ld) return BASAL200_ERR_SHAPE;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(conv) || (ld % 4) ||
+  if (!aligned16(q) || !aligned16(k) || (reinterpret_cast<uintptr_t>(v) & 7) || !aligned16(conv) || (ld % 4) ||
       (reinterpret_cast<uintptr_t>(proj) & 7) || (tail && (reinterpret_cast<uintptr_t>(tail) & 7)))
     return BASAL200_ERR_ALIGN;  // 8-byte loads of 4 channels, 16-byte loads of 4 channels' weights
   const int64_t items = (int64_t)rows * T * Hk;  // a warp each, 8 a CTA
@@ -972,16 +972,26 @@ int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, in
                     z_off, static_cast<const __half*>(gw), eps, rows, T, Hv, static_cast<__half*>(y), q, s);
 }
 
-int gdn_chunk(const float* q, const float* k, const float* v, const float* g, const float* beta, const float* s0,
-              int s0_rows, float* o, float* s_out, int rows, int H, int T, cudaStream_t st) {
-  if (rows < 0 || H <= 0 || T < 0) return BASAL200_ERR_ARG;
+template <typename TV>
+int gdn_chunk_launch(int dev, int slot, const gdnchunk::Params& p, cudaStream_t st) {
+  constexpr size_t smem = sizeof(gdnchunk::Smem);
+  int rc = set_smem(dev, slot, gdnchunk::gdn_chunk_kernel<TV>, smem);
+  if (rc) return rc;
+  return launch_pdl(gdnchunk::gdn_chunk_kernel<TV>, (unsigned)(p.rows * p.H), gdnchunk::NT, smem, st, p);
+}
+
+int gdn_chunk(const float* q, const float* k, const void* v, int v_dtype, const float* g, const float* beta,
+              const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk, int H, int T, cudaStream_t st) {
+  if (rows < 0 || Hk <= 0 || H <= 0 || T < 0) return BASAL200_ERR_ARG;
+  if (H % Hk) return BASAL200_ERR_SHAPE;
+  if (v_dtype != BASAL200_F32 && v_dtype != BASAL200_BF16 && v_dtype != BASAL200_F16) return BASAL200_ERR_DTYPE;
   if (rows == 0) return BASAL200_OK;
   if (T > 0 && (!q || !k || !v || !g || !beta || !o)) return BASAL200_ERR_ARG;  // no tokens: nothing of them is read
   if (s0 && s0_rows != 1 && s0_rows != rows) return BASAL200_ERR_ARG;
   if ((T > 0 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))) || (s0 && !aligned16(s0)) ||
       (s_out && !aligned16(s_out)))
     return BASAL200_ERR_ALIGN;
-  if ((int64_t)rows * H * 2 > INT32_MAX || (int64_t)rows * H * T * 128 > ((int64_t)1 << 40)) return BASAL200_ERR_LIMIT;
+  if ((int64_t)rows * H > INT32_MAX || (int64_t)rows * H * T * 128 > ((int64_t)1 << 40)) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   if (T == 0) {  // no tokens: the state passes through unchanged
@@ -994,8 +1004,6 @@ int gdn_chunk(const float* q, const float* k, const float* v, const float* g, co
         return BASAL200_ERR_LAUNCH;
     return BASAL200_OK;
   }
-  constexpr size_t smem = sizeof(gdnchunk::Smem);
-  if ((rc = set_smem(dev, kSlotGdn, gdnchunk::gdn_chunk_kernel, smem))) return rc;
   gdnchunk::Params p;
   p.q = q;
   p.k = k;
@@ -1007,9 +1015,12 @@ int gdn_chunk(const float* q, const float* k, const float* v, const float* g, co
   p.o = o;
   p.s_out = s_out;
   p.rows = rows;
+  p.Hk = Hk;
   p.H = H;
   p.T = T;
-  return launch_pdl(gdnchunk::gdn_chunk_kernel, (unsigned)(rows * H), gdnchunk::NT, smem, st, p);
+  if (v_dtype == BASAL200_F32) return gdn_chunk_launch<float>(dev, kSlotGdn, p, st);
+  if (v_dtype == BASAL200_BF16) return gdn_chunk_launch<__nv_bfloat16>(dev, kSlotGdnV, p, st);
+  return gdn_chunk_launch<__half>(dev, kSlotGdnV + 1, p, st);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -1187,7 +1198,7 @@ int basal200_rms_norm_fp8_quant(const void* x, int x_dtype, const void* w, float
 
 int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail, int tail_rows, const void* conv,
                       int kw, const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk,
-                      int Hv, float* q, float* k, float* v, float* beta, float* g, void* stream) {
+                      int Hv, float* q, float* k, void* v, float* beta, float* g, void* stream) {
   return gdn_prep(proj, dtype, ld, tail, tail_rows, conv, kw, A_log, dt_bias, b_off, a_off, rows, T, Hk, Hv, q, k, v,
                   beta, g, as_stream(stream));
 }
@@ -1198,10 +1209,10 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
   return gdn_gate_quant(o, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
 }
 
-int basal200_gdn_chunk_rule(const float* q, const float* k, const float* v, const float* g, const float* beta,
-                            const float* s0, int s0_rows, float* o, float* s_out, int rows, int H, int T,
-                            void* stream) {
-  return gdn_chunk(q, k, v, g, beta, s0, s0_rows, o, s_out, rows, H, T, as_stream(stream));
+int basal200_gdn_chunk_rule(const float* q, const float* k, const void* v, int v_dtype, const float* g,
+                            const float* beta, const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk,
+                            int H, int T, void* stream) {
+  return gdn_chunk(q, k, v, v_dtype, g, beta, s0, s0_rows, o, s_out, rows, Hk, H, T, as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing

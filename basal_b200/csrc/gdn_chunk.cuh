@@ -35,16 +35,16 @@ constexpr int LC = CH + 4;  // row stride of A, T, P (read along rows)
 constexpr int LX = 17;      // row stride of the inverse's 16 x 16 scratch blocks
 
 struct Params {
-  const float* q;      // [rows, H, T, 128] (l2-normed, scaled)
-  const float* k;      // [rows, H, T, 128] (l2-normed)
-  const float* v;      // [rows, H, T, 128]
+  const float* q;      // [rows, Hk, T, 128] (l2-normed, scaled); value head h reads key head h / (H / Hk)
+  const float* k;      // [rows, Hk, T, 128] (l2-normed)
+  const void* v;       // [rows, H, T, 128], fp32 or 16-bit
   const float* g;      // [rows, H, T]
   const float* beta;   // [rows, H, T]
   const float* s0;     // [s0_rows, H, 128, 128] or null (zeros); s0_rows 1 (shared) or rows
   int s0_rows;
   float* o;            // [rows, H, T, 128]
   float* s_out;        // [rows, H, 128, 128] or null
-  int rows, H, T;
+  int rows, Hk, H, T;
 };
 
 struct Smem {
@@ -193,6 +193,17 @@ __device__ __forceinline__ void store_tiles(float* m, int ld, const float (&acc)
   }
 }
 
+// 4 consecutive values of v -> fp32
+__device__ __forceinline__ float4 load_v4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+template <typename TV>
+__device__ __forceinline__ float4 load_v4(const TV* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const TV* h = reinterpret_cast<const TV*>(&u);
+  return make_float4(static_cast<float>(h[0]), static_cast<float>(h[1]), static_cast<float>(h[2]),
+                     static_cast<float>(h[3]));
+}
+
+template <typename TV>
 __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sh = *reinterpret_cast<Smem*>(smem_raw);
@@ -200,7 +211,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
   const int g8 = lane >> 2, t4 = lane & 3;
   const int rh = blockIdx.x;  // r * H + h
   const int r = rh / p.H, h = rh % p.H;
-  const int64_t base = (int64_t)rh * p.T;  // token row of (r, h, t = 0) in q / k / v / o, and in g / beta
+  const int64_t base = (int64_t)rh * p.T;  // token row of (r, h, t = 0) in v / o, and in g / beta
+  const int64_t base_qk = ((int64_t)r * p.Hk + h / (p.H / p.Hk)) * p.T;  // ... in q / k (its key head)
+  const TV* vsrc = static_cast<const TV*>(p.v);
   pdl_wait();
   for (int e = tid * 4; e < DK * DV; e += NT * 4) {  // the initial state
     const int kk = e / DV, c = e % DV;
@@ -222,8 +235,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
       const int i = e / (DK / 4), f = e % (DK / 4);
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
       if (i < n) {
-        kv = __ldg(reinterpret_cast<const float4*>(p.k + (base + t0 + i) * DK) + f);
-        qv = __ldg(reinterpret_cast<const float4*>(p.q + (base + t0 + i) * DK) + f);
+        kv = __ldg(reinterpret_cast<const float4*>(p.k + (base_qk + t0 + i) * DK) + f);
+        qv = __ldg(reinterpret_cast<const float4*>(p.q + (base_qk + t0 + i) * DK) + f);
       }
       *reinterpret_cast<float4*>(&sh.K[i * LK + 4 * f]) = kv;
       *reinterpret_cast<float4*>(&sh.QW[i * LK + 4 * f]) = qv;
@@ -234,10 +247,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
     }
     {  // ask L2 for the next chunk's keys, queries and values (128-byte lines), so its loads do not wait for DRAM
       const int n2 = min(CH, p.T - t0 - CH);
-      for (int e = tid; e < 3 * n2 * (DK * 4 / 128); e += NT) {
-        const int m = e / (n2 * 4), rem = e % (n2 * 4);
-        const float* src = m == 0 ? p.k : (m == 1 ? p.q : p.v);
-        prefetch_l2(src + (base + t0 + CH + rem / 4) * DK + (rem % 4) * 32);
+      constexpr int VL = DV * (int)sizeof(TV) / 128;  // lines of a value row
+      for (int e = tid; e < n2 * (8 + VL); e += NT) {
+        const int i = e / (8 + VL), l = e % (8 + VL);
+        if (l < 8) {
+          prefetch_l2((l < 4 ? p.k : p.q) + (base_qk + t0 + CH + i) * DK + (l % 4) * 32);
+        } else {
+          prefetch_l2(vsrc + (base + t0 + CH + i) * DV + (l - 8) * (128 / (int)sizeof(TV)));
+        }
       }
     }
     __syncthreads();
@@ -252,7 +269,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
       const int i = e / (DV / 4), f = e % (DV / 4);
       float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < n) {
-        val = __ldg(reinterpret_cast<const float4*>(p.v + (base + t0 + i) * DV) + f);
+        val = load_v4(vsrc + (base + t0 + i) * DV + 4 * f);
         const float bt = sh.B[i];
         val.x *= bt;
         val.y *= bt;

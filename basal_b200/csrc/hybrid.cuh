@@ -7,7 +7,8 @@
 //   gdn_prep_kernel       the Gated DeltaNet's causal depthwise convolution (k taps) + SiLU over the q / k / v
 //                         channels of the merged input projection, rounded to 16 bits, the l2 norms of q and k (q also
 //                         scaled by dk^-1/2), beta = sigmoid(b), g = -e^A_log softplus(a + dt_bias): the recurrence's
-//                         operands, head-major [rows, value heads, T, d] fp32 (key heads repeated for their values)
+//                         operands, head-major: q, k [rows, key heads, T, d] fp32, v [rows, value heads, T, d] in
+//                         the 16-bit type (its values are 16-bit already), beta, g [rows, value heads, T] fp32
 //   gdn_gate_quant_kernel the Gated DeltaNet's output: each value head's 128 values rounded to 16 bits, RMS-normed,
 //                         times the norm weight, times SiLU(z), rounded, and quantised as one 1 x 128 group (a head is
 //                         exactly one group of the output projection's input)
@@ -141,9 +142,9 @@ struct PrepParams {
   int b_off, a_off;   // columns of b and a in proj
   int rows, T, Hk, Hv;
   float q_scale;      // dk^-1/2
-  float* q;           // [rows, Hv, T, 128]
+  float* q;           // [rows, Hk, T, 128]
   float* k;
-  float* v;
+  void* v;            // [rows, Hv, T, 128] 16-bit
   float* beta;        // [rows, Hv, T]
   float* g;
 };
@@ -238,15 +239,20 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
     ko.y = __fmul_rn(kv[1], rk);
     ko.z = __fmul_rn(kv[2], rk);
     ko.w = __fmul_rn(kv[3], rk);
+    const int64_t oqk = (((int64_t)r * p.Hk + h) * p.T + t) * 128 + c0;
+    *reinterpret_cast<float4*>(p.q + oqk) = qo;
+    *reinterpret_cast<float4*>(p.k + oqk) = ko;
     const int rep = p.Hv / p.Hk;
     for (int j = 0; j < rep; ++j) {
       const int vh = h * rep + j;
       const int64_t o = (((int64_t)r * p.Hv + vh) * p.T + t) * 128 + c0;
-      *reinterpret_cast<float4*>(p.q + o) = qo;
-      *reinterpret_cast<float4*>(p.k + o) = ko;
       float vv[4];
       conv4<T>(src, conv, 2 * p.Hk * 128 + vh * 128 + c0, vv);
-      *reinterpret_cast<float4*>(p.v + o) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      uint2 u;
+      T* uh = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) uh[i] = from_f<T>(vv[i]);  // exact: conv4 rounded them to T
+      *reinterpret_cast<uint2*>(static_cast<T*>(p.v) + o) = u;
       if (lane == 0) {
         const T* pr = src[3];
         const float bb = to_f<T>(pr[p.b_off + vh]);

@@ -485,15 +485,17 @@ def _(x, w, eps):
 def gdn_prep(proj: Tensor, tail: Optional[Tensor], conv: Tensor, A_log: Tensor, dt_bias: Tensor, rows: int, T: int,
              Hk: int, Hv: int, b_off: int, a_off: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The Gated DeltaNet's convolution (with the inputs before token 0 in tail [1 or rows, kw - 1, C]), SiLU, l2 norms
-    and gates over proj [rows * T, ld] -> q, k, v [rows, Hv, T, 128] fp32, beta, g [rows, Hv, T] fp32."""
+    and gates over proj [rows * T, ld] -> q, k [rows, Hk, T, 128] fp32, v [rows, Hv, T, 128] in proj's dtype (16-bit
+    values already), beta, g [rows, Hv, T] fp32."""
     require_cuda(proj, tail, conv, A_log, dt_bias)
     if proj.stride(-1) != 1:
         proj = proj.contiguous()
     conv = _c(conv.to(proj.dtype))
     tail = None if tail is None else _c(tail.to(proj.dtype))
     dev = proj.device
-    q = torch.empty((rows, Hv, T, 128), dtype=torch.float32, device=dev)
-    k, v = torch.empty_like(q), torch.empty_like(q)
+    q = torch.empty((rows, Hk, T, 128), dtype=torch.float32, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty((rows, Hv, T, 128), dtype=proj.dtype, device=dev)
     beta = torch.empty((rows, Hv, T), dtype=torch.float32, device=dev)
     g = torch.empty_like(beta)
     call("basal200_gdn_prep", dev, ptr(proj), code(proj.dtype), proj.stride(0), ptr(tail),
@@ -504,9 +506,9 @@ def gdn_prep(proj: Tensor, tail: Optional[Tensor], conv: Tensor, A_log: Tensor, 
 
 @gdn_prep.register_fake
 def _(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off):
-    q = proj.new_empty((rows, Hv, T, 128), dtype=torch.float32)
+    q = proj.new_empty((rows, Hk, T, 128), dtype=torch.float32)
     b = proj.new_empty((rows, Hv, T), dtype=torch.float32)
-    return q, q.new_empty(q.shape), q.new_empty(q.shape), b, b.new_empty(b.shape)
+    return q, q.new_empty(q.shape), proj.new_empty((rows, Hv, T, 128)), b, b.new_empty(b.shape)
 
 
 @torch.library.custom_op("basal::gdn_gate_fp8_quant", mutates_args=())
@@ -536,21 +538,24 @@ def _(o, proj, z_off, gw, eps, rows, T):
 @torch.library.custom_op("basal::gdn_chunk_rule", mutates_args=())
 def gdn_chunk_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor,
                    s0: Optional[Tensor]) -> tuple[Tensor, Tensor]:
-    """The gated delta rule (fp32) over q, k, v [rows, H, T, 128], g, beta [rows, H, T] from the state s0 [1 or rows, H,
-    128, 128] (None: zeros) -> (o [rows, H, T, 128], the final state [rows, H, 128, 128])."""
+    """The gated delta rule (fp32) over q, k [rows, Hk, T, 128] (value head h reads key head h / (H / Hk)), v [rows, H,
+    T, 128] (fp32 or 16-bit), g, beta [rows, H, T] from the state s0 [1 or rows, H, 128, 128] (None: zeros) -> (o
+    [rows, H, T, 128] fp32, the final state [rows, H, 128, 128])."""
     require_cuda(q, k, v, g, beta, s0)
-    q, k, v, g, beta = (_c(t.float()) for t in (q, k, v, g, beta))
-    rows, H, T, _ = q.shape
-    o = torch.empty_like(v)
+    q, k, g, beta = (_c(t.float()) for t in (q, k, g, beta))
+    v = _c(v if v.dtype in (torch.bfloat16, torch.float16) else v.float())
+    rows, Hk, T, _ = q.shape
+    H = v.shape[1]
+    o = torch.empty(v.shape, dtype=torch.float32, device=q.device)
     s = torch.empty((rows, H, 128, 128), dtype=torch.float32, device=q.device)
     if s0 is not None:
         s0 = _c(s0.float())
-    call("basal200_gdn_chunk_rule", q.device, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(s0),
-         0 if s0 is None else s0.shape[0], ptr(o), ptr(s), rows, H, T)
+    call("basal200_gdn_chunk_rule", q.device, ptr(q), ptr(k), ptr(v), code(v.dtype), ptr(g), ptr(beta), ptr(s0),
+         0 if s0 is None else s0.shape[0], ptr(o), ptr(s), rows, Hk, H, T)
     return o, s
 
 
 @gdn_chunk_rule.register_fake
 def _(q, k, v, g, beta, s0):
-    rows, H = q.shape[0], q.shape[1]
-    return v.new_empty(v.shape), v.new_empty((rows, H, 128, 128))
+    rows, H = v.shape[0], v.shape[1]
+    return q.new_empty(v.shape), q.new_empty((rows, H, 128, 128))

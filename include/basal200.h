@@ -188,11 +188,11 @@ int basal200_rms_norm_fp8_quant(const void* x, int x_dtype, const void* w, float
  * causal depthwise convolution of kw taps (conv [C, kw], C = (2 Hk + Hv) * 128; tail [tail_rows, kw - 1, C] the inputs
  * before token 0, tail_rows 1 (shared) or rows, or NULL for zeros) and SiLU, rounded to `dtype`; the l2 norms of q and
  * k (eps 1e-6; q also times 128^-1/2); beta = sigmoid(b) rounded; g = -exp(A_log) * softplus(a + dt_bias) in fp32.
- * Outputs are head-major fp32: q, k, v [rows, Hv, T, 128] (a key head's q and k repeated for its Hv / Hk value heads),
- * beta, g [rows, Hv, T]. */
+ * Outputs are head-major: q, k [rows, Hk, T, 128] fp32 (one per key head), v [rows, Hv, T, 128] in `dtype` (its
+ * values are `dtype` values already), beta, g [rows, Hv, T] fp32. */
 int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail, int tail_rows, const void* conv,
                       int kw, const float* A_log, const void* dt_bias, int b_off, int a_off, int rows, int T, int Hk,
-                      int Hv, float* q, float* k, float* v, float* beta, float* g, void* stream);
+                      int Hv, float* q, float* k, void* v, float* beta, float* g, void* stream);
 
 /* The Gated DeltaNet's output steps (basal/gdn_graph.py:432-438, Qwen3_5RMSNormGated) fused with the FP8 quantiser of
  * the output projection's input: o [rows, Hv, Tp, 128] fp32 (the recurrence's output, Tp >= T), z in a [rows * T, ld]
@@ -205,13 +205,14 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
 
 /* The gated delta rule of the Gated DeltaNet layers (transformers' torch_chunk_gated_delta_rule / fla's
  * chunk_gated_delta_rule, called by basal/gdn_graph.py:81-87, :492-493), fp32: per row r and value head h, from the
- * state s0 [s0_rows, H, 128, 128] (s0_rows 1: shared by every row; NULL: zeros), over T tokens of q, k, v
- * [rows, H, T, 128] (q, k l2-normed, q scaled as basal200_gdn_prep leaves them), g, beta [rows, H, T]:
- * S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T, o_t = S_t^T q_t -> o [rows, H, T, 128], and
- * the final state into s_out [rows, H, 128, 128] (may be NULL). Computed over chunks of 64 tokens. */
-int basal200_gdn_chunk_rule(const float* q, const float* k, const float* v, const float* g, const float* beta,
-                            const float* s0, int s0_rows, float* o, float* s_out, int rows, int H, int T,
-                            void* stream);
+ * state s0 [s0_rows, H, 128, 128] (s0_rows 1: shared by every row; NULL: zeros), over T tokens of q, k
+ * [rows, Hk, T, 128] fp32 (value head h reads key head h / (H / Hk); l2-normed, q scaled, as basal200_gdn_prep leaves
+ * them), v [rows, H, T, 128] (v_dtype fp32, bf16 or fp16), g, beta [rows, H, T] fp32:
+ * S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T, o_t = S_t^T q_t -> o [rows, H, T, 128] fp32,
+ * and the final state into s_out [rows, H, 128, 128] (may be NULL). Computed over chunks of 64 tokens. */
+int basal200_gdn_chunk_rule(const float* q, const float* k, const void* v, int v_dtype, const float* g,
+                            const float* beta, const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk,
+                            int H, int T, void* stream);
 
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)

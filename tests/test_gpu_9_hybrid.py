@@ -104,11 +104,12 @@ def test_gdn_prep_kernel(hy, rows, T, Hk, Hv):
                                                                                           dtype=BF)):
         got = ops.gdn_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off)
         want = torch_prep(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off)
+        assert got[0].shape == (rows, Hk, T, 128) and got[2].dtype == BF  # q, k once per key head; v in bf16
         for name, a, b in zip("qkvbg", got, want):
-            if name in "qk":
-                assert (a - b).abs().max() <= 1e-6, name
+            if name in "qk":  # the torch statement repeats a key head for its value heads
+                assert (a - b[:, ::Hv // Hk]).abs().max() <= 1e-6, name
             else:
-                assert torch.equal(a, b), name
+                assert torch.equal(a.float(), b), name
 
 
 def test_gdn_gate_quant_kernel(hy):
@@ -358,3 +359,30 @@ def test_attention_into_prefix_buffers_equals_concatenation(hy):
         want, wk, wv = model._attention(L, h, cos, sin, pk, pv)
         got, gk, gv = model._attention(L, h, cos, sin, pk, pv, st.kv_buffers(0, b, T))
         assert torch.equal(got, want) and torch.equal(gk, wk) and torch.equal(gv, wv)
+
+
+@pytest.mark.parametrize("vdt", [torch.bfloat16, torch.float16])
+def test_gdn_chunk_rule_key_heads_and_16bit_values(hy, vdt):
+    """q, k once per key head (2 value heads each) and 16-bit v, as basal::gdn_prep leaves them: the per-token
+    definition on the repeated keys and the widened values within 1e-4; and the same bits as fp32 copies of the repeated
+    q, k and of v."""
+    from basal_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(11)
+    rows, Hk, H, T = 2, 2, 4, 100
+    n = lambda x: x * torch.rsqrt((x * x).sum(-1, keepdim=True) + 1e-6)  # noqa: E731
+    q = n(torch.randn(rows, Hk, T, 128, device="cuda", generator=g)) * 128 ** -0.5
+    k = n(torch.randn(rows, Hk, T, 128, device="cuda", generator=g))
+    v = torch.randn(rows, H, T, 128, device="cuda", generator=g).to(vdt)
+    gl = -torch.rand(rows, H, T, device="cuda", generator=g) * 2
+    beta = torch.rand(rows, H, T, device="cuda", generator=g)
+    s0 = torch.randn(1, H, 128, 128, device="cuda", generator=g) * 0.1
+    o, S = ops.gdn_chunk_rule(q, k, v, gl, beta, s0)
+    qr, kr = q.repeat_interleave(2, 1), k.repeat_interleave(2, 1)
+    o2, S2 = ops.gdn_chunk_rule(qr, kr, v.float(), gl, beta, s0)
+    assert torch.equal(o, o2) and torch.equal(S, S2)
+    c = lambda t: t.cpu().numpy()  # noqa: E731
+    for r in range(rows):
+        oo, SS = ohy.delta_rule(c(qr[r]).transpose(1, 0, 2), c(kr[r]).transpose(1, 0, 2),
+                                c(v[r].float()).transpose(1, 0, 2), c(gl[r]).T, c(beta[r]).T, c(s0[0]))
+        assert np.abs(c(o[r]).transpose(1, 0, 2) - oo).max() <= 1e-4 * max(1.0, np.abs(oo).max())
+        assert np.abs(c(S[r]) - SS).max() <= 1e-4 * max(1.0, np.abs(SS).max())
