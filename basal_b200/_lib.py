@@ -42,6 +42,8 @@ SIGNATURES = {
     "basal200_nvfp4_gemm": [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P],
     "basal200_nvfp4_linear": [_P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
     "basal200_nvfp4_quantize": [_P, _I, _I64, _I64, _P, _P, _P, _P],
+    "basal200_attn_prep": [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _F, _P, _P, _I64, _I, _P, _P, _P, _I64, _I64, _P],
+    "basal200_attn_gate_fp8_quant": [_P, _I, _P, _I64, _I, _I, _I, _P, _P, _P],
     "basal200_code_logits": [_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _P, _I64, _P, _I, _F, _P, _P],
     "basal200_code_probs": [_P, _I64, _I64, _P, _P, _I64, _P, _P],
     "basal200_fp8_block_gemm_glu": [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P, _I64, _P],

@@ -972,6 +972,70 @@ int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, in
                     z_off, static_cast<const __half*>(gw), eps, rows, T, Hv, static_cast<__half*>(y), q, s);
 }
 
+// The attention layer's input steps (q / k norms, rotary embedding, keys and values into their buffers) and its
+// output gate fused with the output projection's quantiser; heads of 128.
+int attn_prep(const void* qkv, int dt, int64_t ld, int rows, int T, int H, int Hk, const void* q_norm,
+              const void* k_norm, float eps, const void* cos, const void* sin, int64_t cs_row, int rot, void* q_out,
+              void* k_out, void* v_out, int64_t kv_len, int64_t kv_off, cudaStream_t st) {
+  if (rows < 0 || T < 0 || H <= 0 || Hk <= 0 || !(eps >= 0.0f) || cs_row < 0 || kv_off < 0) return BASAL200_ERR_ARG;
+  if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (rot < 0 || rot > 128 || rot % 8 || kv_off + T > kv_len || ld < (int64_t)H * 256 + (int64_t)Hk * 256)
+    return BASAL200_ERR_SHAPE;
+  if (rows == 0 || T == 0) return BASAL200_OK;
+  if (!qkv || !q_norm || !k_norm || !q_out || !k_out || !v_out || (rot > 0 && (!cos || !sin))) return BASAL200_ERR_ARG;
+  if ((ld % 4) || (reinterpret_cast<uintptr_t>(qkv) & 7) || (reinterpret_cast<uintptr_t>(q_norm) & 7) ||
+      (reinterpret_cast<uintptr_t>(k_norm) & 7) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out))
+    return BASAL200_ERR_ALIGN;
+  const int64_t items = (int64_t)rows * T * (H + Hk);  // a warp each, 8 a CTA
+  if ((items + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  hybrid::AttnPrepParams p;
+  p.qkv = qkv;
+  p.ld = ld;
+  p.rows = rows;
+  p.T = T;
+  p.H = H;
+  p.Hk = Hk;
+  p.q_norm = q_norm;
+  p.k_norm = k_norm;
+  p.eps = eps;
+  p.cos = cos;
+  p.sin = sin;
+  p.cs_row = cs_row;
+  p.rot = rot;
+  p.q_out = q_out;
+  p.k_out = k_out;
+  p.v_out = v_out;
+  p.kv_len = kv_len;
+  p.kv_off = kv_off;
+  const unsigned grid = (unsigned)((items + 7) / 8);
+  if (dt == BASAL200_BF16) return launch_pdl(hybrid::attn_prep_kernel<__nv_bfloat16>, grid, 256, 0, st, p);
+  return launch_pdl(hybrid::attn_prep_kernel<__half>, grid, 256, 0, st, p);
+}
+
+int attn_gate_quant(const void* o, int dt, const void* qkv, int64_t ld, int rows, int T, int H, uint8_t* q, float* s,
+                    cudaStream_t st) {
+  if (rows < 0 || T < 0 || H <= 0) return BASAL200_ERR_ARG;
+  if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (ld < (int64_t)H * 256) return BASAL200_ERR_SHAPE;
+  if (rows == 0 || T == 0) return BASAL200_OK;
+  if (!o || !qkv || !q || !s) return BASAL200_ERR_ARG;
+  if ((ld % 8) || !aligned16(o) || !aligned16(qkv) || !aligned16(q) || (reinterpret_cast<uintptr_t>(s) & 3))
+    return BASAL200_ERR_ALIGN;
+  const int64_t warps = ((int64_t)rows * T * H + 1) / 2;  // a half-warp per (token, head)
+  if ((warps + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
+  int dev, rc = current_device(&dev);
+  if (rc) return rc;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  if (dt == BASAL200_BF16)
+    return launch_pdl(hybrid::attn_gate_quant_kernel<__nv_bfloat16>, grid, 256, 0, st,
+                      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(qkv), ld, rows, T, H, q,
+                      s);
+  return launch_pdl(hybrid::attn_gate_quant_kernel<__half>, grid, 256, 0, st, static_cast<const __half*>(o),
+                    static_cast<const __half*>(qkv), ld, rows, T, H, q, s);
+}
+
 template <typename TV>
 int gdn_chunk_launch(int dev, int slot, const gdnchunk::Params& p, cudaStream_t st) {
   constexpr size_t smem = sizeof(gdnchunk::Smem);
@@ -1207,6 +1271,18 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream) {
   return gdn_gate_quant(o, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
+}
+
+int basal200_attn_prep(const void* qkv, int dtype, int64_t ld, int rows, int T, int H, int Hk, const void* q_norm,
+                       const void* k_norm, float eps, const void* cos, const void* sin, int64_t cs_row, int rot,
+                       void* q_out, void* k_out, void* v_out, int64_t kv_len, int64_t kv_off, void* stream) {
+  return attn_prep(qkv, dtype, ld, rows, T, H, Hk, q_norm, k_norm, eps, cos, sin, cs_row, rot, q_out, k_out, v_out,
+                   kv_len, kv_off, as_stream(stream));
+}
+
+int basal200_attn_gate_fp8_quant(const void* o, int dtype, const void* qkv, int64_t ld, int rows, int T, int H,
+                                 uint8_t* q, float* s, void* stream) {
+  return attn_gate_quant(o, dtype, qkv, ld, rows, T, H, q, s, as_stream(stream));
 }
 
 int basal200_gdn_chunk_rule(const float* q, const float* k, const void* v, int v_dtype, const float* g,

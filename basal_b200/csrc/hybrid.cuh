@@ -333,5 +333,132 @@ __global__ void __launch_bounds__(256) gdn_gate_quant_kernel(const float* __rest
   pdl_launch();
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Attention input: a warp per (token, head) of the merged q+gate / k / v projection (qkv [rows * T, ld], per token
+// [H heads x (128 q, 128 gate) | Hk x 128 k | Hk x 128 v]), 4 values a lane. q and k heads: Qwen3_5RMSNorm with their
+// weight (RN16(RN(x * r) * RN(1 + w)), r = rsqrt(mean(x^2) + eps)), then the rotary embedding of the first `rot`
+// dimensions (x1 cos - x2 sin, x2 cos + x1 sin, every product and sum rounded to 16 bits as torch's ops round them;
+// cos / sin [rows or 1, T, rot]); the partner dimensions rot / 2 away sit rot / 8 lanes away. q goes to q_out
+// [rows, H, T, 128]; k and the head's v to k_out / v_out [rows, Hk, kv_len, 128] at position kv_off + t, so that the
+// rows' keys land after a prefix's already in the buffer.
+// ---------------------------------------------------------------------------------------------------------------
+struct AttnPrepParams {
+  const void* qkv;
+  int64_t ld;
+  int rows, T, H, Hk;
+  const void* q_norm;   // [128]
+  const void* k_norm;   // [128]
+  float eps;
+  const void* cos;      // [rows or 1, T, rot] 16-bit
+  const void* sin;
+  int64_t cs_row;       // elements between rows of cos / sin (0: shared)
+  int rot;              // rotated dimensions (a multiple of 8, at most 128)
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  int64_t kv_len, kv_off;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) attn_prep_kernel(const AttnPrepParams p) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int heads = p.H + p.Hk;
+  if (item < (int64_t)p.rows * p.T * heads) {  // warp-uniform
+    const int j = (int)(item % heads);
+    const int64_t tok = item / heads;  // r * T + t
+    const int t = (int)(tok % p.T), r = (int)(tok / p.T);
+    const bool isq = j < p.H;
+    const int h = isq ? j : j - p.H;
+    const T* x = static_cast<const T*>(p.qkv) + tok * p.ld;
+    const T* src = isq ? x + h * 256 : x + (int64_t)p.H * 256 + h * 128;
+    const T* w = static_cast<const T*>(isq ? p.q_norm : p.k_norm);
+    float v[4], wv[4];
+    ld4(src + lane * 4, v);
+    ld4(w + lane * 4, wv);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    const float rr = rsqrtf(__fadd_rn(__fdiv_rn(warp_sum(ss), 128.0f), p.eps));
+    float y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = round_to<T>(__fmul_rn(__fmul_rn(v[i], rr), __fadd_rn(1.0f, wv[i])));
+    const int hl = p.rot / 8;  // lanes of half the rotated dimensions
+    const int partner = lane < hl ? lane + hl : lane - hl;
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float other = __shfl_sync(0xffffffffu, y[i], partner & 31);
+      o[i] = y[i];
+      if (lane < 2 * hl) {
+        const int64_t ci = (int64_t)r * p.cs_row + (int64_t)t * p.rot + lane * 4 + i;
+        const float c = to_f<T>(static_cast<const T*>(p.cos)[ci]);
+        const float sn = to_f<T>(static_cast<const T*>(p.sin)[ci]);
+        const float a = round_to<T>(__fmul_rn(y[i], c)), b = round_to<T>(__fmul_rn(other, sn));
+        o[i] = lane < hl ? round_to<T>(__fsub_rn(a, b)) : round_to<T>(__fadd_rn(a, b));
+      }
+    }
+    T* dst = isq ? static_cast<T*>(p.q_out) + (((int64_t)r * p.H + h) * p.T + t) * 128
+                 : static_cast<T*>(p.k_out) + (((int64_t)r * p.Hk + h) * p.kv_len + p.kv_off + t) * 128;
+    uint2 u;
+    T* uh = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) uh[i] = from_f<T>(o[i]);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = u;
+    if (!isq) {  // the head's values, copied
+      const T* vs = x + (int64_t)p.H * 256 + (int64_t)p.Hk * 128 + h * 128 + lane * 4;
+      T* vd = static_cast<T*>(p.v_out) + (((int64_t)r * p.Hk + h) * p.kv_len + p.kv_off + t) * 128 + lane * 4;
+      *reinterpret_cast<uint2*>(vd) = *reinterpret_cast<const uint2*>(vs);
+    }
+  }
+  pdl_launch();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Attention output gate + FP8 quantiser: a half-warp per (token, head), 8 values a lane. o [rows, H, T, 128] (the
+// attention's output), gate in qkv (the second 128 values of each head's q+gate pair): a = RN16(o * RN16(sigmoid(g)))
+// as torch computes o * sigmoid(gate) in 16 bits; each head's 128 values are one quantisation group of the output
+// projection's input: codes q [rows * T, H * 128], scales s [rows * T, H], as act_quant_block_kernel's.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) attn_gate_quant_kernel(const T* __restrict__ o, const T* __restrict__ qkv,
+                                                              int64_t ld, int rows, int ntok, int H,
+                                                              uint8_t* __restrict__ q, float* __restrict__ s) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 15;
+  const int64_t item = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * 2 + (lane >> 4);
+  const bool live = item < (int64_t)rows * ntok * H;
+  float v[8];
+  int64_t tok = 0;
+  int h = 0;
+  if (live) {
+    h = (int)(item % H);
+    tok = item / H;  // r * T + t
+    const int t = (int)(tok % ntok), r = (int)(tok / ntok);
+    float ov[8], gv[8];
+    ld8(o + (((int64_t)r * H + h) * ntok + t) * 128 + l * 8, ov);
+    ld8(qkv + tok * ld + h * 256 + 128 + l * 8, gv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = round_to<T>(__fmul_rn(ov[i], round_to<T>(sigmoid_f(gv[i]))));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o2 = 8; o2 >= 1; o2 >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o2));
+  const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+  const uint2 codes = block_codes8<false>(v, sc);
+  if (live) {
+    *reinterpret_cast<uint2*>(q + tok * (int64_t)H * 128 + h * 128 + l * 8) = codes;
+    if (l == 0) s[tok * H + h] = sc;
+  }
+  pdl_launch();
+}
+
 }  // namespace hybrid
 }  // namespace b200

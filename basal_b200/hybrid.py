@@ -93,20 +93,6 @@ def rms(x, w, eps):
     return (h * (1.0 + w.float())).to(x.dtype)
 
 
-def rope(x, cos, sin, r, out=None):
-    """The first r dims of each head [b, heads, T, d] rotated by the half-split rule (basal/gdn_graph.py:446-451):
-    x1 cos - x2 sin, x2 cos + x1 sin for the halves x1, x2 of those dims, each product and sum rounded to x's dtype as
-    the reference's (x cos + rotate_half(x) sin) rounds them. Written into out (a new tensor when None)."""
-    out = torch.empty(x.shape, dtype=x.dtype, device=x.device) if out is None else out
-    h = r // 2
-    c, s = cos[:, None], sin[:, None]
-    x1, x2 = x[..., :h], x[..., h:r]
-    out[..., :h] = x1 * c[..., :h] - x2 * s[..., :h]
-    out[..., h:r] = x2 * c[..., h:] + x1 * s[..., h:]
-    out[..., r:] = x[..., r:]
-    return out
-
-
 def rope_tables(cfg, pos, dtype):
     """cos, sin [b, T, r] of positions pos [b, T] (fp32 maths, then dtype, as the rotary embedding module returns)."""
     r = cfg.rotary_dims
@@ -144,6 +130,8 @@ class HybridClassifier:
     """The C5 hybrid with random weights (generator `seed`) on `device`; every linear FP8-block quantised."""
 
     def __init__(self, cfg=C5, device="cuda", seed=0, dtype=torch.bfloat16, residual_std=None):
+        if cfg.head_dim != 128 or cfg.lin_k_dim != 128 or cfg.lin_v_dim != 128:
+            raise ValueError("the attention and Gated DeltaNet kernels of this build take heads of 128")
         self.cfg, self.dtype = cfg, dtype
         dev = torch.device(device)
         self.device = dev
@@ -224,41 +212,36 @@ class HybridClassifier:
 
     def _attention(self, L, h, cos, sin, pk, pv, bufs=None):
         """h + attention(rms(h)) over the prefix keys / values pk, pv [1, kv heads, P, d] (or none) and the rows'
-        own tokens, causally (basal/gdn_graph.py:452-466, :578-604) -> (h, the rows' keys, values). bufs: key and
-        value buffers [b, kv heads, P + T, d] that hold the prefix's (PrefixState.kv_buffers); the rows' keys and
-        values are written after it instead of concatenated."""
+        own tokens, causally (basal/gdn_graph.py:452-466, :578-604) -> (h, the rows' keys, values). The norms and rotary
+        embedding are one kernel (basal::attn_prep), which writes the rows' keys and values after the prefix's into
+        bufs (PrefixState.kv_buffers, [b, kv heads, P + T, d], the prefix's already there) or into new buffers; the
+        output gate is fused with the output projection's quantiser, the residual add is in that GEMM's epilogue."""
         cfg = self.cfg
-        b, T, _ = h.shape
+        b, T, D = h.shape
         H, Hk, d = cfg.heads, cfg.kv_heads, cfg.head_dim
-        q8, s8 = ops.rms_norm_fp8_quant(h.reshape(-1, cfg.hidden), L["nw"], cfg.eps)
+        q8, s8 = ops.rms_norm_fp8_quant(h.reshape(-1, D), L["nw"], cfg.eps)
         w = L["w_qkv"]
-        qg, k, v = ops.fp8_block_gemm(q8, s8, w.weight, w.weight_scale, h.dtype).view(b, T, -1).split(cfg.qkv_sizes,
-                                                                                                        -1)
-        q, gate = torch.chunk(qg.view(b, T, H, 2 * d), 2, dim=-1)
+        qkv = ops.fp8_block_gemm(q8, s8, w.weight, w.weight_scale, h.dtype)  # [b * T, (q, gate) * H | k | v]
         P = 0 if pk is None else pk.shape[2]
-        q = rope(rms(q, L["q_norm"], cfg.eps).transpose(1, 2), cos, sin, cfg.rotary_dims)
-        kn = rms(k.view(b, T, Hk, d), L["k_norm"], cfg.eps).transpose(1, 2)
-        v = v.view(b, T, Hk, d).transpose(1, 2)
-        G = H // Hk
         if P and bufs is not None:
             kk, vv = bufs
-            k = rope(kn, cos, sin, cfg.rotary_dims, out=kk[:, :, P:])
-            vv[:, :, P:].copy_(v)
-            v = vv[:, :, P:]
-        elif P:
-            k = rope(kn, cos, sin, cfg.rotary_dims)
-            kk = torch.cat([pk.expand(b, -1, -1, -1), k], 2)
-            vv = torch.cat([pv.expand(b, -1, -1, -1), v], 2)
         else:
-            k = rope(kn, cos, sin, cfg.rotary_dims)
-            kk, vv = k, v
+            kk, vv = h.new_empty(b, Hk, P + T, d), h.new_empty(b, Hk, P + T, d)
+            if P:
+                kk[:, :, :P].copy_(pk.expand(b, -1, -1, -1))
+                vv[:, :, :P].copy_(pv.expand(b, -1, -1, -1))
+        # the q / k norms and rotary embedding, the rows' keys and values written after the prefix's
+        q = ops.attn_prep(qkv, L["q_norm"], L["k_norm"], cfg.eps, cos, sin, cfg.rotary_dims, H, Hk, b, T, kk, vv, P)
+        G = H // Hk
         own = torch.ones(T, T, dtype=torch.bool, device=h.device).tril()
         allow = torch.cat([torch.ones(T, P, dtype=torch.bool, device=h.device), own], 1)
         allow = allow[None, None, None].expand(1, 1, G, T, P + T).reshape(1, 1, G * T, P + T)
         o = F.scaled_dot_product_attention(q.reshape(b, Hk, G * T, d), kk, vv, attn_mask=allow,
                                            scale=1.0 / math.sqrt(d)).reshape(b, H, T, d)
-        a = o.transpose(1, 2).reshape(b, T, H * d) * torch.sigmoid(gate.reshape(b, T, H * d))
-        return L["o"].forward_residual(a, h), k, v
+        qa, sa = ops.attn_gate_fp8_quant(o, qkv, b, T, H)  # o * sigmoid(gate), quantised for the output projection
+        out = L["o"]
+        h = ops.fp8_block_gemm_residual(qa, sa, out.weight, out.weight_scale, out.bias, h.reshape(-1, D))
+        return h.view(b, T, D), kk[:, :, P:], vv[:, :, P:]
 
     def _layers(self, ids, pos, st):
         cfg = self.cfg

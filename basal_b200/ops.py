@@ -29,8 +29,12 @@
   basal::gdn_gate_fp8_quant(o, proj, z_off, gw, eps, rows, T)
                                                  its gated output norm fused with the FP8 quantiser (gdn_graph.py:432-438)
   basal::gdn_chunk_rule(q, k, v, g, beta, s0)   its gated delta rule over chunks of 64 tokens (gdn_graph.py:81-87)
+  basal::attn_prep(qkv, q_norm, k_norm, eps, cos, sin, rot, H, Hk, rows, T, k_buf, v_buf, kv_off)
+                                                 the attention's q / k norms and rotary embedding (gdn_graph.py:452-460)
+  basal::attn_gate_fp8_quant(o, qkv, rows, T, H) its output gate fused with the FP8 quantiser (gdn_graph.py:464-466)
 
-Every op is functional (mutates_args=()), allocates its outputs (and scratch) from the caching allocator, enqueues on
+Every op but attn_prep is functional (mutates_args=(); attn_prep writes the keys and values into the buffers it is
+given), allocates its outputs (and scratch) from the caching allocator, enqueues on
 the current stream and never synchronises: Dynamo traces them through their fake kernels and a CUDA graph captures
 their launches. They need CUDA tensors; there is no CPU implementation.
 """
@@ -509,6 +513,52 @@ def _(proj, tail, conv, A_log, dt_bias, rows, T, Hk, Hv, b_off, a_off):
     q = proj.new_empty((rows, Hk, T, 128), dtype=torch.float32)
     b = proj.new_empty((rows, Hv, T), dtype=torch.float32)
     return q, q.new_empty(q.shape), proj.new_empty((rows, Hv, T, 128)), b, b.new_empty(b.shape)
+
+
+@torch.library.custom_op("basal::attn_prep", mutates_args=("k_buf", "v_buf"))
+def attn_prep(qkv: Tensor, q_norm: Tensor, k_norm: Tensor, eps: float, cos: Tensor, sin: Tensor, rot: int, H: int,
+              Hk: int, rows: int, T: int, k_buf: Tensor, v_buf: Tensor, kv_off: int) -> Tensor:
+    """The attention layer's input steps over the merged projection qkv [rows * T, ld] (per token H heads of (128 q,
+    128 gate), Hk of 128 k, Hk of 128 v): q and k RMS-normed with q_norm / k_norm, their first rot dims rotated by
+    cos / sin [rows or 1, T, rot] -> q [rows, H, T, 128]; k and v written into k_buf / v_buf [rows, Hk, L, 128] at
+    positions kv_off .. kv_off + T - 1."""
+    require_cuda(qkv, q_norm, k_norm, cos, sin, k_buf, v_buf)
+    if qkv.stride(-1) != 1:
+        qkv = qkv.contiguous()
+    dt = qkv.dtype
+    q_norm, k_norm = _c(q_norm.to(dt)), _c(k_norm.to(dt))
+    cos, sin = _c(cos.to(dt)), _c(sin.to(dt))
+    if not (k_buf.is_contiguous() and v_buf.is_contiguous()):
+        raise ValueError("attn_prep: the key and value buffers must be contiguous")
+    q = torch.empty((rows, H, T, 128), dtype=dt, device=qkv.device)
+    cs_row = 0 if cos.shape[0] == 1 else cos.stride(0)
+    call("basal200_attn_prep", qkv.device, ptr(qkv), code(dt), qkv.stride(0), rows, T, H, Hk, ptr(q_norm),
+         ptr(k_norm), float(eps), ptr(cos), ptr(sin), cs_row, rot, ptr(q), ptr(k_buf), ptr(v_buf), k_buf.shape[2],
+         kv_off)
+    return q
+
+
+@attn_prep.register_fake
+def _(qkv, q_norm, k_norm, eps, cos, sin, rot, H, Hk, rows, T, k_buf, v_buf, kv_off):
+    return qkv.new_empty((rows, H, T, 128))
+
+
+@torch.library.custom_op("basal::attn_gate_fp8_quant", mutates_args=())
+def attn_gate_fp8_quant(o: Tensor, qkv: Tensor, rows: int, T: int, H: int) -> tuple[Tensor, Tensor]:
+    """The attention's output o [rows, H, T, 128] times sigmoid of the gates in qkv (as for attn_prep), quantised for
+    the output projection -> (e4m3 codes [rows * T, H * 128], fp32 scales [rows * T, H])."""
+    require_cuda(o, qkv)
+    o, qkv = _c(o), _c(qkv)
+    q = torch.empty((rows * T, H * 128), dtype=E4M3, device=o.device)
+    s = torch.empty((rows * T, H), dtype=torch.float32, device=o.device)
+    call("basal200_attn_gate_fp8_quant", o.device, ptr(o), code(o.dtype), ptr(qkv), qkv.stride(0), rows, T, H, ptr(q),
+         ptr(s))
+    return q, s
+
+
+@attn_gate_fp8_quant.register_fake
+def _(o, qkv, rows, T, H):
+    return o.new_empty((rows * T, H * 128), dtype=E4M3), o.new_empty((rows * T, H), dtype=torch.float32)
 
 
 @torch.library.custom_op("basal::gdn_gate_fp8_quant", mutates_args=())

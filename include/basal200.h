@@ -203,6 +203,25 @@ int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream);
 
+/* The attention layers' input steps (basal/gdn_graph.py:452-460, Qwen 3.5 full attention with a gated output) over
+ * rows of T tokens of the merged projection qkv [rows * T, ld] (`dtype`; per token H heads of (128 q, 128 gate), then
+ * Hk heads of 128 k, then Hk of 128 v): q and k Qwen3_5RMSNorm'ed with q_norm / k_norm [128] (eps), rounded to
+ * `dtype`, then rotated in their first rot dimensions (rot % 8 == 0, rot <= 128; cos / sin [rows or 1, T, rot] with
+ * cs_row elements between rows, 0 when shared) by x1 cos - x2 sin, x2 cos + x1 sin with torch's roundings. q ->
+ * q_out [rows, H, T, 128]; k and v -> k_out / v_out [rows, Hk, kv_len, 128] at positions kv_off .. kv_off + T - 1
+ * (after a prefix's keys and values already there). A norm's sum of squares is in this kernel's own order, so a
+ * normed value may differ from torch's by one unit in the last place. */
+int basal200_attn_prep(const void* qkv, int dtype, int64_t ld, int rows, int T, int H, int Hk, const void* q_norm,
+                       const void* k_norm, float eps, const void* cos, const void* sin, int64_t cs_row, int rot,
+                       void* q_out, void* k_out, void* v_out, int64_t kv_len, int64_t kv_off, void* stream);
+
+/* The attention's output gate (basal/gdn_graph.py:464-466) fused with the FP8 quantiser of the output projection's
+ * input: o [rows, H, T, 128] (`dtype`), the gates in qkv as for basal200_attn_prep: a = o * sigmoid(gate) with
+ * torch's 16-bit roundings, quantised with one scale per head: q [rows * T, H * 128] e4m3, s [rows * T, H] fp32
+ * (bit-exact to basal200_fp8_act_quant of a). */
+int basal200_attn_gate_fp8_quant(const void* o, int dtype, const void* qkv, int64_t ld, int rows, int T, int H,
+                                 uint8_t* q, float* s, void* stream);
+
 /* The gated delta rule of the Gated DeltaNet layers (transformers' torch_chunk_gated_delta_rule / fla's
  * chunk_gated_delta_rule, called by basal/gdn_graph.py:81-87, :492-493), fp32: per row r and value head h, from the
  * state s0 [s0_rows, H, 128, 128] (s0_rows 1: shared by every row; NULL: zeros), over T tokens of q, k

@@ -386,3 +386,59 @@ def test_gdn_chunk_rule_key_heads_and_16bit_values(hy, vdt):
                                 c(v[r].float()).transpose(1, 0, 2), c(gl[r]).T, c(beta[r]).T, c(s0[0]))
         assert np.abs(c(o[r]).transpose(1, 0, 2) - oo).max() <= 1e-4 * max(1.0, np.abs(oo).max())
         assert np.abs(c(S[r]) - SS).max() <= 1e-4 * max(1.0, np.abs(SS).max())
+
+
+def _torch_attn_prep(qkv, qn, kn, eps, cos, sin, rot, H, Hk, rows, T, hy):
+    """The attention input steps in torch (the model's former form): Qwen3_5RMSNorm of q and k, then the rotary
+    embedding as the reference writes it, x cos + rotate_half(x) sin on the first rot dimensions."""
+    x = qkv.view(rows, T, -1)
+    q = x[..., :H * 256].view(rows, T, H, 256)[..., :128]
+    k = x[..., H * 256:H * 256 + Hk * 128].view(rows, T, Hk, 128)
+    v = x[..., H * 256 + Hk * 128:].view(rows, T, Hk, 128)
+
+    def rope(t):
+        tr = t[..., :rot]
+        rh = torch.cat([-tr[..., rot // 2:], tr[..., :rot // 2]], -1)
+        return torch.cat([tr * cos[:, None] + rh * sin[:, None], t[..., rot:]], -1)
+    return (rope(hy.rms(q, qn, eps).transpose(1, 2)), rope(hy.rms(k, kn, eps).transpose(1, 2)),
+            v.transpose(1, 2))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_attn_prep_kernel(hy, dt):
+    """basal::attn_prep against the torch statement: v bit for bit; q and k within 2 units in the last place or 2^-6
+    (a norm's sum of squares in the kernel's own order; the rotation's difference can cancel), nearly all equal; the keys and values land after a prefix already in
+    the buffers, which stays untouched; per-row rotary tables."""
+    from basal_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rows, T, H, Hk, P, rot = 3, 37, 4, 2, 5, 32
+    qkv = torch.randn(rows * T, H * 256 + Hk * 256, device="cuda", generator=g).to(dt)
+    qn = (torch.randn(128, device="cuda", generator=g) * 0.1).to(dt)
+    kn = (torch.randn(128, device="cuda", generator=g) * 0.1).to(dt)
+    ang = (torch.arange(P, P + T, device="cuda")[None, :, None] + torch.arange(rows, device="cuda")[:, None, None]) * \
+        torch.rand(rot // 2, device="cuda", generator=g)
+    cos, sin = torch.cat([ang, ang], -1).cos().to(dt), torch.cat([ang, ang], -1).sin().to(dt)
+    kb = torch.full((rows, Hk, P + T, 128), 7.0, device="cuda", dtype=dt)
+    vb = torch.full((rows, Hk, P + T, 128), -7.0, device="cuda", dtype=dt)
+    q = ops.attn_prep(qkv, qn, kn, 1e-6, cos, sin, rot, H, Hk, rows, T, kb, vb, P)
+    wq, wk, wv = _torch_attn_prep(qkv, qn, kn, 1e-6, cos, sin, rot, H, Hk, rows, T, hy)
+    assert torch.equal(vb[:, :, P:], wv) and (kb[:, :, :P] == 7).all() and (vb[:, :, :P] == -7).all()
+    for got, want in ((q, wq), (kb[:, :, P:], wk)):
+        d = (got.float() - want.float()).abs()
+        ulp = want.float().abs().clamp_min(1e-30) * (2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10)
+        assert (d <= torch.clamp(2 * ulp, min=2.0 ** -6)).all() and (d > 0).float().mean() < 0.01
+
+
+def test_attn_gate_quant_kernel(hy):
+    """basal::attn_gate_fp8_quant: the codes and scales of fp8_act_quant over o * sigmoid(gate) as torch computes it
+    in bf16, bit for bit."""
+    from basal_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(6)
+    rows, T, H, Hk = 3, 37, 4, 2
+    qkv = torch.randn(rows * T, H * 256 + Hk * 256, device="cuda", generator=g).to(BF)
+    o = torch.randn(rows, H, T, 128, device="cuda", generator=g).to(BF)
+    gate = qkv.view(rows, T, -1)[..., :H * 256].view(rows, T, H, 256)[..., 128:]
+    a = o.transpose(1, 2).reshape(rows, T, H * 128) * torch.sigmoid(gate.reshape(rows, T, H * 128))
+    wq, ws = ops.fp8_act_quant(a.reshape(rows * T, H * 128))
+    q, s = ops.attn_gate_fp8_quant(o, qkv, rows, T, H)
+    assert torch.equal(q.view(torch.uint8), wq.view(torch.uint8)) and torch.equal(s, ws)
