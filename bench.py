@@ -537,6 +537,35 @@ def run_sweep(fmts):
                               "fused_us": round(tf, 2), "unfused_us": round(tu, 2), "linear_alone_us": round(tl, 2)}),
                   flush=True)
         fmts = [f for f in fmts if f != "res"]
+    if "c5" in fmts:
+        # one C5 micro-batch (128 requests of 256 suffix tokens after the shared 1024-token prefix, 8 options): its time
+        # (CUDA events, after a warm-up call) and the device time of each kernel in it (torch profiler, one call)
+        from basal_b200 import hybrid, readout
+        model = hybrid.HybridClassifier(hybrid.C5, device=dev, seed=0)
+        prefix, suffix, options = c5_inputs(hybrid.C5.vocab)
+        ro = readout.CodeReadout(model.head)
+        rows, idx, pad = ro.rows([options] * C5_MICRO)
+        st = model.prefix(prefix.to(dev))
+        ids = suffix[:C5_MICRO].to(dev)
+        model.decide(ids, st, ro, rows, idx, pad)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        model.decide(ids, st, ro, rows, idx, pad)
+        e1.record()
+        torch.cuda.synchronize()
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            model.decide(ids, st, ro, rows, idx, pad)
+            torch.cuda.synchronize()
+        ev = [e for e in prof.key_averages() if e.device_time_total > 0]
+        total = sum(e.device_time_total for e in ev)
+        print(json.dumps({"sweep": "C5 micro-batch", "requests": C5_MICRO, "ms": round(e0.elapsed_time(e1), 2),
+                          "kernels_ms": round(total / 1e3, 2)}), flush=True)
+        for e in sorted(ev, key=lambda e: -e.device_time_total)[:16]:
+            print(json.dumps({"kernel": e.key[:90], "calls": e.count, "ms": round(e.device_time_total / 1e3, 3),
+                              "share": round(e.device_time_total / total, 4)}), flush=True)
+        fmts = [f for f in fmts if f != "c5"]
     if "readout" in fmts:
         # C4's readout: h [256, 2048] bf16 ~ N(0, 1) at the answer positions, a 151,936-row bf16 head ~ N(0, 0.02),
         # one code set of k ids shared by all rows; the device part of CodeReadout.probs per call (basal::code_logits +
@@ -942,7 +971,8 @@ def main():
     ap.add_argument("--no-decisions", action="store_true", help="skip the C5 decisions/s measurement")
     ap.add_argument("--decisions-only", action="store_true", help="only the C5 decisions/s measurement (one line)")
     ap.add_argument("--sweep", metavar="FMTS", help="run the C3/C4 sweeps for these parts (fp8,int8,nvfp4,readout, "
-                    "glu,res) instead of the benchmark; 'tp' (under torchrun): C5's column-parallel linears")
+                    "glu,res; c5: one C5 micro-batch and its kernels) instead of the benchmark; 'tp' (under "
+                    "torchrun): C5's column-parallel linears")
     args = ap.parse_args()
     if args.sweep == "tp":  # under torchrun, 2 or more GPUs
         import datetime
