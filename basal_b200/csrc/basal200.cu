@@ -920,7 +920,7 @@ int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_ro
   if (!aligned16(q) || !aligned16(k) || (reinterpret_cast<uintptr_t>(v) & 7) || !aligned16(conv) || (ld % 4) ||
       (reinterpret_cast<uintptr_t>(proj) & 7) || (tail && (reinterpret_cast<uintptr_t>(tail) & 7)))
     return BASAL200_ERR_ALIGN;  // 8-byte loads of 4 channels, 16-byte loads of 4 channels' weights
-  const int64_t items = (int64_t)rows * T * Hk;  // a warp each, 8 a CTA
+  const int64_t items = (int64_t)rows * Hk * ((T + hybrid::PTB - 1) / hybrid::PTB);  // a warp each, 8 a CTA
   if ((items + 7) / 8 > INT32_MAX) return BASAL200_ERR_LIMIT;
   int dev, rc = current_device(&dev);
   if (rc) return rc;

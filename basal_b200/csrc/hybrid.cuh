@@ -158,10 +158,22 @@ __device__ __forceinline__ void ld4(const T* p, float (&v)[4]) {
   for (int i = 0; i < 4; ++i) v[i] = to_f<T>(h[i]);
 }
 
-// The convolution (KW = 4 taps) + SiLU of channels col .. col + 3 at one token, from the token's 4 input rows src[j]
-// (null: zeros before the first input): acc = x_0 w_0, then acc = RN(acc + RN(x_j w_j)); y = RN16(silu(acc)).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// A warp takes PTB consecutive tokens of one row and key head: the convolution window (PTB + 3 input rows) and the
+// weights of each channel group are loaded once for the PTB tokens.
+constexpr int PTB = 4;
+
+// The convolution (4 taps) + SiLU of channels col .. col + 3 at tokens t0 .. t0 + PTB - 1 (those below ntok) from the
+// window's rows src[w] (input token t0 - 3 + w; null: zeros): acc = x_0 w_0, then acc = RN(acc + RN(x_j w_j)) over
+// the taps in order (torch's unfused products and sums); y = RN16(silu(acc)).
 template <typename T>
-__device__ __forceinline__ void conv4(const T* const (&src)[4], const T* conv, int col, float (&y)[4]) {
+__device__ __forceinline__ void conv4_tokens(const T* const (&src)[PTB + 3], const T* conv, int col,
+                                             float (&y)[PTB][4]) {
   float w[16];  // channel i, tap j at w[4 i + j]: the 4 channels' weights are 32 contiguous bytes
   {
     const uint4 a = *reinterpret_cast<const uint4*>(conv + (int64_t)col * 4);
@@ -174,25 +186,22 @@ __device__ __forceinline__ void conv4(const T* const (&src)[4], const T* conv, i
       w[8 + i] = to_f<T>(hb[i]);
     }
   }
-  float acc[4];
+  float x[PTB + 3][4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (src[j]) ld4(src[j] + col, x);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float prod = __fmul_rn(x[i], w[4 * i + j]);
-      acc[i] = j == 0 ? prod : __fadd_rn(acc[i], prod);
-    }
+  for (int k = 0; k < PTB + 3; ++k) {
+    x[k][0] = x[k][1] = x[k][2] = x[k][3] = 0.0f;
+    if (src[k]) ld4(src[k] + col, x[k]);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) y[i] = round_to<T>(silu_f(acc[i]));
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
+  for (int t = 0; t < PTB; ++t) {
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
+    for (int i = 0; i < 4; ++i) {
+      float acc = __fmul_rn(x[t][i], w[4 * i]);
+#pragma unroll
+      for (int j = 1; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(x[t + j][i], w[4 * i + j]));
+      y[t][i] = round_to<T>(silu_f(acc));
+    }
+  }
 }
 
 template <typename T>
@@ -200,68 +209,80 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int64_t items = (int64_t)p.rows * p.T * p.Hk;
-  if (item < items) {
+  const int nb = (p.T + PTB - 1) / PTB;
+  if (item < (int64_t)p.rows * p.Hk * nb) {  // warp-uniform
     const int h = (int)(item % p.Hk);
-    const int t = (int)((item / p.Hk) % p.T);
-    const int r = (int)(item / ((int64_t)p.Hk * p.T));
+    const int tb = (int)((item / p.Hk) % nb);
+    const int r = (int)(item / ((int64_t)p.Hk * nb));
+    const int t0 = tb * PTB, ntok = min(PTB, p.T - t0);
     const int C = (p.Hk * 2 + p.Hv) * 128;
     const T* proj = static_cast<const T*>(p.proj);
     const T* tail = static_cast<const T*>(p.tail);
     const T* conv = static_cast<const T*>(p.conv);
-    const T* src[4];  // the convolution's inputs at tokens t - 3 .. t (the tail's before token 0, or zeros)
+    const T* src[PTB + 3];  // input tokens t0 - 3 .. t0 + PTB - 1 (the tail's before token 0; null past the row)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int tt = t - 3 + j;
-      if (tt >= 0)
-        src[j] = proj + ((int64_t)r * p.T + tt) * p.ld;
+    for (int k = 0; k < PTB + 3; ++k) {
+      const int tt = t0 - 3 + k;
+      if (tt >= p.T)
+        src[k] = nullptr;
+      else if (tt >= 0)
+        src[k] = proj + ((int64_t)r * p.T + tt) * p.ld;
       else
-        src[j] = tail ? tail + ((int64_t)(p.tail_rows == 1 ? 0 : r) * 3 + 3 + tt) * C : nullptr;
+        src[k] = tail ? tail + ((int64_t)(p.tail_rows == 1 ? 0 : r) * 3 + 3 + tt) * C : nullptr;
     }
     const int c0 = lane * 4;
-    float qv[4], kv[4];
-    conv4<T>(src, conv, h * 128 + c0, qv);
-    conv4<T>(src, conv, p.Hk * 128 + h * 128 + c0, kv);
-    float sq = 0.0f, sk = 0.0f;
+    // q and k of key head h: l2 norms by warp sums (q also scaled), written once per key head
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sq = __fadd_rn(sq, __fmul_rn(qv[i], qv[i]));
-      sk = __fadd_rn(sk, __fmul_rn(kv[i], kv[i]));
+    for (int qk = 0; qk < 2; ++qk) {
+      float y[PTB][4];
+      conv4_tokens<T>(src, conv, qk * p.Hk * 128 + h * 128 + c0, y);
+      float* out = qk == 0 ? p.q : p.k;
+#pragma unroll
+      for (int t = 0; t < PTB; ++t) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(y[t][i], y[t][i]));
+        const float rn = rsqrtf(__fadd_rn(warp_sum(ss), 1e-6f));
+        if (t < ntok) {
+          float4 o4;
+          if (qk == 0) {
+            o4 = make_float4(__fmul_rn(__fmul_rn(y[t][0], rn), p.q_scale), __fmul_rn(__fmul_rn(y[t][1], rn), p.q_scale),
+                             __fmul_rn(__fmul_rn(y[t][2], rn), p.q_scale), __fmul_rn(__fmul_rn(y[t][3], rn), p.q_scale));
+          } else {
+            o4 = make_float4(__fmul_rn(y[t][0], rn), __fmul_rn(y[t][1], rn), __fmul_rn(y[t][2], rn),
+                             __fmul_rn(y[t][3], rn));
+          }
+          *reinterpret_cast<float4*>(out + (((int64_t)r * p.Hk + h) * p.T + t0 + t) * 128 + c0) = o4;
+        }
+      }
     }
-    const float rq = rsqrtf(__fadd_rn(warp_sum(sq), 1e-6f));
-    const float rk = rsqrtf(__fadd_rn(warp_sum(sk), 1e-6f));
-    float4 qo, ko;
-    qo.x = __fmul_rn(__fmul_rn(qv[0], rq), p.q_scale);
-    qo.y = __fmul_rn(__fmul_rn(qv[1], rq), p.q_scale);
-    qo.z = __fmul_rn(__fmul_rn(qv[2], rq), p.q_scale);
-    qo.w = __fmul_rn(__fmul_rn(qv[3], rq), p.q_scale);
-    ko.x = __fmul_rn(kv[0], rk);
-    ko.y = __fmul_rn(kv[1], rk);
-    ko.z = __fmul_rn(kv[2], rk);
-    ko.w = __fmul_rn(kv[3], rk);
-    const int64_t oqk = (((int64_t)r * p.Hk + h) * p.T + t) * 128 + c0;
-    *reinterpret_cast<float4*>(p.q + oqk) = qo;
-    *reinterpret_cast<float4*>(p.k + oqk) = ko;
+    // v of the value heads of key head h, 16-bit (conv4 rounded them already)
     const int rep = p.Hv / p.Hk;
     for (int j = 0; j < rep; ++j) {
       const int vh = h * rep + j;
-      const int64_t o = (((int64_t)r * p.Hv + vh) * p.T + t) * 128 + c0;
-      float vv[4];
-      conv4<T>(src, conv, 2 * p.Hk * 128 + vh * 128 + c0, vv);
-      uint2 u;
-      T* uh = reinterpret_cast<T*>(&u);
+      float y[PTB][4];
+      conv4_tokens<T>(src, conv, 2 * p.Hk * 128 + vh * 128 + c0, y);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) uh[i] = from_f<T>(vv[i]);  // exact: conv4 rounded them to T
-      *reinterpret_cast<uint2*>(static_cast<T*>(p.v) + o) = u;
-      if (lane == 0) {
-        const T* pr = src[3];
-        const float bb = to_f<T>(pr[p.b_off + vh]);
-        const float aa = to_f<T>(pr[p.a_off + vh]);
-        const int64_t bo = ((int64_t)r * p.Hv + vh) * p.T + t;
-        p.beta[bo] = round_to<T>(sigmoid_f(bb));
-        const float dt = to_f<T>(static_cast<const T*>(p.dt_bias)[vh]);
-        p.g[bo] = __fmul_rn(-expf(p.A_log[vh]), softplus_f(__fadd_rn(aa, dt)));
+      for (int t = 0; t < PTB; ++t) {
+        if (t < ntok) {
+          uint2 u;
+          T* uh = reinterpret_cast<T*>(&u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) uh[i] = from_f<T>(y[t][i]);
+          *reinterpret_cast<uint2*>(static_cast<T*>(p.v) + (((int64_t)r * p.Hv + vh) * p.T + t0 + t) * 128 + c0) = u;
+        }
       }
+    }
+    // beta and g: entry e = t * rep + j (lane e, e + 32, ..) for token t0 + t and value head h * rep + j
+    for (int e = lane; e < ntok * rep; e += 32) {
+      const int t = e / rep, vh = h * rep + e % rep;
+      const T* pr = proj + ((int64_t)r * p.T + t0 + t) * p.ld;
+      const float bb = to_f<T>(pr[p.b_off + vh]);
+      const float aa = to_f<T>(pr[p.a_off + vh]);
+      const int64_t bo = ((int64_t)r * p.Hv + vh) * p.T + t0 + t;
+      p.beta[bo] = round_to<T>(sigmoid_f(bb));
+      const float dt = to_f<T>(static_cast<const T*>(p.dt_bias)[vh]);
+      p.g[bo] = __fmul_rn(-expf(p.A_log[vh]), softplus_f(__fadd_rn(aa, dt)));
     }
   }
   pdl_launch();
