@@ -50,8 +50,8 @@ SIGNATURES = {
     "basal200_fp8_block_gemm_residual": [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I64, _P],
     "basal200_rms_norm_fp8_quant": [_P, _I, _P, _F, _I64, _I64, _P, _P, _P, _P],
     "basal200_gdn_prep": [_P, _I, _I64, _P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P],
-    "basal200_gdn_gate_fp8_quant": [_P, _I, _P, _I, _I64, _I, _P, _F, _I, _I, _I, _P, _P, _P, _P],
-    "basal200_gdn_chunk_rule": [_P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "basal200_gdn_gate_fp8_quant": [_P, _I, _I, _P, _I, _I64, _I, _P, _F, _I, _I, _I, _P, _P, _P, _P],
+    "basal200_gdn_chunk_rule": [_P, _P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _I, _I, _I, _P],
 }
 
 _lib = None

@@ -42,10 +42,10 @@ int current_device(int* dev) {
 // Bits of DeviceInfo::smem_set, one per kernel instantiation that needs more than the default shared memory.
 enum SmemSlot {
   kSlotBlock = 0, kSlotFp4 = 8, kSlotSmall = 14, kSlotSplit = 26, kSlotSplitQ = 30, kSlotLogits = 38, kSlotGlu = 50,
-  kSlotRes = 58, kSlotGdn = 62, kSlotLogitsTc = 64, kSlotGdnV = 76
+  kSlotRes = 58, kSlotGdn = 62, kSlotLogitsTc = 64, kSlotGdnV = 76, kSlotGdnVO = 78
 };
 // kSlotFp4 .. + 5, kSlotSmall .. + 11, kSlotSplit .. + 3, kSlotSplitQ .. + 7, kSlotLogits .. + 11, kSlotGlu .. + 7,
-// kSlotRes .. + 3, kSlotGdn, kSlotLogitsTc .. + 11, kSlotGdnV .. + 1 (bits of a 128-bit mask)
+// kSlotRes .. + 3, kSlotGdn, kSlotLogitsTc .. + 11, kSlotGdnV .. + 1, kSlotGdnVO .. + 1 (bits of a 128-bit mask)
 
 bool smem_is_set(int dev, int slot) { return (g_dev[dev].smem_set[slot >> 6] >> (slot & 63)) & 1; }
 
@@ -949,10 +949,19 @@ int gdn_prep(const void* proj, int dt, int64_t ld, const void* tail, int tail_ro
   return launch_pdl(hybrid::gdn_prep_kernel<__half>, grid, 256, 0, st, p);
 }
 
-int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, int z_off, const void* gw, float eps,
-                   int rows, int T, int Hv, void* y, uint8_t* q, float* s, cudaStream_t st) {
+template <typename T, typename TO>
+int gdn_gate_quant_launch(unsigned grid, const void* o, int Tp, const void* z, int64_t ld, int z_off, const void* gw,
+                          float eps, int rows, int ntok, int Hv, void* y, uint8_t* q, float* s, cudaStream_t st) {
+  return launch_pdl(hybrid::gdn_gate_quant_kernel<T, TO>, grid, 256, 0, st, static_cast<const TO*>(o), Tp,
+                    static_cast<const T*>(z), ld, z_off, static_cast<const T*>(gw), eps, rows, ntok, Hv,
+                    static_cast<T*>(y), q, s);
+}
+
+int gdn_gate_quant(const void* o, int o_dtype, int Tp, const void* z, int dt, int64_t ld, int z_off, const void* gw,
+                   float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s, cudaStream_t st) {
   if (rows < 0 || T < 0 || Hv <= 0 || Tp < T || !(eps >= 0.0f)) return BASAL200_ERR_ARG;
   if (dt != BASAL200_BF16 && dt != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (o_dtype != BASAL200_F32 && o_dtype != dt) return BASAL200_ERR_DTYPE;
   if (rows == 0 || T == 0) return BASAL200_OK;
   if (!o || !z || !gw || !q || !s) return BASAL200_ERR_ARG;
   if (z_off < 0 || z_off + (int64_t)Hv * 128 > ld || (ld % 8) || (z_off % 8)) return BASAL200_ERR_SHAPE;
@@ -964,12 +973,13 @@ int gdn_gate_quant(const float* o, int Tp, const void* z, int dt, int64_t ld, in
   int dev, rc = current_device(&dev);
   if (rc) return rc;
   const unsigned grid = (unsigned)((warps + 7) / 8);
+  using bf16 = __nv_bfloat16;
+  const bool f32 = o_dtype == BASAL200_F32;
   if (dt == BASAL200_BF16)
-    return launch_pdl(hybrid::gdn_gate_quant_kernel<__nv_bfloat16>, grid, 256, 0, st, o, Tp,
-                      static_cast<const __nv_bfloat16*>(z), ld, z_off, static_cast<const __nv_bfloat16*>(gw), eps,
-                      rows, T, Hv, static_cast<__nv_bfloat16*>(y), q, s);
-  return launch_pdl(hybrid::gdn_gate_quant_kernel<__half>, grid, 256, 0, st, o, Tp, static_cast<const __half*>(z), ld,
-                    z_off, static_cast<const __half*>(gw), eps, rows, T, Hv, static_cast<__half*>(y), q, s);
+    return f32 ? gdn_gate_quant_launch<bf16, float>(grid, o, Tp, z, ld, z_off, gw, eps, rows, T, Hv, y, q, s, st)
+               : gdn_gate_quant_launch<bf16, bf16>(grid, o, Tp, z, ld, z_off, gw, eps, rows, T, Hv, y, q, s, st);
+  return f32 ? gdn_gate_quant_launch<__half, float>(grid, o, Tp, z, ld, z_off, gw, eps, rows, T, Hv, y, q, s, st)
+             : gdn_gate_quant_launch<__half, __half>(grid, o, Tp, z, ld, z_off, gw, eps, rows, T, Hv, y, q, s, st);
 }
 
 // The attention layer's input steps (q / k norms, rotary embedding, keys and values into their buffers) and its
@@ -1036,19 +1046,21 @@ int attn_gate_quant(const void* o, int dt, const void* qkv, int64_t ld, int rows
                     static_cast<const __half*>(qkv), ld, rows, T, H, q, s);
 }
 
-template <typename TV>
+template <typename TV, typename TO>
 int gdn_chunk_launch(int dev, int slot, const gdnchunk::Params& p, cudaStream_t st) {
   constexpr size_t smem = sizeof(gdnchunk::Smem);
-  int rc = set_smem(dev, slot, gdnchunk::gdn_chunk_kernel<TV>, smem);
+  int rc = set_smem(dev, slot, gdnchunk::gdn_chunk_kernel<TV, TO>, smem);
   if (rc) return rc;
-  return launch_pdl(gdnchunk::gdn_chunk_kernel<TV>, (unsigned)(p.rows * p.H), gdnchunk::NT, smem, st, p);
+  return launch_pdl(gdnchunk::gdn_chunk_kernel<TV, TO>, (unsigned)(p.rows * p.H), gdnchunk::NT, smem, st, p);
 }
 
 int gdn_chunk(const float* q, const float* k, const void* v, int v_dtype, const float* g, const float* beta,
-              const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk, int H, int T, cudaStream_t st) {
+              const float* s0, int s0_rows, void* o, int o_dtype, float* s_out, int rows, int Hk, int H, int T,
+              cudaStream_t st) {
   if (rows < 0 || Hk <= 0 || H <= 0 || T < 0) return BASAL200_ERR_ARG;
   if (H % Hk) return BASAL200_ERR_SHAPE;
   if (v_dtype != BASAL200_F32 && v_dtype != BASAL200_BF16 && v_dtype != BASAL200_F16) return BASAL200_ERR_DTYPE;
+  if (o_dtype != BASAL200_F32 && o_dtype != v_dtype) return BASAL200_ERR_DTYPE;  // fp32, or v's 16-bit type
   if (rows == 0) return BASAL200_OK;
   if (T > 0 && (!q || !k || !v || !g || !beta || !o)) return BASAL200_ERR_ARG;  // no tokens: nothing of them is read
   if (s0 && s0_rows != 1 && s0_rows != rows) return BASAL200_ERR_ARG;
@@ -1082,9 +1094,13 @@ int gdn_chunk(const float* q, const float* k, const void* v, int v_dtype, const 
   p.Hk = Hk;
   p.H = H;
   p.T = T;
-  if (v_dtype == BASAL200_F32) return gdn_chunk_launch<float>(dev, kSlotGdn, p, st);
-  if (v_dtype == BASAL200_BF16) return gdn_chunk_launch<__nv_bfloat16>(dev, kSlotGdnV, p, st);
-  return gdn_chunk_launch<__half>(dev, kSlotGdnV + 1, p, st);
+  const bool f32 = o_dtype == BASAL200_F32;
+  if (v_dtype == BASAL200_F32) return gdn_chunk_launch<float, float>(dev, kSlotGdn, p, st);
+  if (v_dtype == BASAL200_BF16)
+    return f32 ? gdn_chunk_launch<__nv_bfloat16, float>(dev, kSlotGdnV, p, st)
+               : gdn_chunk_launch<__nv_bfloat16, __nv_bfloat16>(dev, kSlotGdnVO, p, st);
+  return f32 ? gdn_chunk_launch<__half, float>(dev, kSlotGdnV + 1, p, st)
+             : gdn_chunk_launch<__half, __half>(dev, kSlotGdnVO + 1, p, st);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -1267,10 +1283,10 @@ int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail,
                   beta, g, as_stream(stream));
 }
 
-int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype, int64_t ld, int z_off,
+int basal200_gdn_gate_fp8_quant(const void* o, int o_dtype, int Tp, const void* z, int dtype, int64_t ld, int z_off,
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream) {
-  return gdn_gate_quant(o, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
+  return gdn_gate_quant(o, o_dtype, Tp, z, dtype, ld, z_off, gw, eps, rows, T, Hv, y, q, s, as_stream(stream));
 }
 
 int basal200_attn_prep(const void* qkv, int dtype, int64_t ld, int rows, int T, int H, int Hk, const void* q_norm,
@@ -1286,9 +1302,9 @@ int basal200_attn_gate_fp8_quant(const void* o, int dtype, const void* qkv, int6
 }
 
 int basal200_gdn_chunk_rule(const float* q, const float* k, const void* v, int v_dtype, const float* g,
-                            const float* beta, const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk,
-                            int H, int T, void* stream) {
-  return gdn_chunk(q, k, v, v_dtype, g, beta, s0, s0_rows, o, s_out, rows, Hk, H, T, as_stream(stream));
+                            const float* beta, const float* s0, int s0_rows, void* o, int o_dtype, float* s_out,
+                            int rows, int Hk, int H, int T, void* stream) {
+  return gdn_chunk(q, k, v, v_dtype, g, beta, s0, s0_rows, o, o_dtype, s_out, rows, Hk, H, T, as_stream(stream));
 }
 
 // The two kernels of basal200_fp8_block_linear, the quantiser writing into the library's own device array. Nothing

@@ -42,7 +42,7 @@ struct Params {
   const float* beta;   // [rows, H, T]
   const float* s0;     // [s0_rows, H, 128, 128] or null (zeros); s0_rows 1 (shared) or rows
   int s0_rows;
-  float* o;            // [rows, H, T, 128]
+  void* o;             // [rows, H, T, 128], fp32 or v's 16-bit type (then each value rounded once)
   float* s_out;        // [rows, H, 128, 128] or null
   int rows, Hk, H, T;
 };
@@ -203,7 +203,16 @@ __device__ __forceinline__ float4 load_v4(const TV* p) {
                      static_cast<float>(h[3]));
 }
 
-template <typename TV>
+__device__ __forceinline__ void store2(float* d, float a, float b) {
+  *reinterpret_cast<float2*>(d) = make_float2(a, b);
+}
+template <typename TO>
+__device__ __forceinline__ void store2(TO* d, float a, float b) {
+  TO h[2] = {static_cast<TO>(a), static_cast<TO>(b)};
+  *reinterpret_cast<uint32_t*>(d) = *reinterpret_cast<const uint32_t*>(h);
+}
+
+template <typename TV, typename TO>
 __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sh = *reinterpret_cast<Smem*>(smem_raw);
@@ -358,8 +367,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const Params p) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int c = n32 + 8 * j + 2 * t4;
-            *reinterpret_cast<float2*>(p.o + (base + t0 + i) * DV + c) =
-                make_float2(fmaf(eg, qs[j][2 * hh], pv[j][2 * hh]), fmaf(eg, qs[j][2 * hh + 1], pv[j][2 * hh + 1]));
+            store2(static_cast<TO*>(p.o) + (base + t0 + i) * DV + c, fmaf(eg, qs[j][2 * hh], pv[j][2 * hh]),
+                   fmaf(eg, qs[j][2 * hh + 1], pv[j][2 * hh + 1]));
           }
         }
       }

@@ -290,12 +290,20 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const PrepParams p) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Gated DeltaNet output + FP8 quantiser: a half-warp per (token, value head), 8 values a lane. o [rows, Hv, Tp, 128]
-// fp32 (the recurrence's output, Tp >= ntok tokens a row), z in proj (16-bit, row stride ld, column z_off + vh * 128), gw [128]:
+// (the recurrence's output, fp32 or already rounded to T; Tp >= ntok tokens a row), z in proj (16-bit, row stride ld,
+// column z_off + vh * 128), gw [128]:
 // u = RN16(o); n = RN16(RN(u * rsqrt(mean(u^2) + eps))); n = RN16(RN(gw * n)); out = RN16(RN(n * silu(z)));
 // codes / scale of the 128 values as act_quant_block_kernel's, into q [rows * T, Hv * 128] / s [rows * T, Hv].
 // ---------------------------------------------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(256) gdn_gate_quant_kernel(const float* __restrict__ o, int Tp,
+template <typename TO>
+__device__ __forceinline__ void load_o8(const TO* p, float (&v)[8]) {
+  uint4 w[sizeof(TO) / 2];
+  raw_load8(p, w);
+  unpack8(w, p, v);
+}
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(256) gdn_gate_quant_kernel(const TO* __restrict__ o, int Tp,
                                                              const T* __restrict__ z, int64_t ld, int z_off,
                                                              const T* __restrict__ gw, float eps, int rows, int ntok,
                                                              int Hv, T* __restrict__ y, uint8_t* __restrict__ q,
@@ -313,10 +321,7 @@ __global__ void __launch_bounds__(256) gdn_gate_quant_kernel(const float* __rest
     vh = (int)(item % Hv);
     tok = item / Hv;  // r * T + t
     const int t = (int)(tok % ntok), r = (int)(tok / ntok);
-    const float* src = o + (((int64_t)r * Hv + vh) * Tp + t) * 128 + l * 8;
-    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    load_o8(o + (((int64_t)r * Hv + vh) * Tp + t) * 128 + l * 8, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = round_to<T>(v[i]);
   } else {

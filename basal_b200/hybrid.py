@@ -201,7 +201,7 @@ class HybridClassifier:
         b_off, a_off = C + cfg.value_dim, C + cfg.value_dim + cfg.lin_v_heads
         q, k, v, beta, g = ops.gdn_prep(proj, tail0, L["conv"], L["A_log"], L["dt_bias"], b, T, cfg.lin_k_heads,
                                         cfg.lin_v_heads, b_off, a_off)
-        o, s = ops.gdn_chunk_rule(q, k, v, g, beta, s0)
+        o, s = ops.gdn_chunk_rule(q, k, v, g, beta, s0, True)  # o in the projection's type, as the norm rounds it
         qo, so = ops.gdn_gate_fp8_quant(o, proj, z_off, L["gnorm"], cfg.eps, b, T)
         out = L["out"]
         h = ops.fp8_block_gemm_residual(qo, so, out.weight, out.weight_scale, None, h2).view(b, T, D)

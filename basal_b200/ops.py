@@ -28,7 +28,8 @@
                                                  the Gated DeltaNet's convolution, norms and gates (gdn_graph.py:131-140)
   basal::gdn_gate_fp8_quant(o, proj, z_off, gw, eps, rows, T)
                                                  its gated output norm fused with the FP8 quantiser (gdn_graph.py:432-438)
-  basal::gdn_chunk_rule(q, k, v, g, beta, s0)   its gated delta rule over chunks of 64 tokens (gdn_graph.py:81-87)
+  basal::gdn_chunk_rule(q, k, v, g, beta, s0, o_16bit)
+                                                 its gated delta rule over chunks of 64 tokens (gdn_graph.py:81-87)
   basal::attn_prep(qkv, q_norm, k_norm, eps, cos, sin, rot, H, Hk, rows, T, k_buf, v_buf, kv_off)
                                                  the attention's q / k norms and rotary embedding (gdn_graph.py:452-460)
   basal::attn_gate_fp8_quant(o, qkv, rows, T, H) its output gate fused with the FP8 quantiser (gdn_graph.py:464-466)
@@ -564,18 +565,18 @@ def _(o, qkv, rows, T, H):
 @torch.library.custom_op("basal::gdn_gate_fp8_quant", mutates_args=())
 def gdn_gate_fp8_quant(o: Tensor, proj: Tensor, z_off: int, gw: Tensor, eps: float, rows: int,
                        T: int) -> tuple[Tensor, Tensor]:
-    """The recurrence's output o [rows, Hv, Tp, 128] fp32 (Tp >= T) through the gated RMSNorm with z from proj
-    [rows * T, ld] (columns z_off ..) -> the FP8 codes [rows * T, Hv * 128] and per-head scales [rows * T, Hv] of the
-    output projection's input."""
+    """The recurrence's output o [rows, Hv, Tp, 128] (Tp >= T; fp32, or proj's dtype) through the gated RMSNorm with
+    z from proj [rows * T, ld] (columns z_off ..) -> the FP8 codes [rows * T, Hv * 128] and per-head scales
+    [rows * T, Hv] of the output projection's input."""
     require_cuda(o, proj, gw)
-    o = _c(o)
+    o = _c(o if o.dtype == proj.dtype else o.float())
     if proj.stride(-1) != 1:
         proj = proj.contiguous()
     Hv, Tp = o.shape[1], o.shape[2]
     q = torch.empty((rows * T, Hv * 128), dtype=E4M3, device=o.device)
     s = torch.empty((rows * T, Hv), dtype=torch.float32, device=o.device)
-    call("basal200_gdn_gate_fp8_quant", o.device, ptr(o), Tp, ptr(proj), code(proj.dtype), proj.stride(0), z_off,
-         ptr(_c(gw.to(proj.dtype))), float(eps), rows, T, Hv, None, ptr(q), ptr(s))
+    call("basal200_gdn_gate_fp8_quant", o.device, ptr(o), code(o.dtype), Tp, ptr(proj), code(proj.dtype),
+         proj.stride(0), z_off, ptr(_c(gw.to(proj.dtype))), float(eps), rows, T, Hv, None, ptr(q), ptr(s))
     return q, s
 
 
@@ -586,26 +587,29 @@ def _(o, proj, z_off, gw, eps, rows, T):
 
 
 @torch.library.custom_op("basal::gdn_chunk_rule", mutates_args=())
-def gdn_chunk_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor,
-                   s0: Optional[Tensor]) -> tuple[Tensor, Tensor]:
+def gdn_chunk_rule(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, s0: Optional[Tensor],
+                   o_16bit: bool = False) -> tuple[Tensor, Tensor]:
     """The gated delta rule (fp32) over q, k [rows, Hk, T, 128] (value head h reads key head h / (H / Hk)), v [rows, H,
     T, 128] (fp32 or 16-bit), g, beta [rows, H, T] from the state s0 [1 or rows, H, 128, 128] (None: zeros) -> (o
-    [rows, H, T, 128] fp32, the final state [rows, H, 128, 128])."""
+    [rows, H, T, 128] fp32, or in v's 16-bit dtype when o_16bit (each value rounded once), the final state
+    [rows, H, 128, 128] fp32)."""
     require_cuda(q, k, v, g, beta, s0)
     q, k, g, beta = (_c(t.float()) for t in (q, k, g, beta))
     v = _c(v if v.dtype in (torch.bfloat16, torch.float16) else v.float())
     rows, Hk, T, _ = q.shape
     H = v.shape[1]
-    o = torch.empty(v.shape, dtype=torch.float32, device=q.device)
+    o_dtype = v.dtype if o_16bit and v.dtype != torch.float32 else torch.float32
+    o = torch.empty(v.shape, dtype=o_dtype, device=q.device)
     s = torch.empty((rows, H, 128, 128), dtype=torch.float32, device=q.device)
     if s0 is not None:
         s0 = _c(s0.float())
     call("basal200_gdn_chunk_rule", q.device, ptr(q), ptr(k), ptr(v), code(v.dtype), ptr(g), ptr(beta), ptr(s0),
-         0 if s0 is None else s0.shape[0], ptr(o), ptr(s), rows, Hk, H, T)
+         0 if s0 is None else s0.shape[0], ptr(o), code(o_dtype), ptr(s), rows, Hk, H, T)
     return o, s
 
 
 @gdn_chunk_rule.register_fake
-def _(q, k, v, g, beta, s0):
+def _(q, k, v, g, beta, s0, o_16bit=False):
     rows, H = v.shape[0], v.shape[1]
-    return q.new_empty(v.shape), q.new_empty((rows, H, 128, 128))
+    o_dtype = v.dtype if o_16bit and v.dtype != torch.float32 else torch.float32
+    return q.new_empty(v.shape, dtype=o_dtype), q.new_empty((rows, H, 128, 128), dtype=torch.float32)

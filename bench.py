@@ -462,12 +462,12 @@ def run_c5_case(b2, name, rows, T, D, dev, g):
                 b_off + cfg.lin_v_heads)
         q, k, v, beta, gg = b2.ops.gdn_prep(*args)
         s0 = torch.randn(1, cfg.lin_v_heads, 128, 128, device=dev, generator=g) * 0.05
-        o, _ = b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0)
+        o, _ = b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0, True)
         for _ in range(5):
             if name == "gdn_prep":
                 b2.ops.gdn_prep(*args)
             elif name == "gdn_chunk":
-                b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0)
+                b2.ops.gdn_chunk_rule(q, k, v, gg, beta, s0, True)
             else:
                 b2.ops.gdn_gate_fp8_quant(o, proj, cfg.conv_dim, torch.ones(128, device=dev).bfloat16(), cfg.eps,
                                           rows, T)

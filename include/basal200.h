@@ -195,11 +195,12 @@ int basal200_gdn_prep(const void* proj, int dtype, int64_t ld, const void* tail,
                       int Hv, float* q, float* k, void* v, float* beta, float* g, void* stream);
 
 /* The Gated DeltaNet's output steps (basal/gdn_graph.py:432-438, Qwen3_5RMSNormGated) fused with the FP8 quantiser of
- * the output projection's input: o [rows, Hv, Tp, 128] fp32 (the recurrence's output, Tp >= T), z in a [rows * T, ld]
+ * the output projection's input: o [rows, Hv, Tp, 128] (the recurrence's output, Tp >= T; o_dtype fp32 or `dtype`,
+ * the same bits when basal200_gdn_chunk_rule wrote it in `dtype` as when in fp32), z in a [rows * T, ld]
  * matrix of `dtype` from column z_off (Hv * 128 values a token), gw [128]: each head's values rounded to `dtype`,
  * RMS-normed (eps), times gw, times silu(z), rounded -> y [rows * T, Hv * 128] (may be NULL), and quantised with one
  * scale per head: q [rows * T, Hv * 128] e4m3, s [rows * T, Hv] fp32 (bit-exact to basal200_fp8_act_quant of y). */
-int basal200_gdn_gate_fp8_quant(const float* o, int Tp, const void* z, int dtype, int64_t ld, int z_off,
+int basal200_gdn_gate_fp8_quant(const void* o, int o_dtype, int Tp, const void* z, int dtype, int64_t ld, int z_off,
                                 const void* gw, float eps, int rows, int T, int Hv, void* y, uint8_t* q, float* s,
                                 void* stream);
 
@@ -227,11 +228,12 @@ int basal200_attn_gate_fp8_quant(const void* o, int dtype, const void* qkv, int6
  * state s0 [s0_rows, H, 128, 128] (s0_rows 1: shared by every row; NULL: zeros), over T tokens of q, k
  * [rows, Hk, T, 128] fp32 (value head h reads key head h / (H / Hk); l2-normed, q scaled, as basal200_gdn_prep leaves
  * them), v [rows, H, T, 128] (v_dtype fp32, bf16 or fp16), g, beta [rows, H, T] fp32:
- * S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T, o_t = S_t^T q_t -> o [rows, H, T, 128] fp32,
- * and the final state into s_out [rows, H, 128, 128] (may be NULL). Computed over chunks of 64 tokens. */
+ * S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T, o_t = S_t^T q_t -> o [rows, H, T, 128]
+ * (o_dtype fp32, or v_dtype when that is 16-bit: each fp32 value rounded to nearest once), and the final state into
+ * s_out [rows, H, 128, 128] fp32 (may be NULL). Computed over chunks of 64 tokens. */
 int basal200_gdn_chunk_rule(const float* q, const float* k, const void* v, int v_dtype, const float* g,
-                            const float* beta, const float* s0, int s0_rows, float* o, float* s_out, int rows, int Hk,
-                            int H, int T, void* stream);
+                            const float* beta, const float* s0, int s0_rows, void* o, int o_dtype, float* s_out,
+                            int rows, int Hk, int H, int T, void* stream);
 
 /* Size limit of basal200_fp8_block_linear_noalloc: at most this many activation values (M * K) a call. */
 #define BASAL200_NOALLOC_MAX_ELEMS (1 << 24)

@@ -123,8 +123,8 @@ def test_gdn_gate_quant_kernel(hy):
     y = torch.empty(rows * T, Hv * 128, dtype=BF, device="cuda")
     q = torch.empty(rows * T, Hv * 128, dtype=torch.uint8, device="cuda")
     s = torch.empty(rows * T, Hv, dtype=torch.float32, device="cuda")
-    _lib.call("basal200_gdn_gate_fp8_quant", o.device, o.data_ptr(), Tp, proj.data_ptr(), _lib.BF16, ld, z_off,
-              gw.data_ptr(), 1e-6, rows, T, Hv, y.data_ptr(), q.data_ptr(), s.data_ptr())
+    _lib.call("basal200_gdn_gate_fp8_quant", o.device, o.data_ptr(), _lib.F32, Tp, proj.data_ptr(), _lib.BF16, ld,
+              z_off, gw.data_ptr(), 1e-6, rows, T, Hv, y.data_ptr(), q.data_ptr(), s.data_ptr())
     u = o[:, :, :T].transpose(1, 2).to(BF).float()  # [rows, T, Hv, 128]
     n = (u * torch.rsqrt(u.pow(2).mean(-1, keepdim=True) + 1e-6)).to(BF)
     n = gw * n
@@ -135,6 +135,8 @@ def test_gdn_gate_quant_kernel(hy):
     assert torch.equal(q, qa.view(torch.uint8)) and torch.equal(s, sa)
     q2, s2 = ops.gdn_gate_fp8_quant(o, proj, z_off, gw, 1e-6, rows, T)
     assert torch.equal(q2.view(torch.uint8), q) and torch.equal(s2, s)
+    q3, s3 = ops.gdn_gate_fp8_quant(o.to(BF), proj, z_off, gw, 1e-6, rows, T)  # o already rounded: the same bits
+    assert torch.equal(q3.view(torch.uint8), q) and torch.equal(s3, s)
 
 
 @pytest.mark.parametrize("M", [16, 300])
@@ -380,6 +382,8 @@ def test_gdn_chunk_rule_key_heads_and_16bit_values(hy, vdt):
     qr, kr = q.repeat_interleave(2, 1), k.repeat_interleave(2, 1)
     o2, S2 = ops.gdn_chunk_rule(qr, kr, v.float(), gl, beta, s0)
     assert torch.equal(o, o2) and torch.equal(S, S2)
+    o3, S3 = ops.gdn_chunk_rule(q, k, v, gl, beta, s0, True)  # o written in v's type: fp32 o rounded once
+    assert o3.dtype == vdt and torch.equal(o3, o.to(vdt)) and torch.equal(S3, S)
     c = lambda t: t.cpu().numpy()  # noqa: E731
     for r in range(rows):
         oo, SS = ohy.delta_rule(c(qr[r]).transpose(1, 0, 2), c(kr[r]).transpose(1, 0, 2),
