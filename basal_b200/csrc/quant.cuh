@@ -1,9 +1,9 @@
 // Quantisers of the block formats and of NVFP4, bit-exact to the reference's CPU arithmetic (rkinas/basal 2.8.1):
-// every division gives the code of an IEEE round-to-nearest division (__fdiv_rn, or a reciprocal product checked
-// against the code's rounding boundaries: block_codes8, e2m1_cut_distance), every product that the reference rounds
-// on its own is __fmul_rn (no contraction into an FMA), casts to e4m3 round to nearest even with saturation at +-448
-// (cvt.rn.satfinite), e2m1 codes round to nearest even with saturation at 6 (cvt.rn.satfinite.e2m1x2), int8 rounds
-// half to even.
+// every division gives the code of an IEEE round-to-nearest division (__fdiv_rn, or reciprocal products that bound the
+// quotient or are checked against the code's rounding boundaries: block_codes8, e2m1_cut_distance), every product that
+// the reference rounds on its own is __fmul_rn (no contraction into an FMA), casts to e4m3 round to nearest even with
+// saturation at +-448 (cvt.rn.satfinite), e2m1 codes round to nearest even with saturation at 6
+// (cvt.rn.satfinite.e2m1x2), int8 rounds half to even.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -87,17 +87,22 @@ __device__ __forceinline__ uint8_t float_to_e4m3(float v) {
 
 // 8 values of one group -> 8 code bytes of v / sc (an IEEE division in the reference); INT8: round half to even, clamp
 // to +-127, cast; FP8: cast two at a time with cvt.rn.satfinite.e4m3x2, whose saturation at +-448 is the reference's
-// clamp (the quotient never exceeds 448 by more than rounding).
-// The quotients are first taken as y = v * RN(1 / sc), within 1.5 ulp of the correctly rounded quotient, so y gives
-// the same code unless some quotient lies within a few ulps of a rounding boundary of the code: an e4m3 midpoint
-// (low 20 mantissa bits near 0x80000) or the e4m3 subnormal range |y| < 2^-6 (FP8), a half-integer (INT8). Then
-// (about 1e-4 of random data) the lane redoes its 8 values with the exact division; every code equals the one of
-// the reference's x / s (checked against the oracle).
+// clamp (the quotient never exceeds 448 by more than rounding). Every code equals the one of the reference's x / s
+// (checked against the oracle); the quotients are first bounded, and the lane divides its 8 values exactly only when
+// the bounds leave the code open (about 1e-5 of random data):
+//   INT8: y = v * RN(1 / sc) is within 1.5 ulp of the correctly rounded quotient, so it gives the same code unless
+//   some y lies within a few ulps of a half-integer.
+//   FP8: lo = RZ(v * RD(1 / sc)) and hi = RU(|v| * RU(1 / sc)) bracket |v / sc| (|lo| <= |v / sc| <= hi), hence
+//   also its correctly rounded value; the e4m3 cast is monotone in magnitude, so equal codes of |lo| and hi are the
+//   code's magnitude, and lo carries the sign (a -0 included). RD / RU (1 / sc) come from r = RN(1 / sc) and the sign
+//   of 1 - r sc (one fma): r itself on one side, its neighbour float on the other.
+// ---------------------------------------------------------------------------------------------------------------
 template <bool INT8>
 __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
   const float rcp = __frcp_rn(sc);
   float y[8];
   bool near = false;
+  uint32_t w[2] = {0u, 0u};
   if (INT8) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -105,21 +110,28 @@ __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
       near |= fabsf(__fsub_rn(y[i], __fadd_rn(floorf(y[i]), 0.5f))) < 0x1p-14f;
     }
   } else {
-    uint32_t dmid = 0xFFFFFFFFu, dsub = 0xFFFFFFFFu;
+    const float e = __fmaf_rn(-rcp, sc, 1.0f);  // its sign is that of 1 / sc - rcp (NaN for sc = inf: rcp = 0 kept)
+    const uint32_t rb = __float_as_uint(rcp);
+    const float rlo = e < 0.0f ? __uint_as_float(rb - 1u) : rcp;
+    const float rhi = e > 0.0f ? __uint_as_float(rb + 1u) : rcp;
+    uint32_t diff = 0u;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      y[i] = __fmul_rn(v[i], rcp);
-      const uint32_t b = __float_as_uint(y[i]);
-      dmid = min(dmid, (b & 0xFFFFFu) - 0x7FFFCu);  // wraps above 8 unless within 4 ulp of a midpoint
-      dsub = min(dsub, (b & 0x7FFFFFFFu) - 1u);     // 0 < |y| < 2^-6 <=> below 0x3C800000 - 1
+    for (int i = 0; i < 8; i += 2) {
+      const uint32_t lo = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+          make_float2(__fmul_rz(v[i], rlo), __fmul_rz(v[i + 1], rlo)), __NV_SATFINITE, __NV_E4M3));
+      const uint32_t hi = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+          make_float2(__fmul_ru(fabsf(v[i]), rhi), __fmul_ru(fabsf(v[i + 1]), rhi)), __NV_SATFINITE, __NV_E4M3));
+      diff |= (lo & 0x7F7Fu) ^ hi;
+      w[i >> 2] |= lo << (8 * (i & 3));
     }
-    near = dmid <= 8u || dsub < 0x3C800000u - 1u;
+    if (diff == 0u) return make_uint2(w[0], w[1]);
+    near = true;
+    w[0] = w[1] = 0u;
   }
   if (near) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = __fdiv_rn(v[i], sc);
   }
-  uint32_t w[2] = {0u, 0u};
   if (INT8) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {

@@ -71,6 +71,34 @@ def test_act_quant_bit_exact(b2, fmt, M, K, dtype):
     assert np.array_equal(f32bits(s), so.view(np.uint32))
 
 
+def e4m3_boundary_rows(rows, seed):
+    """fp32 activations whose quotients x / s land on and within 3 fp32 ulps of every e4m3 rounding midpoint (normal
+    and subnormal, both signs), each 1 x 128 group led by its amax so that s = amax / 448 is known."""
+    rng = np.random.default_rng(seed)
+    mids = [2.0 ** e * (1 + (2 * m + 1) / 16) for e in range(-6, 9) for m in range(8)]
+    mids += [(2 * m + 1) * 2.0 ** -10 for m in range(8)]  # subnormal midpoints, and the one below 2^-6
+    mids = np.array([v for v in mids if v < 448], dtype=np.float32)
+    x = np.empty((rows, 1024), dtype=np.float32)
+    for g in range(rows * 8):
+        amax = np.float32(rng.uniform(0.5, 8.0) * 2.0 ** rng.integers(-6, 7))
+        s = np.float32(amax / np.float32(448))
+        t = rng.choice(mids, 127) * s
+        t = t.astype(np.float32).view(np.int32) + rng.integers(-3, 4, 127).astype(np.int32)
+        t = t.view(np.float32) * np.where(rng.random(127) < 0.5, -1, 1).astype(np.float32)
+        x.reshape(-1, 128)[g] = np.concatenate([[amax], np.clip(t, -amax, amax)])
+    return x
+
+
+def test_act_quant_fp8_code_boundaries(b2):
+    """Codes of quotients at and beside the e4m3 rounding midpoints: the quantiser's bounding products leave these open
+    and its exact division settles them; every code and scale equals the oracle's."""
+    x = e4m3_boundary_rows(64, seed=5)
+    q, s = b2.fp8block.act_quant(torch.from_numpy(x).cuda())
+    qo, so = obq.act_quant(x, "fp8")
+    assert np.array_equal(u8(q), qo.view(np.uint8))
+    assert np.array_equal(f32bits(s), so.view(np.uint32))
+
+
 def test_act_quant_empty_and_refusals(b2):
     q, s = b2.fp8block.act_quant(torch.empty(0, 256, device="cuda", dtype=torch.bfloat16))
     assert q.shape == (0, 256) and s.shape == (0, 2)

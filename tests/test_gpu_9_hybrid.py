@@ -48,7 +48,7 @@ def ulps_bf16(a, b):
 def test_rms_norm_quant_kernel(hy):
     from basal_b200 import _lib, ops
     g = torch.Generator(device="cuda").manual_seed(0)
-    for M, D in ((1, 128), (37, 2560), (300, 384), (4099, 2048)):
+    for M, D in ((1, 128), (37, 2560), (300, 384), (4099, 2048), (9, 2304), (7, 2688)):  # 2688: the two-pass form
         x = (torch.randn(M, D, device="cuda", generator=g) * 3).to(BF)
         x[0, :128] = 0  # a zero group among others
         w = (torch.randn(D, device="cuda", generator=g) * 0.1).to(BF)
