@@ -390,6 +390,12 @@ CASES = {
     "gdn_prep": ("c5", 32, 256, 2560),
     "gdn_chunk": ("c5", 32, 256, 2560),
     "gdn_gate": ("c5", 32, 256, 2560),
+    # the same steps at one full C5 micro-batch (128 requests x 256 tokens, M = 32768 rows: inputs larger than L2),
+    # and the quantiser of the MLP's down-projection input (D = 9728)
+    "rms_quant_mb": ("c5", 128, 256, 2560),
+    "gdn_prep_mb": ("c5", 128, 256, 2560),
+    "gdn_gate_mb": ("c5", 128, 256, 2560),
+    "act_quant_mb": ("c5", 128, 256, 9728),
 }
 
 
@@ -445,7 +451,12 @@ def run_c5_case(b2, name, rows, T, D, dev, g):
     from basal_b200 import hybrid
     cfg = hybrid.C5
     M = rows * T
-    if name == "rms_quant":
+    name = name.removesuffix("_mb")
+    if name == "act_quant":
+        x = torch.randn(M, D, device=dev, generator=g).bfloat16()
+        for _ in range(5):
+            b2.ops.fp8_act_quant(x)
+    elif name == "rms_quant":
         x = torch.randn(M, D, device=dev, generator=g).bfloat16()
         w = (torch.randn(D, device=dev, generator=g) * 0.02).bfloat16()
         for _ in range(5):
