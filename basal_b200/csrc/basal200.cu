@@ -151,19 +151,28 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
 // then take no SM it still needs), else after its work. `per_sm` = the quantiser's CTAs an SM holds at once.
 int early_trigger(int dev, int64_t grid, int per_sm) { return grid <= (int64_t)g_dev[dev].sms * per_sm ? 1 : 0; }
 
+// PAIRS > 0: act_quant_block_kernel with PAIRS group pairs a warp; PAIRS < 0: act_quant_wide_kernel with -PAIRS
+// steps of 4 groups a warp.
+template <bool INT8, int PAIRS, typename T>
+int act_quant_launch_t(const void* x, int64_t groups, uint8_t* q, float* s, int grid, cudaStream_t st, int early) {
+  if constexpr (PAIRS > 0)
+    return launch_pdl(act_quant_block_kernel<T, INT8, PAIRS>, grid, 256, 0, st, static_cast<const T*>(x), groups, q,
+                      s, early);
+  else
+    return launch_pdl(act_quant_wide_kernel<T, INT8, -PAIRS>, grid, 256, 0, st, static_cast<const T*>(x), groups, q,
+                      s, early);
+}
+
 template <bool INT8, int PAIRS>
 int act_quant_launch(const void* x, int xt, int64_t groups, uint8_t* q, float* s, int grid, cudaStream_t st,
                      int early) {
   switch (xt) {
     case BASAL200_BF16:
-      return launch_pdl(act_quant_block_kernel<__nv_bfloat16, INT8, PAIRS>, grid, 256, 0, st,
-                        static_cast<const __nv_bfloat16*>(x), groups, q, s, early);
+      return act_quant_launch_t<INT8, PAIRS, __nv_bfloat16>(x, groups, q, s, grid, st, early);
     case BASAL200_F16:
-      return launch_pdl(act_quant_block_kernel<__half, INT8, PAIRS>, grid, 256, 0, st, static_cast<const __half*>(x),
-                        groups, q, s, early);
+      return act_quant_launch_t<INT8, PAIRS, __half>(x, groups, q, s, grid, st, early);
     case BASAL200_F32:
-      return launch_pdl(act_quant_block_kernel<float, INT8, PAIRS>, grid, 256, 0, st, static_cast<const float*>(x),
-                        groups, q, s, early);
+      return act_quant_launch_t<INT8, PAIRS, float>(x, groups, q, s, grid, st, early);
     default:
       return BASAL200_ERR_DTYPE;
   }
@@ -180,10 +189,10 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   if (rc) return rc;
   const int64_t groups = M * (K / 128);
   uint8_t* qb = static_cast<uint8_t*>(q);
-  // 8 warps a CTA, 2 x PAIRS groups a warp; 4 pairs once every SM gets 16 such CTAs
+  // 8 warps a CTA; once every SM gets 16 CTAs of 8 groups a warp: the wide kernel (2 steps of 4 groups a warp)
   if (groups >= (int64_t)g_dev[dev].sms * 16 * 64) {
     const int grid = grid_for(dev, groups, 64);
-    return act_quant_launch<INT8, 4>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 3));
+    return act_quant_launch<INT8, -2>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 3));
   }
   const int grid = grid_for(dev, groups, 16);
   return act_quant_launch<INT8, 1>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 4));

@@ -152,8 +152,8 @@ __device__ __forceinline__ uint2 block_codes8(const float (&v)[8], float sc) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Activations, FP8 / INT8 block formats: one half-warp per 128-feature group (8 values a lane), amax by shuffles; a
-// warp loads PAIRS pairs of groups before it computes any (4 when there are enough groups to fill the GPU: 0.51 of
-// HBM against 0.47 with 1 at 8192 x 6144 bf16; 1 for a few rows, where fewer, longer warps cost latency).
+// warp loads PAIRS pairs of groups before it computes any (1 for a few rows, where fewer, longer warps cost latency;
+// enough groups to fill the GPU take act_quant_wide_kernel below).
 // basal/blockquant.py:118-123: s = max(amax, 1e-12) / qmax; q = cast(clamp(x / s)) (INT8: round first). The
 // activations are contiguous, so group g is the 128 values from element 128 g. (Measured on B200: this kernel is
 // bound by its per-value arithmetic, not by bytes in flight; staging chunks through shared memory did not speed it.)
@@ -203,6 +203,59 @@ __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restric
   }
   // else the next kernel (a GEMM whose CTAs each fill an SM while they wait for this grid) may launch once every
   // CTA here has done its work: triggered at the start, its CTAs took the SMs from this grid's later waves
+  if (!early) pdl_launch();
+}
+
+// The same quantiser for many groups: 8 lanes a group (16 values a lane, 32 contiguous bytes of bf16), 4 groups a warp
+// step, the loads of U steps issued before any arithmetic. Its per-group work (3 shuffles, the scale's division and
+// reciprocal) is shared by twice the values a lane; the codes are the same as act_quant_block_kernel's.
+template <typename T, bool INT8, int U>
+__global__ void __launch_bounds__(256) act_quant_wide_kernel(const T* __restrict__ x, int64_t groups,
+                                                             uint8_t* __restrict__ q, float* __restrict__ s,
+                                                             int early) {
+  if (early) pdl_launch();
+  pdl_wait();
+  constexpr float kQmax = INT8 ? 127.0f : 448.0f;
+  constexpr int W = sizeof(T) / 2;  // 16-byte words of 8 values
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3, l = lane & 7;  // the group within the warp step, the lane within the group
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t p = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * U; 4 * p < groups;
+       p += warps * U) {
+    uint4 w[U][2][W];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = 4 * (p + u) + sub;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (g < groups) {
+          raw_load8(x + g * 128 + l * 16 + h * 8, w[u][h]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < W; ++i) w[u][h][i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = 4 * (p + u) + sub;
+      float v[2][8];
+      unpack8(w[u][0], x, v[0]);
+      unpack8(w[u][1], x, v[1]);
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(v[0][i]), fabsf(v[1][i])));
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
+      const uint2 c0 = block_codes8<INT8>(v[0], sc);
+      const uint2 c1 = block_codes8<INT8>(v[1], sc);
+      if (g < groups) {
+        *reinterpret_cast<uint4*>(q + g * 128 + l * 16) = make_uint4(c0.x, c0.y, c1.x, c1.y);
+        if (l == 0) s[g] = sc;
+      }
+    }
+  }
   if (!early) pdl_launch();
 }
 

@@ -78,21 +78,21 @@ def e4m3_boundary_rows(rows, seed):
     mids = [2.0 ** e * (1 + (2 * m + 1) / 16) for e in range(-6, 9) for m in range(8)]
     mids += [(2 * m + 1) * 2.0 ** -10 for m in range(8)]  # subnormal midpoints, and the one below 2^-6
     mids = np.array([v for v in mids if v < 448], dtype=np.float32)
-    x = np.empty((rows, 1024), dtype=np.float32)
-    for g in range(rows * 8):
-        amax = np.float32(rng.uniform(0.5, 8.0) * 2.0 ** rng.integers(-6, 7))
-        s = np.float32(amax / np.float32(448))
-        t = rng.choice(mids, 127) * s
-        t = t.astype(np.float32).view(np.int32) + rng.integers(-3, 4, 127).astype(np.int32)
-        t = t.view(np.float32) * np.where(rng.random(127) < 0.5, -1, 1).astype(np.float32)
-        x.reshape(-1, 128)[g] = np.concatenate([[amax], np.clip(t, -amax, amax)])
-    return x
+    G = rows * 8
+    amax = (rng.uniform(0.5, 8.0, G) * 2.0 ** rng.integers(-6, 7, G)).astype(np.float32)
+    s = (amax / np.float32(448)).astype(np.float32)
+    t = (rng.choice(mids, (G, 127)) * s[:, None]).astype(np.float32)
+    t = (t.view(np.int32) + rng.integers(-3, 4, (G, 127)).astype(np.int32)).view(np.float32)
+    t = t * np.where(rng.random((G, 127)) < 0.5, -1, 1).astype(np.float32)
+    t = np.clip(t, -amax[:, None], amax[:, None])
+    return np.concatenate([amax[:, None], t], axis=1).reshape(rows, 1024)
 
 
-def test_act_quant_fp8_code_boundaries(b2):
+@pytest.mark.parametrize("rows", [64, 19000])  # 512 groups (the few-groups kernel), 152000 (the wide kernel)
+def test_act_quant_fp8_code_boundaries(b2, rows):
     """Codes of quotients at and beside the e4m3 rounding midpoints: the quantiser's bounding products leave these open
     and its exact division settles them; every code and scale equals the oracle's."""
-    x = e4m3_boundary_rows(64, seed=5)
+    x = e4m3_boundary_rows(rows, seed=5)
     q, s = b2.fp8block.act_quant(torch.from_numpy(x).cuda())
     qo, so = obq.act_quant(x, "fp8")
     assert np.array_equal(u8(q), qo.view(np.uint8))
