@@ -159,7 +159,7 @@ int act_quant_launch_t(const void* x, int64_t groups, uint8_t* q, float* s, int 
     return launch_pdl(act_quant_block_kernel<T, INT8, PAIRS>, grid, 256, 0, st, static_cast<const T*>(x), groups, q,
                       s, early);
   else
-    return launch_pdl(act_quant_wide_kernel<T, INT8, -PAIRS>, grid, 256, 0, st, static_cast<const T*>(x), groups, q,
+    return launch_pdl(act_quant_wide_kernel<T, INT8, -PAIRS, 4>, grid, 256, 0, st, static_cast<const T*>(x), groups, q,
                       s, early);
 }
 
@@ -189,10 +189,11 @@ int act_quant(const void* x, int xt, int64_t M, int64_t K, void* q, float* s, cu
   if (rc) return rc;
   const int64_t groups = M * (K / 128);
   uint8_t* qb = static_cast<uint8_t*>(q);
-  // 8 warps a CTA; once every SM gets 16 CTAs of 8 groups a warp: the wide kernel (2 steps of 4 groups a warp)
+  // 8 warps a CTA; once every SM gets 16 CTAs of 8 groups a warp: the wide kernel (4 lanes a group, 1 step of 8
+  // groups a warp)
   if (groups >= (int64_t)g_dev[dev].sms * 16 * 64) {
     const int grid = grid_for(dev, groups, 64);
-    return act_quant_launch<INT8, -2>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 3));
+    return act_quant_launch<INT8, -1>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 3));
   }
   const int grid = grid_for(dev, groups, 16);
   return act_quant_launch<INT8, 1>(x, xt, groups, qb, s, grid, st, early_trigger(dev, grid, 4));

@@ -206,10 +206,10 @@ __global__ void __launch_bounds__(256) act_quant_block_kernel(const T* __restric
   if (!early) pdl_launch();
 }
 
-// The same quantiser for many groups: 8 lanes a group (16 values a lane, 32 contiguous bytes of bf16), 4 groups a warp
-// step, the loads of U steps issued before any arithmetic. Its per-group work (3 shuffles, the scale's division and
-// reciprocal) is shared by twice the values a lane; the codes are the same as act_quant_block_kernel's.
-template <typename T, bool INT8, int U>
+// The same quantiser for many groups: LPG lanes a group (128 / LPG values a lane, contiguous), 32 / LPG groups a warp
+// step, the loads of U steps issued before any arithmetic. Its per-group work (the shuffles, the scale's division and
+// reciprocal) is shared by more values a lane; the codes are the same as act_quant_block_kernel's.
+template <typename T, bool INT8, int U, int LPG>
 __global__ void __launch_bounds__(256) act_quant_wide_kernel(const T* __restrict__ x, int64_t groups,
                                                              uint8_t* __restrict__ q, float* __restrict__ s,
                                                              int early) {
@@ -217,19 +217,22 @@ __global__ void __launch_bounds__(256) act_quant_wide_kernel(const T* __restrict
   pdl_wait();
   constexpr float kQmax = INT8 ? 127.0f : 448.0f;
   constexpr int W = sizeof(T) / 2;  // 16-byte words of 8 values
+  constexpr int NV = 128 / LPG;     // values a lane
+  constexpr int NC = NV / 8;        // 8-value chunks a lane
+  constexpr int GPS = 32 / LPG;     // groups a warp step
   const int lane = threadIdx.x & 31;
-  const int sub = lane >> 3, l = lane & 7;  // the group within the warp step, the lane within the group
+  const int sub = lane / LPG, l = lane % LPG;  // the group within the warp step, the lane within the group
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t p = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * U; 4 * p < groups;
+  for (int64_t p = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * U; GPS * p < groups;
        p += warps * U) {
-    uint4 w[U][2][W];
+    uint4 w[U][NC][W];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t g = 4 * (p + u) + sub;
+      const int64_t g = GPS * (p + u) + sub;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < NC; ++h) {
         if (g < groups) {
-          raw_load8(x + g * 128 + l * 16 + h * 8, w[u][h]);
+          raw_load8(x + g * 128 + l * NV + h * 8, w[u][h]);
         } else {
 #pragma unroll
           for (int i = 0; i < W; ++i) w[u][h][i] = make_uint4(0u, 0u, 0u, 0u);
@@ -238,22 +241,25 @@ __global__ void __launch_bounds__(256) act_quant_wide_kernel(const T* __restrict
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t g = 4 * (p + u) + sub;
-      float v[2][8];
-      unpack8(w[u][0], x, v[0]);
-      unpack8(w[u][1], x, v[1]);
+      const int64_t g = GPS * (p + u) + sub;
+      float v[NC][8];
+#pragma unroll
+      for (int h = 0; h < NC; ++h) unpack8(w[u][h], x, v[h]);
       float amax = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(v[0][i]), fabsf(v[1][i])));
+      for (int h = 0; h < NC; ++h)
 #pragma unroll
-      for (int o = 4; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[h][i]));
+#pragma unroll
+      for (int o = LPG / 2; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float sc = __fdiv_rn(fmaxf(amax, 1e-12f), kQmax);
-      const uint2 c0 = block_codes8<INT8>(v[0], sc);
-      const uint2 c1 = block_codes8<INT8>(v[1], sc);
-      if (g < groups) {
-        *reinterpret_cast<uint4*>(q + g * 128 + l * 16) = make_uint4(c0.x, c0.y, c1.x, c1.y);
-        if (l == 0) s[g] = sc;
+#pragma unroll
+      for (int h = 0; h < NC; h += 2) {
+        const uint2 c0 = block_codes8<INT8>(v[h], sc);
+        const uint2 c1 = block_codes8<INT8>(v[h + 1], sc);
+        if (g < groups) *reinterpret_cast<uint4*>(q + g * 128 + l * NV + h * 8) = make_uint4(c0.x, c0.y, c1.x, c1.y);
       }
+      if (g < groups && l == 0) s[g] = sc;
     }
   }
   if (!early) pdl_launch();
